@@ -1,0 +1,114 @@
+/*
+ * metallora_b200 -- C ABI of the B200 (sm_100a) LoRA-linear kernels.
+ *
+ * Drop-in boundary for the LoRA-linear hot path of Wilbatronic/MetalLora.  The
+ * reference exposes this path as Python functions over MLX arrays
+ * (python/metal_lora/ops.py, kernels.py, kernels/*.metal); every entry point
+ * below names the reference interface it replaces.
+ *
+ * Conventions
+ *   - All tensor arguments are DEVICE pointers of the current CUDA device,
+ *     row-major and contiguous unless a leading dimension says otherwise.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Every call only enqueues work on that stream; none synchronises.
+ *   - Return value: MLORA_OK (0) or a negative MLORA_ERR_* code; the detail is
+ *     in mlora_last_error_message() (thread-local).  Arguments are validated
+ *     before anything is launched.
+ *   - The library never allocates device memory during a call.  Calls that
+ *     need scratch take a caller-owned `workspace` whose size comes from the
+ *     matching *_workspace_bytes query.
+ *   - Kernels bound every internal wait.  A wait that runs out records a code
+ *     in a per-device status word (mlora_device_status) instead of hanging.
+ *   - Shapes: M tokens, K in_features, N out_features, r LoRA rank (1..256).
+ *     The tensor-core paths need K % 8 == 0, N % 8 == 0 and r % 8 == 0 (16-byte
+ *     TMA row alignment); the Python layer zero-pads the rank to a multiple of 8,
+ *     which leaves every result unchanged.
+ */
+#ifndef METALLORA_B200_H_
+#define METALLORA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MLORA_API __attribute__((visibility("default")))
+#else
+#define MLORA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MLORA_OK 0
+#define MLORA_ERR_INVALID_ARG -1   /* bad pointer, shape, stride or alignment */
+#define MLORA_ERR_UNSUPPORTED -2   /* valid request this build does not handle */
+#define MLORA_ERR_CUDA -3          /* CUDA runtime/driver error */
+#define MLORA_ERR_WORKSPACE -4     /* workspace too small or misaligned */
+#define MLORA_ERR_DEVICE -5        /* device is not sm_100 */
+
+/* ---- element types ----------------------------------------------------- */
+#define MLORA_DTYPE_BF16 0
+#define MLORA_DTYPE_F16 1
+#define MLORA_DTYPE_F32 2
+
+/* ---- library / device -------------------------------------------------- */
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+MLORA_API int mlora_version(void);
+
+/* Human-readable name of a status code. */
+MLORA_API const char* mlora_status_string(int status);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+MLORA_API const char* mlora_last_error_message(void);
+
+/* 1 if `device` is an sm_100 GPU these kernels run on, else 0.
+ * Replaces kernels.is_metal_available() (python/metal_lora/kernels.py:502). */
+MLORA_API int mlora_device_supported(int device);
+
+/* Reads (and with reset != 0 clears) the status word of the current device.
+ * *out = 0 when no kernel has recorded a bounded-wait timeout.  Synchronous. */
+MLORA_API int mlora_device_status(uint32_t* out, int reset);
+
+/* ---- fused LoRA linear ------------------------------------------------- */
+
+/* Bytes of workspace mlora_lora_forward needs. */
+MLORA_API size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r);
+
+/* y[M,N] = x[M,K].w0[N,K]^T + (alpha/r) (x.a[r,K]^T).b[N,r]^T
+ * Replaces ops.lora_forward (python/metal_lora/ops.py:32-103, pure-MLX path
+ * :91-94) and kernels.lora_forward_metal (kernels.py:507-566).  dtype is
+ * BF16 or F16 for x, w0, a, b and y (fp32 accumulation).
+ * saved_xa (optional, may be NULL): receives (alpha/r).(x.a^T)^T as [r_pad, ldm]
+ * of the same dtype, r_pad = the smallest power of two >= max(r, 16) and
+ * ldm = M rounded up to a multiple of 8 -- the input mlora_lora_backward takes
+ * to skip recomputing it (the Ax cache of kernels/lora_train.metal:66). */
+MLORA_API int mlora_lora_forward(const void* x, const void* w0, const void* a, const void* b, void* y,
+                       void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                       int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace mlora_lora_backward needs. */
+MLORA_API size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r);
+
+/* Gradients of y = x.w0^T + s (x.a^T).b^T, s = alpha/r:
+ *   dx = dy.w0 + s (dy.b).a                      (optional: w0/dx may be NULL)
+ *   da = s (dy.b)^T . x      -> fp32 [r, K]
+ *   db = s dy^T . (x.a^T)    -> fp32 [N, r]
+ * clipped elementwise to [-clip_value, clip_value] when clip_value > 0.
+ * Replaces ops.lora_backward (python/metal_lora/ops.py:117-155, which clips the
+ * summed gradients, default 1.0) and kernels.lora_backward_metal
+ * (kernels.py:569-612); dx is the autodiff gradient of ops.py:91-94.
+ * saved_xa: the [r_pad, ldm] output of mlora_lora_forward, or NULL to recompute. */
+MLORA_API int mlora_lora_backward(const void* dy, const void* x, const void* w0, const void* a,
+                        const void* b, const void* saved_xa, void* dx, float* da, float* db,
+                        int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                        float clip_value, int dtype, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* METALLORA_B200_H_ */

@@ -1,0 +1,93 @@
+"""ctypes binding of ``libmetallora_b200.so`` (the C ABI in include/metallora_b200.h).
+
+Loading is lazy; a missing library or an unsupported device raises
+``DeviceError`` -- there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from pathlib import Path
+
+from .exceptions import DeviceError, MetalLoRAError, ShapeError
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmetallora_b200.so"
+
+MLORA_OK = 0
+MLORA_ERR_INVALID_ARG = -1
+MLORA_ERR_UNSUPPORTED = -2
+MLORA_ERR_CUDA = -3
+MLORA_ERR_WORKSPACE = -4
+MLORA_ERR_DEVICE = -5
+
+DTYPE_BF16 = 0
+DTYPE_F16 = 1
+DTYPE_F32 = 2
+
+_lib = None
+_lock = threading.Lock()
+
+vp = C.c_void_p
+i64 = C.c_int64
+f32 = C.c_float
+i32 = C.c_int
+sz = C.c_size_t
+
+# name -> (restype, argtypes); kept in the order of include/metallora_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "mlora_version": (i32, []),
+    "mlora_status_string": (C.c_char_p, [i32]),
+    "mlora_last_error_message": (C.c_char_p, []),
+    "mlora_device_supported": (i32, [i32]),
+    "mlora_device_status": (i32, [C.POINTER(C.c_uint32), i32]),
+    "mlora_lora_forward_workspace_bytes": (sz, [i64, i64, i64, i64]),
+    "mlora_lora_forward": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, i32, vp, sz, vp]),
+    "mlora_lora_backward_workspace_bytes": (sz, [i64, i64, i64, i64]),
+    "mlora_lora_backward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, f32,
+                                  i32, vp, sz, vp]),
+}
+
+
+def load(path: str | os.PathLike | None = None):
+    """Loads (once) and returns the library handle with typed signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.is_file():
+            raise DeviceError(
+                f"{p} is missing: build it with `python -m metallora_b200.build` "
+                "(the CUDA extension is required; there is no CPU fallback)")
+        lib = C.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    return load().mlora_last_error_message().decode(errors="replace")
+
+
+def check(status: int, what: str) -> None:
+    """Maps a C-ABI status to the reference's exception family."""
+    if status == MLORA_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status in (MLORA_ERR_INVALID_ARG, MLORA_ERR_UNSUPPORTED, MLORA_ERR_WORKSPACE):
+        raise ShapeError(msg)
+    if status == MLORA_ERR_DEVICE:
+        raise DeviceError(msg)
+    raise MetalLoRAError(msg)
+
+
+def device_status(reset: bool = False) -> int:
+    out = C.c_uint32(0)
+    check(load().mlora_device_status(C.byref(out), 1 if reset else 0), "mlora_device_status")
+    return int(out.value)

@@ -1,0 +1,319 @@
+// Persistent tcgen05 GEMM with an appended rank-r block:
+//
+//     D[M, N] = X[M, K] . W^T  +  X2[M, R] . W2^T
+//
+// It serves both dense LoRA-linear GEMMs:
+//   forward  y  = x . W0^T + (s x A^T) . B^T        X = x,  W = W0 (K-major), X2 = s.x.A^T, W2 = B
+//   backward dx = dy . W0  + (s dy B) . A           X = dy, W = W0 (MN-major), X2 = s.dy.B, W2 = A
+// (reference math: python/metal_lora/ops.py:91-94 and its chain rule).  The rank-r
+// block is just R/16 more UMMA k-steps into the same TMEM accumulator, so D is
+// written exactly once.
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0     TMA producer (one elected lane): X tile [128 x 64] and W tile
+//              [256 x 64] per stage, 128-byte swizzle, mbarrier tx accounting.
+//   warp 1     TMEM allocator + UMMA issuer (one elected lane): M=128, N=256,
+//              K=16 per instruction, fp32 accumulators double-buffered in TMEM
+//              (2 x 256 of the 512 columns) so the epilogue of tile i overlaps
+//              the main loop of tile i+1.
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, convert, 16-byte
+//              global stores; each thread owns one output row.
+// Tiles are visited n-fastest so the CTAs resident at one time share W and X
+// tiles in L2.
+#include "internal.h"
+#include "ptx.cuh"
+#include "../../include/metallora_b200.h"
+
+namespace mlora {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kXTileBytes = kBM * kBK * 2;  // 16 KB
+constexpr uint32_t kWTileBytes = kBN * kBK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kXTileBytes + kWTileBytes;
+constexpr uint32_t kMNBoxBytes = 64 * kBK * 2;   // one MN-major TMA box (8 KB)
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr uint32_t kTmemCols = 512;
+constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+
+struct GemmParams {
+  int M, N;
+  int num_kb_main, num_kb_extra, R;
+  int tiles_n, num_tiles;
+  void* d;
+  long long ldd;
+  uint32_t* status;
+};
+
+template <bool kWMN, bool kBF16, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    lora_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_x2,
+                     const __grid_constant__ CUtensorMap tm_w2, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* acc_full = empty_bar + kStages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;         // [2]
+  uint64_t* drain_bar = acc_empty + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps * 32);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_w);
+    if (p.num_kb_extra > 0) {
+      prefetch_tmap(&tm_x2);
+      prefetch_tmap(&tm_w2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_kb = p.num_kb_main + p.num_kb_extra;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (elect_one()) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t armed_parity[kStages];
+      bool armed[kStages];
+      for (int s = 0; s < kStages; ++s) armed[s] = false, armed_parity[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * kBM;
+        const int n0 = (tile % p.tiles_n) * kBN;
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.status, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sx = smem + stage * kStageBytes;
+          uint8_t* sw = sx + kXTileBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          armed[stage] = true;
+          armed_parity[stage] = phase;
+          const bool extra = kb >= p.num_kb_main;
+          const CUtensorMap* mx = extra ? &tm_x2 : &tm_x;
+          const CUtensorMap* mw = extra ? &tm_w2 : &tm_w;
+          const int k0 = (extra ? kb - p.num_kb_main : kb) * kBK;
+          tma_load_2d(sx, mx, &full_bar[stage], k0, m0);
+          if constexpr (kWMN) {
+#pragma unroll
+            for (int i = 0; i < kBN / 64; ++i)
+              tma_load_2d(sw + i * kMNBoxBytes, mw, &full_bar[stage], n0 + i * 64, k0);
+          } else {
+            tma_load_2d(sw, mw, &full_bar[stage], k0, n0);
+          }
+          if (++stage == kStages) stage = 0, phase ^= 1u;
+        }
+      }
+      // Never leave a bulk copy in flight at exit.
+      for (int s = 0; s < kStages; ++s)
+        if (armed[s]) mbar_wait(&full_bar[s], armed_parity[s], p.status, kDevTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA --
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, false, kWMN, kBF16);
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+        const uint32_t buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
+        if (!mbar_wait(&acc_empty[buf], use ^ 1u, p.status, kDevTimeoutAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.status, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sx = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sw = sx + kXTileBytes;
+          int nk = 4;
+          if (kb >= p.num_kb_main) {
+            const int rem = p.R - (kb - p.num_kb_main) * kBK;
+            nk = rem >= kBK ? 4 : rem / 16;
+          }
+          for (int k = 0; k < nk; ++k) {
+            const uint64_t ad = desc_kmajor_sw128(sx, k);
+            uint64_t bd;
+            if constexpr (kWMN)
+              bd = desc_mnmajor_sw128(sw, k, kMNBoxBytes);
+            else
+              bd = desc_kmajor_sw128(sw, k);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == kStages) stage = 0, phase ^= 1u;
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+      // Drain: every UMMA issued above has completed before TMEM is released.
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0, p.status, kDevTimeoutDrain);
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue --
+    const uint32_t quarter = warp & 3u;  // TMEM lanes [32*quarter, 32*quarter+32)
+    const uint32_t row = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const uint32_t buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
+      if (!mbar_wait(&acc_full[buf], use, p.status, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const int m = (tile / p.tiles_n) * kBM + static_cast<int>(row);
+      const int n_base = (tile % p.tiles_n) * kBN;
+      OutT* out_row = reinterpret_cast<OutT*>(p.d) + static_cast<long long>(m) * p.ldd + n_base;
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (m < p.M) {
+          const int n0 = n_base + c * 32;
+          if constexpr (sizeof(OutT) == 2) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack2<OutT>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (n0 + v * 8 < p.N)
+                *reinterpret_cast<uint4*>(out_row + c * 32 + v * 8) =
+                    make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (n0 + v * 4 < p.N)
+                *reinterpret_cast<uint4*>(out_row + c * 32 + v * 4) =
+                    make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <bool kWMN, bool kBF16, typename OutT>
+int launch_typed(const GemmArgs& a, cudaStream_t stream) {
+  CUtensorMap tx, tw, tx2, tw2;
+  if (!make_tmap_2d_16b(&tx, a.x, a.K, a.M, a.ldx, kBK, kBM)) return MLORA_ERR_INVALID_ARG;
+  if (kWMN) {
+    if (!make_tmap_2d_16b(&tw, a.w, a.N, a.K, a.ldw, 64, kBK)) return MLORA_ERR_INVALID_ARG;
+  } else {
+    if (!make_tmap_2d_16b(&tw, a.w, a.K, a.N, a.ldw, kBK, kBN)) return MLORA_ERR_INVALID_ARG;
+  }
+  if (a.R > 0) {
+    const int64_t r64 = (a.R + 63) / 64 * 64;
+    if (!make_tmap_2d_16b(&tx2, a.x2, r64, a.M, a.ldx2, kBK, kBM)) return MLORA_ERR_INVALID_ARG;
+    if (kWMN) {
+      if (!make_tmap_2d_16b(&tw2, a.w2, a.N, a.w2_rows, a.ldw2, 64, kBK))
+        return MLORA_ERR_INVALID_ARG;
+    } else {
+      if (!make_tmap_2d_16b(&tw2, a.w2, a.w2_rows, a.N, a.ldw2, kBK, kBN))
+        return MLORA_ERR_INVALID_ARG;
+    }
+  } else {
+    tx2 = tx;
+    tw2 = tw;
+  }
+  GemmParams p;
+  p.M = static_cast<int>(a.M);
+  p.N = static_cast<int>(a.N);
+  p.num_kb_main = static_cast<int>((a.K + kBK - 1) / kBK);
+  p.R = static_cast<int>(a.R);
+  p.num_kb_extra = static_cast<int>((a.R + kBK - 1) / kBK);
+  const int tiles_m = static_cast<int>((a.M + kBM - 1) / kBM);
+  p.tiles_n = static_cast<int>((a.N + kBN - 1) / kBN);
+  p.num_tiles = tiles_m * p.tiles_n;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.status = device_status_ptr();
+
+  auto kern = lora_gemm_kernel<kWMN, kBF16, OutT>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) {
+      set_error(std::string("cudaFuncSetAttribute(gemm): ") + cudaGetErrorString(e));
+      return MLORA_ERR_CUDA;
+    }
+    attr_set[dev] = true;
+  }
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(tx, tw, tx2, tw2, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("gemm launch: ") + cudaGetErrorString(e));
+    return MLORA_ERR_CUDA;
+  }
+  return MLORA_OK;
+}
+
+}  // namespace
+
+int launch_gemm(const GemmArgs& a, cudaStream_t stream) {
+  const bool bf16 = a.elt == Elt::kBF16;
+  if (a.out_dtype == MLORA_DTYPE_F32) {
+    if (a.w_mn_major)
+      return bf16 ? launch_typed<true, true, float>(a, stream)
+                  : launch_typed<true, false, float>(a, stream);
+    return bf16 ? launch_typed<false, true, float>(a, stream)
+                : launch_typed<false, false, float>(a, stream);
+  }
+  if (bf16) {
+    return a.w_mn_major ? launch_typed<true, true, __nv_bfloat16>(a, stream)
+                        : launch_typed<false, true, __nv_bfloat16>(a, stream);
+  }
+  return a.w_mn_major ? launch_typed<true, false, __half>(a, stream)
+                      : launch_typed<false, false, __half>(a, stream);
+}
+
+}  // namespace mlora

@@ -1,0 +1,160 @@
+"""Kernel-level API over the C ABI, taking and returning ``torch.Tensor``.
+
+Mirrors the reference's kernel module (python/metal_lora/kernels.py): the same
+entry-point names (``is_metal_available``, ``lora_forward_metal``,
+``lora_backward_metal``, ``lora_adamw_step_metal``,
+``persistent_gpu_state_init/step``), backed by sm_100a CUDA kernels instead of
+Metal shaders.  Every call enqueues on the current torch CUDA stream and never
+synchronises; workspaces come from torch's caching allocator.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .exceptions import DeviceError, ShapeError
+
+_DT = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16, torch.float32: _lib.DTYPE_F32}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise DeviceError("metallora_b200 kernels take CUDA tensors (no CPU fallback)")
+
+
+def is_metal_available() -> bool:
+    """True when the CUDA extension loads and the current device is sm_100.
+
+    Same name and meaning as the reference's ``kernels.is_metal_available()``
+    (kernels.py:502): "can the custom kernels run here"."""
+    try:
+        lib = _lib.load()
+    except DeviceError:
+        return False
+    if not torch.cuda.is_available():
+        return False
+    return bool(lib.mlora_device_supported(torch.cuda.current_device()))
+
+
+def rank_tile(r: int) -> int:
+    """Padded rank the tensor-core kernels use (power of two >= 16)."""
+    R = 16
+    while R < r:
+        R *= 2
+    return R
+
+
+def _pad_rank(a: torch.Tensor, b: torch.Tensor, alpha: float):
+    """Zero-pads A [r, K] / B [N, r] to a multiple-of-8 rank (16-byte rows) and
+    rescales alpha so that alpha'/r' == alpha/r.  Zero rows/columns add nothing."""
+    r = a.shape[0]
+    r8 = (r + 7) // 8 * 8
+    if r8 == r:
+        return a, b, alpha, r
+    a_p = torch.zeros((r8, a.shape[1]), dtype=a.dtype, device=a.device)
+    a_p[:r] = a
+    b_p = torch.zeros((b.shape[0], r8), dtype=b.dtype, device=b.device)
+    b_p[:, :r] = b
+    return a_p, b_p, alpha * r8 / r, r8
+
+
+def _check_2d(name: str, t: torch.Tensor, shape: tuple, dtype: torch.dtype) -> None:
+    if tuple(t.shape) != tuple(shape):
+        raise ShapeError(f"{name} shape mismatch: expected {tuple(shape)}, got {tuple(t.shape)}")
+    if t.dtype != dtype:
+        raise ShapeError(f"{name} dtype mismatch: expected {dtype}, got {t.dtype}")
+
+
+def lora_linear_fwd(x2d: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                    alpha: float, save_xa: bool = False):
+    """y = x.W0^T + (alpha/r).(x.A^T).B^T for 2-D x [M, K].
+
+    Returns (y, saved_xa) where saved_xa is [R, ceil8(M)] (R = padded rank) or None."""
+    _need_cuda(x2d, w0, a, b)
+    dt = x2d.dtype
+    if dt not in (torch.bfloat16, torch.float16):
+        raise ShapeError(f"lora_linear_fwd takes bf16/fp16 activations, got {dt}")
+    M, K = x2d.shape
+    N = w0.shape[0]
+    a, b, alpha, r = _pad_rank(a, b, alpha)
+    _check_2d("W0", w0, (N, K), dt)
+    _check_2d("A", a, (r, K), dt)
+    _check_2d("B", b, (N, r), dt)
+    x2d, w0, a, b = (t.contiguous() for t in (x2d, w0, a, b))
+    lib = _lib.load()
+    y = torch.empty((M, N), dtype=dt, device=x2d.device)
+    saved = (torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=dt, device=x2d.device)
+             if save_xa else None)
+    nbytes = lib.mlora_lora_forward_workspace_bytes(M, K, N, r)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x2d.device)
+    st = lib.mlora_lora_forward(_ptr(x2d), _ptr(w0), _ptr(a), _ptr(b), _ptr(y), _ptr(saved), M, K,
+                                N, r, float(alpha), _DT[dt], _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_lora_forward")
+    return y, saved
+
+
+def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | None,
+                    a: torch.Tensor, b: torch.Tensor, alpha: float,
+                    saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
+                    need_dx: bool = True):
+    """(dx, dA, dB) of the LoRA linear for 2-D dy [M, N], x [M, K].
+
+    dA/dB are fp32; clip_value > 0 clips them elementwise (ops.py:155)."""
+    _need_cuda(dy2d, x2d, a, b)
+    dt = x2d.dtype
+    M, K = x2d.shape
+    N = dy2d.shape[1]
+    r_orig = a.shape[0]
+    a_p, b_p, alpha_p, r = _pad_rank(a, b, alpha)
+    if r != r_orig:
+        saved_xa = None  # computed for the unpadded problem layout; recompute
+    _check_2d("grad_output", dy2d, (M, N), dt)
+    _check_2d("A", a_p, (r, K), dt)
+    _check_2d("B", b_p, (N, r), dt)
+    if need_dx:
+        if w0 is None:
+            raise ShapeError("dx needs W0")
+        _check_2d("W0", w0, (N, K), dt)
+        w0 = w0.contiguous()
+    dy2d, x2d, a_p, b_p = (t.contiguous() for t in (dy2d, x2d, a_p, b_p))
+    lib = _lib.load()
+    dx = torch.empty((M, K), dtype=dt, device=x2d.device) if need_dx else None
+    da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
+    db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
+    nbytes = lib.mlora_lora_backward_workspace_bytes(M, K, N, r)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x2d.device)
+    st = lib.mlora_lora_backward(_ptr(dy2d), _ptr(x2d), _ptr(w0) if need_dx else None, _ptr(a_p),
+                                 _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da), _ptr(db), M, K, N,
+                                 r, float(alpha_p), float(clip_value), _DT[dt], _ptr(ws),
+                                 ws.numel(), _stream())
+    _lib.check(st, "mlora_lora_backward")
+    if r != r_orig:
+        da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
+    return dx, da, db
+
+
+def lora_forward_metal(x, w0, a, b, alpha: float = 16.0, batch_size=None, seq_len=None,
+                       use_simd=None):
+    """Fused LoRA forward (reference: kernels.py:507-566).  x is [B, S, K] or
+    [S, K]; batch_size/seq_len/use_simd are accepted for signature parity."""
+    shp = x.shape
+    y, _ = lora_linear_fwd(x.reshape(-1, shp[-1]), w0, a, b, alpha)
+    return y.reshape(*shp[:-1], w0.shape[0])
+
+
+def lora_backward_metal(grad_output, x, a, b, alpha: float = 16.0, clip_value: float = 1.0):
+    """(grad_A, grad_B) of the LoRA branch, clipped to +-clip_value (reference:
+    kernels.py:569-612 / ops.py:143-155), returned in A's/B's dtype."""
+    g = grad_output.reshape(-1, grad_output.shape[-1])
+    xx = x.reshape(-1, x.shape[-1])
+    _, da, db = lora_linear_bwd(g, xx, None, a, b, alpha, None, clip_value, need_dx=False)
+    return da.to(a.dtype), db.to(b.dtype)

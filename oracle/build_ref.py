@@ -1,0 +1,93 @@
+"""Build recipe for ``oracle/_ref/libmlref.so`` -- test infrastructure only.
+
+Compiles the reference's own Metal compute shaders as host C++ (through the
+shim headers in ``oracle/msl_shim``) so the numpy oracle can be checked against
+the reference itself.  Inputs are read where they lie in the reference tree:
+
+* ``kernels/lora_quantized.metal`` and ``kernels/lora_train.metal``, included
+  directly by ``oracle/ref_driver.cpp``;
+* the inline MSL kernel bodies of ``python/metal_lora/kernels.py``
+  (``LORA_FORWARD_FUSED_SOURCE`` :41, ``LORA_BACKWARD_SOURCE`` :249,
+  ``LORA_ADAMW_SOURCE`` :314, ``LORA_MAINTENANCE_SOURCE`` :351), pulled out with
+  ``ast`` (the module imports MLX, which is not installed, so it is parsed, not
+  imported) and written to ``oracle/_ref/gen/*.inc``.
+
+Everything this writes goes to ``oracle/_ref/`` (git-ignored).  Nothing here
+runs the reference's build system.  Usage::
+
+    python oracle/build_ref.py [--reference /path/to/MetalLora]
+"""
+from __future__ import annotations
+
+import argparse
+import ast
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+OUT = HERE / "_ref"
+DEFAULT_REFERENCE = "/root/reference"
+
+# kernels.py string constant -> generated include name
+INLINE_BODIES = {
+    "LORA_FORWARD_FUSED_SOURCE": "lora_forward_fused.inc",
+    "LORA_BACKWARD_SOURCE": "lora_backward_fused.inc",
+    "LORA_ADAMW_SOURCE": "lora_adamw_step.inc",
+    "LORA_MAINTENANCE_SOURCE": "lora_maintenance.inc",
+}
+
+
+def extract_inline_bodies(kernels_py: Path) -> dict[str, str]:
+    tree = ast.parse(kernels_py.read_text())
+    found: dict[str, str] = {}
+    for node in tree.body:
+        if (
+            isinstance(node, ast.Assign)
+            and len(node.targets) == 1
+            and isinstance(node.targets[0], ast.Name)
+            and node.targets[0].id in INLINE_BODIES
+            and isinstance(node.value, ast.Constant)
+            and isinstance(node.value.value, str)
+        ):
+            found[node.targets[0].id] = node.value.value
+    missing = set(INLINE_BODIES) - set(found)
+    if missing:
+        raise RuntimeError(f"inline kernel sources not found in {kernels_py}: {sorted(missing)}")
+    return found
+
+
+def build(reference: str | os.PathLike | None = None, quiet: bool = False) -> Path | None:
+    """Build ``oracle/_ref/libmlref.so``; returns its path, or None when the
+    reference tree is absent (the prebuilt library is then used as is)."""
+    ref = Path(reference or os.environ.get("MLORA_REFERENCE_DIR", DEFAULT_REFERENCE))
+    kernels_py = ref / "python" / "metal_lora" / "kernels.py"
+    kernels_dir = ref / "kernels"
+    if not kernels_py.is_file() or not (kernels_dir / "lora_quantized.metal").is_file():
+        if not quiet:
+            print(f"[oracle/_ref] reference tree not found at {ref}; skipping", file=sys.stderr)
+        return None
+    gen = OUT / "gen"
+    gen.mkdir(parents=True, exist_ok=True)
+    for const, fname in INLINE_BODIES.items():
+        body = extract_inline_bodies(kernels_py)[const]
+        (gen / fname).write_text(body)
+    lib = OUT / "libmlref.so"
+    cmd = [
+        "g++", "-O2", "-std=c++17", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared",
+        "-Wno-attributes", "-Wno-unused-variable", "-Wno-unused-parameter",
+        "-I", str(HERE / "msl_shim"), "-I", str(kernels_dir), "-I", str(gen),
+        str(HERE / "ref_driver.cpp"), "-o", str(lib),
+    ]
+    subprocess.run(cmd, check=True)
+    if not quiet:
+        print(f"[oracle/_ref] built {lib}")
+    return lib
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=None)
+    args = ap.parse_args()
+    build(args.reference)
