@@ -1,0 +1,419 @@
+"""Benchmark of the LoRA-linear hot path (one JSON line on rank 0).
+
+Workload (default): the bf16 fused LoRA forward+backward at 4096 -> 4096,
+rank 16, alpha 32, 8192 tokens (batch 4 x seq 2048) per GPU -- one "step" is
+forward (y) plus backward (dx, dA, dB) of that batch through ``LoRALinear``,
+and for N > 1 GPUs the all-reduce of the LoRA gradients (weak scaling: every
+rank processes its own 8192 tokens).  Inputs are synthetic (seeded normal /
+uniform draws with the reference configuration's distributions); they total
+~290 MB per GPU, larger than the 126 MB L2, so no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference's CPU path instead: the numpy
+restatement of its pure-MLX op sequence (oracle/lora_oracle.py) on the host
+cores, on bounded token samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOAD = {
+    "workload": "lora_linear_fwd_bwd_bf16",
+    "in_features": 4096,
+    "out_features": 4096,
+    "rank": 16,
+    "alpha": 32.0,
+    "tokens_per_gpu": 8192,
+    "batch": 4,
+    "seq_len": 2048,
+}
+METRIC = "LoRA-linear fwd+bwd tokens/s (bf16, 4096->4096, r16)"
+
+
+def flops_per_token(K, N, r):
+    fwd = 2.0 * (K * N + K * r + r * N)
+    bwd = 2.0 * (N * K + 2 * N * r + 2 * r * K)
+    return fwd + bwd
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# --------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [f.strip() for f in line.split(",")]))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        inside = [s for t, s in self.samples if t0 - 0.15 <= t <= t1 + 0.15]
+        if not inside:  # timed region shorter than the sampling period: nearest samples
+            near = sorted(self.samples, key=lambda ts: min(abs(ts[0] - t0), abs(ts[0] - t1)))
+            inside = [s for _, s in near[:3]]
+        sm = [float(s[1]) for s in inside if s[1].replace(".", "").isdigit()]
+        smax = [float(s[2]) for s in inside if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in inside for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(inside)}
+
+
+# --------------------------------------------------------- CPU baseline ----
+
+def cpu_baseline(tokens: int, reps: int, seed: int = 0):
+    """Times the numpy restatement of the reference's CPU op path (forward,
+    dx, dA, dB in fp32 on bf16-rounded inputs) on `tokens` tokens."""
+    from oracle import lora_oracle as lo
+    K, N, r, alpha = (WORKLOAD[k] for k in ("in_features", "out_features", "rank", "alpha"))
+    rng = np.random.default_rng(seed)
+
+    def bf16(a):
+        a = np.asarray(a, np.float32)
+        b = a.view(np.uint32)
+        b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+        return b.astype(np.uint32).view(np.float32)
+
+    x = bf16(rng.standard_normal((tokens, K)))
+    W = bf16(rng.standard_normal((N, K)) / 64)
+    A = bf16(rng.uniform(-1 / 64, 1 / 64, (r, K)))
+    B = bf16(rng.standard_normal((N, r)) * np.sqrt(0.02))
+    dy = bf16(rng.standard_normal((tokens, N)))
+    times = []
+    for _ in range(reps + 1):
+        t = time.perf_counter()
+        lo.lora_forward(x, W, A, B, alpha)
+        lo.lora_grad_x(dy, W, A, B, alpha)
+        lo.lora_backward(dy, x, A, B, alpha, None)
+        times.append(time.perf_counter() - t)
+    med = statistics.median(times[1:])  # first run warms caches/threads
+    cores = len(os.sched_getaffinity(0))
+    try:
+        model = next((ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo")
+                      if ln.startswith("model name")), "unknown")
+    except OSError:
+        model = "unknown"
+    return {"value": tokens / med, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{tokens} tokens x {reps} reps of fwd+dx+dA+dB (numpy fp32 on bf16-rounded "
+                      f"inputs, OpenBLAS, {model})",
+            "seconds_per_rep": med}
+
+
+# ------------------------------------------------------------- our arm -----
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from metallora_b200 import _lib, kernels
+    from metallora_b200.layers import LoRALinear
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if not kernels.is_metal_available():
+        raise SystemExit("metallora_b200 CUDA extension unavailable on this device")
+    M = WORKLOAD["tokens_per_gpu"]
+    K, N, r, alpha = (WORKLOAD[k] for k in ("in_features", "out_features", "rank", "alpha"))
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    layer = LoRALinear(K, N, rank=r, alpha=alpha, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        layer.W0.copy_(torch.randn(N, K, device=dev, generator=g) / 64)
+        layer.A.copy_((torch.rand(r, K, device=dev, generator=g) * 2 - 1) / 64)
+        layer.B.copy_(torch.randn(N, r, device=dev, generator=g) * 0.02 ** 0.5)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+    flat_grads = None
+
+    def step(xin, dyin):
+        nonlocal flat_grads
+        layer.A.grad = None
+        layer.B.grad = None
+        xin.grad = None
+        y = layer(xin)
+        y.backward(dyin)
+        if world > 1:
+            flat = torch.cat([layer.A.grad.reshape(-1), layer.B.grad.reshape(-1)]).float()
+            dist.all_reduce(flat)
+            flat_grads = flat
+        return y
+
+    for _ in range(args.warmup):
+        step(x, dy)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    sampler.start()
+    time.sleep(0.3)
+    _lib.profile_read(reset=True)
+    _lib.profile_enable(True)
+    launches0 = _lib.launch_count()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(x, dy)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    launches = _lib.launch_count() - launches0
+    _lib.profile_enable(False)
+    prof = _lib.profile_read(reset=True)
+    sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * M * args.steps / (ms / 1e3)
+
+    # roofline: the dominant kernel is the tcgen05 GEMM (forward y and backward dx)
+    peaks = load_peaks()
+    gemm_ms, gemm_n = prof["gemm"]
+    gemm_flops = 2.0 * M * N * (K + r)  # per launch: X.W^T (+ rank block); fwd and dx alike
+    achieved = gemm_flops / (gemm_ms / gemm_n / 1e3) / 1e12 if gemm_n else None
+    peak = peaks["bf16_tflops_sustained"]
+    breakdown = {k: {"ms_per_launch": round(v[0] / v[1], 4), "launches": v[1]}
+                 for k, v in prof.items() if v[1]}
+
+    # end-to-end through the public API with host buffers (pinned), overlapped
+    e2e = run_e2e(args, layer, M, K, N, dev, world)
+
+    total_tflops = world * flops_per_token(K, N, r) * M * args.steps / (ms / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations/grads, N(0,1/4096) base, U(+-1/64) A, "
+                "N(0,0.02) B)",
+        "config": {**WORKLOAD, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)",
+                   "l2": "inputs > L2 (~290 MB resident per GPU), no flush"},
+        "tflops": round(total_tflops, 1),
+        "roofline": {"bound": "tensor", "kernel": "lora_gemm_kernel (tcgen05)",
+                     "achieved": round(achieved, 1) if achieved else None,
+                     "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4) if achieved else None,
+                     "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                     "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4) if achieved else None,
+                     "traffic": None, "per_launch_gflop": round(gemm_flops / 1e9, 2)},
+        "kernels": breakdown,
+        "gpu_launches": launches,
+        "clocks": sampler.summary(t_wall0, t_wall1),
+        "e2e": e2e,
+    }
+    if rank == 0:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_tokens, args.cpu_reps)
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, layer, M, K, N, dev, world):
+    """Same step through the public API with host-resident inputs and results:
+    per step, H2D of x and dy from pinned memory and D2H of y, dx, dA, dB, on a
+    copy stream overlapped with the previous step's compute."""
+    import torch
+    import torch.distributed as dist
+
+    steps = max(3, min(args.steps, 20))
+    g = torch.Generator().manual_seed(99)
+    xh = [torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory() for _ in range(2)]
+    dyh = [torch.randn(M, N, generator=g).to(torch.bfloat16).pin_memory() for _ in range(2)]
+    outs = {k: [torch.empty(s, dtype=dt).pin_memory() for _ in range(2)]
+            for k, s, dt in (("y", (M, N), torch.bfloat16), ("dx", (M, K), torch.bfloat16),
+                             ("dA", tuple(layer.A.shape), layer.A.dtype),
+                             ("dB", tuple(layer.B.shape), layer.B.dtype))}
+    xd = [torch.empty(M, K, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    dyd = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    copy = torch.cuda.Stream(device=dev)
+    h2d = 2 * M * K + 2 * M * N
+    d2h = 2 * M * N + 2 * M * K + layer.A.element_size() * (layer.A.numel() + layer.B.numel())
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def load(i):
+        b = i % 2
+        with torch.cuda.stream(copy):
+            xd[b].copy_(xh[b], non_blocking=True)
+            dyd[b].copy_(dyh[b], non_blocking=True)
+            loaded[b].record(copy)
+
+    torch.cuda.synchronize()
+    ev0.record(comp)
+    load(0)
+    for i in range(steps):
+        b = i % 2
+        if i + 1 < steps:
+            load(i + 1)
+        comp.wait_event(loaded[b])
+        xin = xd[b].requires_grad_(True)
+        layer.A.grad = None
+        layer.B.grad = None
+        y = layer(xin)
+        y.backward(dyd[b])
+        ga, gb = layer.A.grad, layer.B.grad
+        if world > 1:
+            flat = torch.cat([ga.reshape(-1), gb.reshape(-1)]).float()
+            dist.all_reduce(flat)
+        done[b].record(comp)
+        dx = xin.grad
+        with torch.cuda.stream(copy):
+            copy.wait_event(done[b])
+            for t in (y, dx, ga, gb):
+                t.record_stream(copy)
+            outs["y"][b].copy_(y.detach(), non_blocking=True)
+            outs["dx"][b].copy_(dx, non_blocking=True)
+            outs["dA"][b].copy_(ga, non_blocking=True)
+            outs["dB"][b].copy_(gb, non_blocking=True)
+        xin.grad = None
+        xd[b].requires_grad_(False)
+    comp.wait_stream(copy)
+    ev1.record(comp)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": round(world * M * steps / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "ms_per_step": round(ms / steps, 4),
+            "path": "LoRALinear forward+backward, pinned host buffers, copies overlapped"}
+
+
+# -------------------------------------------------------- reference arm ----
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    tokens = args.ref_tokens
+    for _ in range(args.warmup):
+        cpu_baseline(tokens, 1)
+    t = time.perf_counter()
+    res = None
+    for _ in range(args.steps):
+        res = cpu_baseline(tokens, 1)
+    elapsed = time.perf_counter() - t
+    value = tokens * args.steps / elapsed
+    K, N, r = WORKLOAD["in_features"], WORKLOAD["out_features"], WORKLOAD["rank"]
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * elapsed / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (same distributions as our arm)",
+        "config": {**WORKLOAD, "parallelism": "host CPU, rank 0 only",
+                   "sample_tokens_per_step": tokens},
+        "impl": "reference",
+        "tflops": round(flops_per_token(K, N, r) * value / 1e12, 4),
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": res["cores"],
+                         "kind": "port", "sample": res["sample"]},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "MLX (the reference's CPU backend) cannot be installed here; its pure-MLX op "
+                "sequence (ops.py:91-94,144-155) is timed as the numpy restatement",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--cpu-reps", type=int, default=3)
+    ap.add_argument("--ref-tokens", type=int, default=256)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

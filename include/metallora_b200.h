@@ -72,15 +72,35 @@ MLORA_API int mlora_device_supported(int device);
  * *out = 0 when no kernel has recorded a bounded-wait timeout.  Synchronous. */
 MLORA_API int mlora_device_status(uint32_t* out, int reset);
 
+/* ---- measurement ------------------------------------------------------- */
+
+/* Number of kernels this library has launched in this process (all devices). */
+MLORA_API long long mlora_launch_count(void);
+
+/* Enables (on != 0) or disables timing of every launch with a pair of CUDA
+ * events recorded on the launch stream.  Off by default; costs two event
+ * records per launch while on. */
+MLORA_API int mlora_profile_enable(int on);
+
+/* Sums the recorded launch times per kernel kind (0 GEMM, 1 rank projection,
+ * 2 weight gradient, 3 elementwise, 4 quantisation, 5 GEMV, 6 optimizer) into
+ * total_ms[0..nkinds) and counts into launches[0..nkinds); waits for the
+ * recorded events.  reset != 0 clears the records. */
+MLORA_API int mlora_profile_read(double* total_ms, long long* launches, int nkinds, int reset);
+
 /* ---- fused LoRA linear ------------------------------------------------- */
 
-/* Bytes of workspace mlora_lora_forward needs. */
-MLORA_API size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r);
+/* Bytes of workspace mlora_lora_forward needs for this shape and dtype. */
+MLORA_API size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                                    int dtype);
 
 /* y[M,N] = x[M,K].w0[N,K]^T + (alpha/r) (x.a[r,K]^T).b[N,r]^T
  * Replaces ops.lora_forward (python/metal_lora/ops.py:32-103, pure-MLX path
  * :91-94) and kernels.lora_forward_metal (kernels.py:507-566).  dtype is
- * BF16 or F16 for x, w0, a, b and y (fp32 accumulation).
+ * BF16 or F16 for x, w0, a, b and y (fp32 accumulation), or F32: every
+ * operand is split into bf16 hi/lo parts and the three significant partial
+ * products are accumulated in fp32 on the tensor cores (about 2^-16 relative
+ * error per product; saved_xa must then be NULL).
  * saved_xa (optional, may be NULL): receives (alpha/r).(x.a^T)^T as [r_pad, ldm]
  * of the same dtype, r_pad = the smallest power of two >= max(r, 16) and
  * ldm = M rounded up to a multiple of 8 -- the input mlora_lora_backward takes
@@ -89,8 +109,9 @@ MLORA_API int mlora_lora_forward(const void* x, const void* w0, const void* a, c
                        void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                        int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Bytes of workspace mlora_lora_backward needs. */
-MLORA_API size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r);
+/* Bytes of workspace mlora_lora_backward needs for this shape and dtype. */
+MLORA_API size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                                     int dtype);
 
 /* Gradients of y = x.w0^T + s (x.a^T).b^T, s = alpha/r:
  *   dx = dy.w0 + s (dy.b).a                      (optional: w0/dx may be NULL)
@@ -100,12 +121,37 @@ MLORA_API size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64
  * Replaces ops.lora_backward (python/metal_lora/ops.py:117-155, which clips the
  * summed gradients, default 1.0) and kernels.lora_backward_metal
  * (kernels.py:569-612); dx is the autodiff gradient of ops.py:91-94.
- * saved_xa: the [r_pad, ldm] output of mlora_lora_forward, or NULL to recompute. */
+ * saved_xa: the [r_pad, ldm] output of mlora_lora_forward, or NULL to recompute
+ * (always recomputed for F32).  dy, x, w0, a, b, dx share `dtype`. */
 MLORA_API int mlora_lora_backward(const void* dy, const void* x, const void* w0, const void* a,
                         const void* b, const void* saved_xa, void* dx, float* da, float* db,
                         int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                         float clip_value, int dtype, void* workspace, size_t workspace_bytes,
                         void* stream);
+
+/* ---- merged weights ------------------------------------------------------ */
+
+/* Bytes of workspace mlora_linear needs (0 except for F32). */
+MLORA_API size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype);
+
+/* y[M,N] = x[M,K] . w[N,K]^T -- the forward after the adapter is merged.
+ * Replaces ops.lora_forward_inference (python/metal_lora/ops.py:106-114) and the
+ * merged-mode call of LoRALinear (layers.py:112-117 then :92). */
+MLORA_API int mlora_linear(const void* x, const void* w, void* y, int64_t M, int64_t K, int64_t N,
+                           int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace mlora_merge needs (0 except for F32). */
+MLORA_API size_t mlora_merge_workspace_bytes(int64_t N, int64_t K, int64_t r, int dtype);
+
+/* w_out[N,K] = w0 + (alpha/r) . b[N,r] . a[r,K]; w_out may alias w0 (in place).
+ * K and r must be multiples of 8; N is free.
+ * Replaces ops.merge_lora_weights (python/metal_lora/ops.py:162-172), used by
+ * LoRALinear.merge_weights / to_inference_mode (layers.py:108-117).  Runs as a
+ * tensor-core GEMM over the rank with w0 added in the epilogue, so w0 is read
+ * once and w_out written once. */
+MLORA_API int mlora_merge(const void* w0, const void* a, const void* b, void* w_out, int64_t N,
+                          int64_t K, int64_t r, float alpha, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

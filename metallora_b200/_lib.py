@@ -41,11 +41,18 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_last_error_message": (C.c_char_p, []),
     "mlora_device_supported": (i32, [i32]),
     "mlora_device_status": (i32, [C.POINTER(C.c_uint32), i32]),
-    "mlora_lora_forward_workspace_bytes": (sz, [i64, i64, i64, i64]),
+    "mlora_launch_count": (C.c_longlong, []),
+    "mlora_profile_enable": (i32, [i32]),
+    "mlora_profile_read": (i32, [C.POINTER(C.c_double), C.POINTER(C.c_longlong), i32, i32]),
+    "mlora_lora_forward_workspace_bytes": (sz, [i64, i64, i64, i64, i32]),
     "mlora_lora_forward": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, i32, vp, sz, vp]),
-    "mlora_lora_backward_workspace_bytes": (sz, [i64, i64, i64, i64]),
+    "mlora_lora_backward_workspace_bytes": (sz, [i64, i64, i64, i64, i32]),
     "mlora_lora_backward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, f32,
                                   i32, vp, sz, vp]),
+    "mlora_linear_workspace_bytes": (sz, [i64, i64, i64, i32]),
+    "mlora_linear": (i32, [vp, vp, vp, i64, i64, i64, i32, vp, sz, vp]),
+    "mlora_merge_workspace_bytes": (sz, [i64, i64, i64, i32]),
+    "mlora_merge": (i32, [vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp]),
 }
 
 
@@ -85,6 +92,26 @@ def check(status: int, what: str) -> None:
     if status == MLORA_ERR_DEVICE:
         raise DeviceError(msg)
     raise MetalLoRAError(msg)
+
+
+KERNEL_KINDS = ("gemm", "rank", "wgrad", "elementwise", "quant", "gemv", "optim")
+
+
+def launch_count() -> int:
+    return int(load().mlora_launch_count())
+
+
+def profile_enable(on: bool) -> None:
+    check(load().mlora_profile_enable(1 if on else 0), "mlora_profile_enable")
+
+
+def profile_read(reset: bool = True) -> dict[str, tuple[float, int]]:
+    """{kind: (total_ms, launches)} of the launches timed since the last reset."""
+    n = len(KERNEL_KINDS)
+    ms = (C.c_double * n)()
+    cnt = (C.c_longlong * n)()
+    check(load().mlora_profile_read(ms, cnt, n, 1 if reset else 0), "mlora_profile_read")
+    return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(KERNEL_KINDS)}
 
 
 def device_status(reset: bool = False) -> int:

@@ -3,8 +3,11 @@
 // include/metallora_b200.h for the contract of each entry point.
 #include <cudaTypedefs.h>
 
+#include <atomic>
+#include <initializer_list>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "internal.h"
 #include "../../include/metallora_b200.h"
@@ -107,8 +110,8 @@ int check_device() {
 int check_shapes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype) {
   if (M <= 0 || K <= 0 || N <= 0) return fail(MLORA_ERR_INVALID_ARG, "M, K, N must be positive");
   if (r < 1 || r > 256) return fail(MLORA_ERR_INVALID_ARG, "rank must be in [1, 256]");
-  if (dtype != MLORA_DTYPE_BF16 && dtype != MLORA_DTYPE_F16)
-    return fail(MLORA_ERR_UNSUPPORTED, "dtype must be BF16 or F16");
+  if (dtype != MLORA_DTYPE_BF16 && dtype != MLORA_DTYPE_F16 && dtype != MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_UNSUPPORTED, "dtype must be BF16, F16 or F32");
   if (K % 8 || N % 8 || r % 8)
     return fail(MLORA_ERR_UNSUPPORTED, "K, N and r must be multiples of 8 (16-byte rows)");
   if (M > (int64_t(1) << 31) - 1 || K > (1 << 24) || N > (1 << 24))
@@ -178,7 +181,329 @@ BwdPlan plan_backward(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, bool
   return p;
 }
 
+// ---- fp32 (split-precision) plans -----------------------------------------
+// Every fp32 operand is copied once as bf16 hi/lo segments; a product of two
+// fp32 tensors becomes one bf16 GEMM over a 3x longer reduction whose segment
+// pairs are (hi,hi), (hi,lo), (lo,hi).
+struct F32FwdPlan {
+  int64_t R, R3_64;
+  int splits;
+  uint32_t* counters;
+  void* xs;     // [M, 3K]  (hi, hi, lo)
+  void* ws;     // [N, 3K]  (hi, lo, hi)
+  void* as;     // [r, 3K]  (hi, lo, hi)
+  void* bs;     // [N, 3R]  (hi, lo, hi)
+  void* t_rows; // [M, pad64(3R)] (hi, hi, lo) of s.x.A^T
+  float* partials;
+  size_t bytes;
+};
+
+F32FwdPlan plan_forward_f32(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, bool lora) {
+  F32FwdPlan p;
+  p.R = rank_tile(r);
+  p.R3_64 = pad64(3 * p.R);
+  p.splits = rank_splits(M, 3 * K);
+  Carve c(ws);
+  p.counters = static_cast<uint32_t*>(c.take(((M + 127) / 128) * 4));
+  p.xs = c.take(static_cast<size_t>(M) * 3 * K * 2);
+  p.ws = c.take(static_cast<size_t>(N) * 3 * K * 2);
+  p.as = lora ? c.take(static_cast<size_t>(r) * 3 * K * 2) : nullptr;
+  p.bs = lora ? c.take(static_cast<size_t>(N) * 3 * p.R * 2) : nullptr;
+  p.t_rows = lora ? c.take(static_cast<size_t>(M) * p.R3_64 * 2) : nullptr;
+  p.partials = (lora && p.splits > 1)
+                   ? static_cast<float*>(c.take(size_t(p.splits) * M * p.R * 4))
+                   : nullptr;
+  p.bytes = align_up(c.off, 256);
+  return p;
+}
+
+struct F32BwdPlan {
+  int64_t R, R3_64, ld3;
+  int rsplits, wsplits;
+  uint32_t* counters;  // [tm] U | [tm] T | [tn] dB | [tk] dA
+  size_t counter_bytes;
+  void* dys_cols;  // [M, 3N] HHL
+  void* xs_cols;   // [M, 3K] HHL
+  void* dy_rows;   // [3M, N] HHL
+  void* x_rows;    // [3M, K] HHL
+  void* w0_rows;   // [3N, K] HLH (dx only)
+  void* bts;       // [R, 3N] HLH
+  void* as_cols;   // [r, 3K] HLH
+  void* as_rows;   // [3R, K] HHL (dx only)
+  void* u_rows;    // [M, pad64(3R)] HLH (dx only)
+  void* u_t;       // [R, ld3] HLH
+  void* t_t;       // [R, ld3] HLH
+  float* rpartials;
+  float* wpart_db;
+  float* wpart_da;
+  size_t bytes;
+};
+
+F32BwdPlan plan_backward_f32(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, bool dx) {
+  F32BwdPlan p;
+  p.R = rank_tile(r);
+  p.R3_64 = pad64(3 * p.R);
+  p.ld3 = pad8(3 * M);
+  const int64_t big = 3 * (N > K ? N : K);
+  p.rsplits = rank_splits(M, big);
+  p.wsplits = wgrad_splits(3 * M, N > K ? N : K, 2);
+  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128, tk = (K + 127) / 128;
+  Carve c(ws);
+  p.counter_bytes = static_cast<size_t>(2 * tm + tn + tk) * 4;
+  p.counters = static_cast<uint32_t*>(c.take(p.counter_bytes));
+  p.dys_cols = c.take(static_cast<size_t>(M) * 3 * N * 2);
+  p.xs_cols = c.take(static_cast<size_t>(M) * 3 * K * 2);
+  p.dy_rows = c.take(static_cast<size_t>(3 * M) * N * 2);
+  p.x_rows = c.take(static_cast<size_t>(3 * M) * K * 2);
+  p.w0_rows = dx ? c.take(static_cast<size_t>(3 * N) * K * 2) : nullptr;
+  p.bts = c.take(static_cast<size_t>(p.R) * 3 * N * 2);
+  p.as_cols = c.take(static_cast<size_t>(r) * 3 * K * 2);
+  p.as_rows = dx ? c.take(static_cast<size_t>(3 * p.R) * K * 2) : nullptr;
+  p.u_rows = dx ? c.take(static_cast<size_t>(M) * p.R3_64 * 2) : nullptr;
+  p.u_t = c.take(static_cast<size_t>(p.R) * p.ld3 * 2);
+  p.t_t = c.take(static_cast<size_t>(p.R) * p.ld3 * 2);
+  p.rpartials = p.rsplits > 1 ? static_cast<float*>(c.take(size_t(p.rsplits) * M * p.R * 4)) : nullptr;
+  p.wpart_db = p.wsplits > 1 ? static_cast<float*>(c.take(size_t(p.wsplits) * N * p.R * 4)) : nullptr;
+  p.wpart_da = p.wsplits > 1 ? static_cast<float*>(c.take(size_t(p.wsplits) * K * p.R * 4)) : nullptr;
+  p.bytes = align_up(c.off, 256);
+  return p;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MLORA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int check_ptrs16(std::initializer_list<const void*> ptrs) {
+  for (const void* q : ptrs)
+    if (q && !aligned16(q)) return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  return MLORA_OK;
+}
+
+int lora_forward_f32(const float* x, const float* w0, const float* a, const float* b, float* y,
+                     int64_t M, int64_t K, int64_t N, int64_t r, float alpha, void* workspace,
+                     size_t workspace_bytes, cudaStream_t s) {
+  const bool lora = a != nullptr;
+  const F32FwdPlan need = plan_forward_f32(nullptr, M, K, N, r, lora);
+  if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
+    return fail(MLORA_ERR_WORKSPACE, "fp32 forward workspace needs " + std::to_string(need.bytes) + " bytes");
+  const F32FwdPlan p = plan_forward_f32(workspace, M, K, N, r, lora);
+  int rc;
+  if ((rc = launch_split3_cols(x, M, K, K, p.xs, K, 3 * K, kHHL, s))) return rc;
+  if ((rc = launch_split3_cols(w0, N, K, K, p.ws, K, 3 * K, kHLH, s))) return rc;
+  GemmArgs ga;
+  ga.x = p.xs;
+  ga.w = p.ws;
+  ga.d = y;
+  ga.M = M;
+  ga.N = N;
+  ga.K = 3 * K;
+  ga.ldx = 3 * K;
+  ga.ldw = 3 * K;
+  ga.ldd = N;
+  ga.w_mn_major = false;
+  ga.elt = Elt::kBF16;
+  ga.out_dtype = MLORA_DTYPE_F32;
+  if (lora) {
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "memset");
+    if ((rc = launch_split3_cols(a, r, K, K, p.as, K, 3 * K, kHLH, s))) return rc;
+    if ((rc = launch_split3_cols(b, N, r, r, p.bs, p.R, 3 * p.R, kHLH, s))) return rc;
+    RankArgs ra;
+    ra.x = p.xs;
+    ra.l = p.as;
+    ra.M = M;
+    ra.K = 3 * K;
+    ra.r = r;
+    ra.R = p.R;
+    ra.ldx = 3 * K;
+    ra.ldl = 3 * K;
+    ra.scale = alpha / static_cast<float>(r);
+    ra.out_rows = p.t_rows;
+    ra.ld_rows = p.R3_64;
+    ra.out_t = nullptr;
+    ra.ld_t = 0;
+    ra.split_out = true;
+    ra.split_pattern = kHHL;
+    ra.partials = p.partials;
+    ra.counters = p.counters;
+    ra.splits = p.splits;
+    ra.elt = Elt::kBF16;
+    if ((rc = launch_rank(ra, s))) return rc;
+    ga.x2 = p.t_rows;
+    ga.w2 = p.bs;
+    ga.R = 3 * p.R;
+    ga.w2_rows = 3 * p.R;
+    ga.ldx2 = p.R3_64;
+    ga.ldw2 = 3 * p.R;
+  }
+  return launch_gemm(ga, s);
+}
+
+int lora_backward_f32(const float* dy, const float* x, const float* w0, const float* a,
+                      const float* b, float* dx, float* da, float* db, int64_t M, int64_t K,
+                      int64_t N, int64_t r, float alpha, float clip, void* workspace,
+                      size_t workspace_bytes, cudaStream_t s) {
+  const bool want_dx = dx != nullptr;
+  const F32BwdPlan need = plan_backward_f32(nullptr, M, K, N, r, want_dx);
+  if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
+    return fail(MLORA_ERR_WORKSPACE, "fp32 backward workspace needs " + std::to_string(need.bytes) + " bytes");
+  const F32BwdPlan p = plan_backward_f32(workspace, M, K, N, r, want_dx);
+  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
+  const float scale = alpha / static_cast<float>(r);
+  int rc;
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  if ((rc = launch_split3_cols(dy, M, N, N, p.dys_cols, N, 3 * N, kHHL, s))) return rc;
+  if ((rc = launch_split3_cols(x, M, K, K, p.xs_cols, K, 3 * K, kHHL, s))) return rc;
+  if ((rc = launch_split3_rows(dy, M, N, N, p.dy_rows, M, kHHL, s))) return rc;
+  if ((rc = launch_split3_rows(x, M, K, K, p.x_rows, M, kHHL, s))) return rc;
+  if ((rc = launch_split3_cols_t(b, N, r, r, p.bts, p.R, N, 3 * N, kHLH, s))) return rc;
+  if ((rc = launch_split3_cols(a, r, K, K, p.as_cols, K, 3 * K, kHLH, s))) return rc;
+
+  // s.dy.B (hi, lo, hi): rows feed the dx GEMM, the transpose feeds dA.
+  RankArgs ru;
+  ru.x = p.dys_cols;
+  ru.l = p.bts;
+  ru.M = M;
+  ru.K = 3 * N;
+  ru.r = p.R;
+  ru.R = p.R;
+  ru.ldx = 3 * N;
+  ru.ldl = 3 * N;
+  ru.scale = scale;
+  ru.out_rows = want_dx ? p.u_rows : nullptr;
+  ru.ld_rows = p.R3_64;
+  ru.out_t = p.u_t;
+  ru.ld_t = p.ld3;
+  ru.split_out = true;
+  ru.split_pattern = kHLH;
+  ru.partials = p.rpartials;
+  ru.counters = p.counters;
+  ru.splits = rank_splits(M, 3 * N);
+  if (ru.splits > p.rsplits) ru.splits = p.rsplits;
+  ru.elt = Elt::kBF16;
+  if ((rc = launch_rank(ru, s))) return rc;
+  // s.x.A^T (hi, lo, hi) transposed: feeds dB.
+  RankArgs rt = ru;
+  rt.x = p.xs_cols;
+  rt.l = p.as_cols;
+  rt.K = 3 * K;
+  rt.r = r;
+  rt.ldx = 3 * K;
+  rt.ldl = 3 * K;
+  rt.out_rows = nullptr;
+  rt.out_t = p.t_t;
+  rt.counters = p.counters + tm;
+  rt.splits = rank_splits(M, 3 * K);
+  if (rt.splits > p.rsplits) rt.splits = p.rsplits;
+  if ((rc = launch_rank(rt, s))) return rc;
+
+  if (want_dx) {
+    if ((rc = launch_split3_rows(w0, N, K, K, p.w0_rows, N, kHLH, s))) return rc;
+    if ((rc = launch_split3_rows(a, r, K, K, p.as_rows, p.R, kHHL, s))) return rc;
+    GemmArgs ga;
+    ga.x = p.dys_cols;
+    ga.w = p.w0_rows;
+    ga.x2 = p.u_rows;
+    ga.w2 = p.as_rows;
+    ga.d = dx;
+    ga.M = M;
+    ga.N = K;
+    ga.K = 3 * N;
+    ga.R = 3 * p.R;
+    ga.w2_rows = 3 * p.R;
+    ga.ldx = 3 * N;
+    ga.ldw = K;
+    ga.ldx2 = p.R3_64;
+    ga.ldw2 = K;
+    ga.ldd = K;
+    ga.w_mn_major = true;
+    ga.elt = Elt::kBF16;
+    ga.out_dtype = MLORA_DTYPE_F32;
+    if ((rc = launch_gemm(ga, s))) return rc;
+  }
+
+  WgradArgs w[2];
+  w[0].big = p.dy_rows;
+  w[0].st = p.t_t;
+  w[0].ld_st = p.ld3;
+  w[0].M = 3 * M;
+  w[0].P = N;
+  w[0].r = r;
+  w[0].R = p.R;
+  w[0].ldb = N;
+  w[0].out = db;
+  w[0].ldo = r;
+  w[0].transposed = false;
+  w[0].clip = clip;
+  w[0].partials = p.wpart_db;
+  w[0].counters = p.counters + 2 * tm;
+  w[0].splits = p.wsplits;
+  w[0].elt = Elt::kBF16;
+  w[1] = w[0];
+  w[1].big = p.x_rows;
+  w[1].st = p.u_t;
+  w[1].P = K;
+  w[1].ldb = K;
+  w[1].out = da;
+  w[1].ldo = K;
+  w[1].transposed = true;
+  w[1].partials = p.wpart_da;
+  w[1].counters = p.counters + 2 * tm + tn;
+  return launch_wgrad(w, 2, s);
+}
+
+// ---- plain linear and merge plans ----------------------------------------
+size_t linear_ws(int64_t M, int64_t K, int64_t N, int dtype) {
+  if (dtype != MLORA_DTYPE_F32) return 0;
+  return plan_forward_f32(nullptr, M, K, N, 1, false).bytes;
+}
+
+size_t merge_ws(int64_t N, int64_t K, int64_t r, int dtype) {
+  if (dtype != MLORA_DTYPE_F32) return 0;
+  const int64_t r8 = pad8(r);
+  return align_up(static_cast<size_t>(N) * 3 * r8 * 2, 256) +
+         align_up(static_cast<size_t>(3 * r8) * K * 2, 256);
+}
+
+// ---- launch accounting / profiling ---------------------------------------
+std::atomic<long long> g_launches{0};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+struct ProfRec {
+  int kind;
+  cudaEvent_t start, stop;
+};
+std::vector<ProfRec> g_prof_recs;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pool_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
 }  // namespace
+
+LaunchScope::LaunchScope(int kind, cudaStream_t stream) : kind_(kind), stream_(stream) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  if (!g_prof_on) return;
+  cudaEvent_t start = pool_event();
+  stop_ = pool_event();
+  if (start == nullptr || stop_ == nullptr) return;
+  cudaEventRecord(start, stream_);
+  g_prof_recs.push_back({kind_, start, stop_});
+}
+
+LaunchScope::~LaunchScope() {
+  if (stop_ != nullptr) cudaEventRecord(stop_, stream_);
+}
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 
@@ -254,9 +579,9 @@ int mlora_device_status(uint32_t* out, int reset) {
   return MLORA_OK;
 }
 
-size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r) {
-  (void)N;
-  if (M <= 0 || K <= 0 || r <= 0) return 0;
+size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype) {
+  if (M <= 0 || K <= 0 || N <= 0 || r <= 0) return 0;
+  if (dtype == MLORA_DTYPE_F32) return plan_forward_f32(nullptr, M, K, N, r, true).bytes;
   return plan_forward(nullptr, M, K, r, true).bytes;
 }
 
@@ -270,6 +595,13 @@ int mlora_lora_forward(const void* x, const void* w0, const void* a, const void*
       (saved_xa && !aligned16(saved_xa)))
     return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
   if ((rc = check_device())) return rc;
+  if (dtype == MLORA_DTYPE_F32) {
+    if (saved_xa) return fail(MLORA_ERR_UNSUPPORTED, "saved_xa is not produced for F32");
+    return lora_forward_f32(static_cast<const float*>(x), static_cast<const float*>(w0),
+                            static_cast<const float*>(a), static_cast<const float*>(b),
+                            static_cast<float*>(y), M, K, N, r, alpha, workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
+  }
   const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
     return fail(MLORA_ERR_WORKSPACE, "forward workspace needs " + std::to_string(need.bytes) + " bytes");
@@ -322,8 +654,9 @@ int mlora_lora_forward(const void* x, const void* w0, const void* a, const void*
   return launch_gemm(ga, s);
 }
 
-size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r) {
+size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype) {
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0) return 0;
+  if (dtype == MLORA_DTYPE_F32) return plan_backward_f32(nullptr, M, K, N, r, true).bytes;
   return plan_backward(nullptr, M, K, N, r, true).bytes;
 }
 
@@ -341,6 +674,12 @@ int mlora_lora_backward(const void* dy, const void* x, const void* w0, const voi
   for (const void* q : ptrs)
     if (q && !aligned16(q)) return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
   if ((rc = check_device())) return rc;
+  if (dtype == MLORA_DTYPE_F32)
+    return lora_backward_f32(static_cast<const float*>(dy), static_cast<const float*>(x),
+                             static_cast<const float*>(w0), static_cast<const float*>(a),
+                             static_cast<const float*>(b), static_cast<float*>(dx), da, db, M, K,
+                             N, r, alpha, clip_value, workspace, workspace_bytes,
+                             static_cast<cudaStream_t>(stream));
   const BwdPlan need = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
     return fail(MLORA_ERR_WORKSPACE, "backward workspace needs " + std::to_string(need.bytes) + " bytes");
@@ -448,6 +787,124 @@ int mlora_lora_backward(const void* dy, const void* x, const void* w0, const voi
   w[1].partials = p.wpart_da;
   w[1].counters = p.counters + 2 * tm + tn;
   return launch_wgrad(w, 2, s);
+}
+
+long long mlora_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int mlora_profile_enable(int on) {
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  g_prof_on = on != 0;
+  return MLORA_OK;
+}
+
+int mlora_profile_read(double* total_ms, long long* launches, int nkinds, int reset) {
+  if (total_ms == nullptr || launches == nullptr || nkinds <= 0)
+    return fail(MLORA_ERR_INVALID_ARG, "NULL output");
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  for (int k = 0; k < nkinds; ++k) total_ms[k] = 0.0, launches[k] = 0;
+  for (const ProfRec& r : g_prof_recs) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, r.start, r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "profile event");
+    if (r.kind < nkinds) total_ms[r.kind] += ms, launches[r.kind] += 1;
+  }
+  if (reset) {
+    for (const ProfRec& r : g_prof_recs) {
+      g_event_pool.push_back(r.start);
+      g_event_pool.push_back(r.stop);
+    }
+    g_prof_recs.clear();
+  }
+  return MLORA_OK;
+}
+
+size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return linear_ws(M, K, N, dtype);
+}
+
+int mlora_linear(const void* x, const void* w, void* y, int64_t M, int64_t K, int64_t N, int dtype,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shapes(M, K, N, 8, dtype);
+  if (rc) return rc;
+  if (!x || !w || !y) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({x, w, y, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MLORA_DTYPE_F32)
+    return lora_forward_f32(static_cast<const float*>(x), static_cast<const float*>(w), nullptr,
+                            nullptr, static_cast<float*>(y), M, K, N, 1, 1.f, workspace,
+                            workspace_bytes, s);
+  GemmArgs ga;
+  ga.x = x;
+  ga.w = w;
+  ga.d = y;
+  ga.M = M;
+  ga.N = N;
+  ga.K = K;
+  ga.ldx = K;
+  ga.ldw = K;
+  ga.ldd = N;
+  ga.w_mn_major = false;
+  ga.elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
+  ga.out_dtype = dtype;
+  return launch_gemm(ga, s);
+}
+
+size_t mlora_merge_workspace_bytes(int64_t N, int64_t K, int64_t r, int dtype) {
+  if (N <= 0 || K <= 0 || r <= 0) return 0;
+  return merge_ws(N, K, r, dtype);
+}
+
+int mlora_merge(const void* w0, const void* a, const void* b, void* w_out, int64_t N, int64_t K,
+                int64_t r, float alpha, int dtype, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  // out_features (N) is the GEMM's row dimension here and may be ragged.
+  int rc = check_shapes(8, K, 8, r, dtype);
+  if (rc) return rc;
+  if (N <= 0 || N > (1 << 24)) return fail(MLORA_ERR_INVALID_ARG, "N must be in [1, 2^24]");
+  if (!w0 || !a || !b || !w_out) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({w0, a, b, w_out, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  GemmArgs ga;
+  ga.M = N;
+  ga.N = K;
+  ga.c = w0;
+  ga.ldc = K;
+  ga.d = w_out;
+  ga.ldd = K;
+  ga.acc_scale = alpha / static_cast<float>(r);
+  ga.w_mn_major = true;
+  ga.out_dtype = dtype;
+  if (dtype == MLORA_DTYPE_F32) {
+    const size_t need = merge_ws(N, K, r, dtype);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(MLORA_ERR_WORKSPACE, "fp32 merge workspace needs " + std::to_string(need) + " bytes");
+    const int64_t r8 = pad8(r);
+    Carve c(workspace);
+    void* bs = c.take(static_cast<size_t>(N) * 3 * r8 * 2);
+    void* as = c.take(static_cast<size_t>(3 * r8) * K * 2);
+    if ((rc = launch_split3_cols(static_cast<const float*>(b), N, r, r, bs, r8, 3 * r8, kHHL, s)))
+      return rc;
+    if ((rc = launch_split3_rows(static_cast<const float*>(a), r, K, K, as, r8, kHLH, s))) return rc;
+    ga.x = bs;
+    ga.w = as;
+    ga.K = 3 * r8;
+    ga.ldx = 3 * r8;
+    ga.ldw = K;
+    ga.elt = Elt::kBF16;
+    return launch_gemm(ga, s);
+  }
+  // W' = W0 + s.B.A: GEMM over the rank with W0 as the epilogue addend.
+  ga.x = b;
+  ga.w = a;
+  ga.K = r;
+  ga.ldx = r;
+  ga.ldw = K;
+  ga.elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
+  return launch_gemm(ga, s);
 }
 
 }  // extern "C"

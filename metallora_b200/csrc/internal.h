@@ -23,6 +23,34 @@ void set_error(const std::string& msg);
 bool make_tmap_2d_16b(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                       uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
 
+// ---- launch accounting / opt-in profiling ----------------------------------
+// Kernel kinds for mlora_profile_* (index into the per-kind totals).
+enum KernelKind : int {
+  kKindGemm = 0,
+  kKindRank = 1,
+  kKindWgrad = 2,
+  kKindElementwise = 3,
+  kKindQuant = 4,
+  kKindGemv = 5,
+  kKindOptim = 6,
+  kNumKinds = 7,
+};
+// Records one launch of `kind` on `stream`: bumps the launch counter and, while
+// profiling is enabled, brackets the launch with CUDA events.  Construct right
+// before the launch; the destructor records the stop event.
+class LaunchScope {
+ public:
+  LaunchScope(int kind, cudaStream_t stream);
+  ~LaunchScope();
+  LaunchScope(const LaunchScope&) = delete;
+  LaunchScope& operator=(const LaunchScope&) = delete;
+
+ private:
+  int kind_;
+  cudaStream_t stream_;
+  cudaEvent_t stop_ = nullptr;
+};
+
 // Device status word of the current device (kernels record bounded-wait
 // timeouts here).
 uint32_t* device_status_ptr();
@@ -34,13 +62,16 @@ int num_sms();
 struct GemmArgs {
   const void* x;   // [M, K], row stride ldx
   const void* w;   // K-major: [N, K] stride ldw ; MN-major: [K, N] stride ldw
-  const void* x2;  // [M, R64] stride ldx2 (nullptr when R == 0)
-  const void* w2;  // K-major: [N, r] stride ldw2 ; MN-major: [r, N] stride ldw2
+  const void* x2 = nullptr;  // [M, R64] stride ldx2 (nullptr when R == 0)
+  const void* w2 = nullptr;  // K-major: [N, r] stride ldw2 ; MN-major: [r, N] stride ldw2
   void* d;         // [M, N] stride ldd
+  const void* c = nullptr;  // optional addend [M, N] stride ldc, same type as d
+  int64_t ldc = 0;
+  float acc_scale = 1.f;    // D = acc_scale * (X.W^T + X2.W2^T) + C
   int64_t M, N, K;
-  int64_t R;       // extra reduction width, multiple of 16 (0 = none)
-  int64_t w2_rows; // K-major: r (columns of w2); MN-major: r (rows of w2)
-  int64_t ldx, ldw, ldx2, ldw2, ldd;
+  int64_t R = 0;   // extra reduction width, multiple of 16 (0 = none)
+  int64_t w2_rows = 0;  // K-major: r (columns of w2); MN-major: r (rows of w2)
+  int64_t ldx = 0, ldw = 0, ldx2 = 0, ldw2 = 0, ldd = 0;
   bool w_mn_major;
   Elt elt;
   int out_dtype;   // MLORA_DTYPE_*
@@ -61,6 +92,11 @@ struct RankArgs {
   int64_t ld_rows;
   void* out_t;     // bf16/f16 [R, ld_t] or nullptr (ld_t >= M, multiple of 8)
   int64_t ld_t;
+  // fp32 path: with split_out, out_rows row m = [part_0 | part_1 | part_2]
+  // (R columns each) and out_t[j, s*M + m] = part_s, where part_s is the bf16
+  // hi or lo part of the value as bit s of split_pattern says (0 = hi).
+  bool split_out = false;
+  uint32_t split_pattern = 0;
   float* partials; // [splits, M, R] fp32 workspace
   uint32_t* counters;  // [ceil(M/128)] zeroed
   int splits;
@@ -92,5 +128,17 @@ int launch_wgrad(const WgradArgs* probs, int nprobs, cudaStream_t stream);
 // ---------------------------------------------------------- elementwise ------
 int launch_transpose_pad(const void* b, int64_t N, int64_t r, int64_t ldb, void* bt, int64_t R,
                          Elt elt, cudaStream_t stream);
+
+// Split-precision (bf16 hi/lo) copies of fp32 tensors; pattern bit s = 1 puts
+// the lo part in segment s.  Patterns: kHHL = (hi, hi, lo), kHLH = (hi, lo, hi).
+constexpr uint32_t kHHL = 0b100u;
+constexpr uint32_t kHLH = 0b010u;
+int launch_split3_cols(const float* src, int64_t rows, int64_t cols, int64_t ld_src, void* dst,
+                       int64_t seg, int64_t ld_dst, uint32_t pattern, cudaStream_t stream);
+int launch_split3_rows(const float* src, int64_t rows, int64_t cols, int64_t ld_src, void* dst,
+                       int64_t seg_rows, uint32_t pattern, cudaStream_t stream);
+int launch_split3_cols_t(const float* src, int64_t N, int64_t r, int64_t ld_src, void* dst,
+                         int64_t R, int64_t seg, int64_t ld_dst, uint32_t pattern,
+                         cudaStream_t stream);
 
 }  // namespace mlora

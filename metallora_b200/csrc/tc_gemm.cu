@@ -46,6 +46,9 @@ struct GemmParams {
   int tiles_n, num_tiles;
   void* d;
   long long ldd;
+  const void* c;  // optional addend, same type/layout as d (ldc)
+  long long ldc;
+  float acc_scale;
   uint32_t* status;
 };
 
@@ -206,22 +209,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         if (m < p.M) {
           const int n0 = n_base + c * 32;
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.acc_scale;
+          if (p.c != nullptr) {
+            const OutT* crow = reinterpret_cast<const OutT*>(p.c) +
+                               static_cast<long long>(m) * p.ldc + n0;
+            if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (n0 + q * 8 < p.N) {
+                  const uint4 cv = *reinterpret_cast<const uint4*>(crow + q * 8);
+                  const OutT* ce = reinterpret_cast<const OutT*>(&cv);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) v[q * 8 + i] += static_cast<float>(ce[i]);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (n0 + q * 4 < p.N) {
+                  const float4 cv = *reinterpret_cast<const float4*>(crow + q * 4);
+                  v[q * 4] += cv.x;
+                  v[q * 4 + 1] += cv.y;
+                  v[q * 4 + 2] += cv.z;
+                  v[q * 4 + 3] += cv.w;
+                }
+              }
+            }
+          }
           if constexpr (sizeof(OutT) == 2) {
             uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pk[i] = pack2<OutT>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+            for (int i = 0; i < 16; ++i) pk[i] = pack2<OutT>(v[2 * i], v[2 * i + 1]);
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (n0 + v * 8 < p.N)
-                *reinterpret_cast<uint4*>(out_row + c * 32 + v * 8) =
-                    make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            for (int q = 0; q < 4; ++q)
+              if (n0 + q * 8 < p.N)
+                *reinterpret_cast<uint4*>(out_row + c * 32 + q * 8) =
+                    make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
           } else {
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-              if (n0 + v * 4 < p.N)
-                *reinterpret_cast<uint4*>(out_row + c * 32 + v * 4) =
-                    make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+            for (int q = 0; q < 8; ++q)
+              if (n0 + q * 4 < p.N)
+                *reinterpret_cast<float4*>(out_row + c * 32 + q * 4) =
+                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
           }
         }
       }
@@ -272,6 +303,9 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.num_tiles = tiles_m * p.tiles_n;
   p.d = a.d;
   p.ldd = a.ldd;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.acc_scale = a.acc_scale;
   p.status = device_status_ptr();
 
   auto kern = lora_gemm_kernel<kWMN, kBF16, OutT>;
@@ -288,6 +322,7 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
     attr_set[dev] = true;
   }
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  LaunchScope scope(kKindGemm, stream);
   kern<<<grid, kThreads, kSmemBytes, stream>>>(tx, tw, tx2, tw2, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

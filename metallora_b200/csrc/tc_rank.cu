@@ -196,6 +196,8 @@ struct RankParams {
   long long ld_rows;
   void* out_t;
   long long ld_t;
+  int split_out;
+  uint32_t split_pattern;
   float* partials;
   uint32_t* counters;
   uint32_t* status;
@@ -255,8 +257,41 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int i = 0; i < R; ++i) acc[i] = 0.f;
     }
-    if (split_reduce<R>(acc, p.partials, p.counters, tile, w.split, p.splits, row, p.M, flag) &&
-        row < p.M) {
+    const bool final_cta =
+        split_reduce<R>(acc, p.partials, p.counters, tile, w.split, p.splits, row, p.M, flag);
+    if (final_cta && row < p.M && p.split_out) {
+      // fp32 path: bf16 hi/lo parts of the scaled value (bf16 instantiation only)
+#pragma unroll
+      for (int i = 0; i < R; ++i) acc[i] *= p.scale;
+      if (p.out_rows != nullptr) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out_rows) + row * p.ld_rows;
+        for (int s = 0; s < 3; ++s) {
+          const bool lo = (p.split_pattern >> s) & 1u;
+#pragma unroll
+          for (int i = 0; i < R / 2; ++i) {
+            const float a0 = acc[2 * i], a1 = acc[2 * i + 1];
+            const float h0 = __bfloat162float(__float2bfloat16_rn(a0));
+            const float h1 = __bfloat162float(__float2bfloat16_rn(a1));
+            *reinterpret_cast<uint32_t*>(dst + s * R + 2 * i) =
+                lo ? pack2<__nv_bfloat16>(a0 - h0, a1 - h1) : pack2<__nv_bfloat16>(a0, a1);
+          }
+        }
+        for (long long j = 3 * R; j < p.ld_rows; j += 8)
+          *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
+      }
+      if (p.out_t != nullptr) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out_t);
+        for (int s = 0; s < 3; ++s) {
+          const bool lo = (p.split_pattern >> s) & 1u;
+#pragma unroll
+          for (int j = 0; j < R; ++j) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(acc[j]);
+            dst[static_cast<long long>(j) * p.ld_t + s * p.M + row] =
+                lo ? __float2bfloat16_rn(acc[j] - __bfloat162float(h)) : h;
+          }
+        }
+      }
+    } else if (final_cta && row < p.M) {
       if (p.out_rows != nullptr) {
         T* dst = reinterpret_cast<T*>(p.out_rows) + row * p.ld_rows;
 #pragma unroll
@@ -367,13 +402,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (split_reduce<R>(acc, q.partials, q.counters, tile, w.split, q.splits, prow, q.P, flag) &&
         prow < q.P) {
       const bool clip = q.clip > 0.f;
-      for (int j = 0; j < q.r; ++j) {
-        float v = acc[j];
-        if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
-        if (q.transposed)
-          q.out[static_cast<long long>(j) * q.ldo + prow] = v;
-        else
-          q.out[prow * q.ldo + j] = v;
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        if (j < q.r) {
+          float v = acc[j];
+          if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
+          if (q.transposed)
+            q.out[static_cast<long long>(j) * q.ldo + prow] = v;
+          else
+            q.out[prow * q.ldo + j] = v;
+        }
       }
     }
   }
@@ -411,12 +449,15 @@ int launch_rank_typed(const RankArgs& a, cudaStream_t stream) {
   p.ld_rows = a.ld_rows;
   p.out_t = a.out_t;
   p.ld_t = a.ld_t;
+  p.split_out = a.split_out ? 1 : 0;
+  p.split_pattern = a.split_pattern;
   p.partials = a.partials;
   p.counters = a.counters;
   p.status = device_status_ptr();
   auto kern = rank_proj_kernel<R, kBF16>;
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
   dim3 grid(static_cast<unsigned>((a.M + 127) / 128), static_cast<unsigned>(a.splits));
+  LaunchScope scope(kKindRank, stream);
   kern<<<grid, kThreads, smem_bytes(R), stream>>>(tx, tl, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -455,6 +496,7 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
   p.status = device_status_ptr();
   auto kern = wgrad_kernel<R, kBF16>;
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
+  LaunchScope scope(kKindWgrad, stream);
   kern<<<total, kThreads, smem_bytes(R), stream>>>(tb[0], ts[0], tb[1], ts[1], p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

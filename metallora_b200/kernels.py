@@ -6,6 +6,10 @@ entry-point names (``is_metal_available``, ``lora_forward_metal``,
 ``persistent_gpu_state_init/step``), backed by sm_100a CUDA kernels instead of
 Metal shaders.  Every call enqueues on the current torch CUDA stream and never
 synchronises; workspaces come from torch's caching allocator.
+
+Activations and weights are bf16 or fp16 (fp32 accumulation), or fp32, which
+runs as split-precision bf16 tensor-core GEMMs (three partial products per
+product of two fp32 values, ~2^-16 relative error each).
 """
 from __future__ import annotations
 
@@ -29,6 +33,17 @@ def _need_cuda(*ts: torch.Tensor) -> None:
     for t in ts:
         if t is not None and not t.is_cuda:
             raise DeviceError("metallora_b200 kernels take CUDA tensors (no CPU fallback)")
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise ShapeError(f"unsupported dtype {t.dtype}; use bfloat16, float16 or float32") from None
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
 def is_metal_available() -> bool:
@@ -78,11 +93,11 @@ def lora_linear_fwd(x2d: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: tor
                     alpha: float, save_xa: bool = False):
     """y = x.W0^T + (alpha/r).(x.A^T).B^T for 2-D x [M, K].
 
-    Returns (y, saved_xa) where saved_xa is [R, ceil8(M)] (R = padded rank) or None."""
+    Returns (y, saved_xa); saved_xa is the [R, ceil8(M)] rank intermediate the
+    backward can reuse (bf16/fp16 only), else None."""
     _need_cuda(x2d, w0, a, b)
     dt = x2d.dtype
-    if dt not in (torch.bfloat16, torch.float16):
-        raise ShapeError(f"lora_linear_fwd takes bf16/fp16 activations, got {dt}")
+    code = _dtype_code(x2d)
     M, K = x2d.shape
     N = w0.shape[0]
     a, b, alpha, r = _pad_rank(a, b, alpha)
@@ -92,12 +107,12 @@ def lora_linear_fwd(x2d: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: tor
     x2d, w0, a, b = (t.contiguous() for t in (x2d, w0, a, b))
     lib = _lib.load()
     y = torch.empty((M, N), dtype=dt, device=x2d.device)
-    saved = (torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=dt, device=x2d.device)
-             if save_xa else None)
-    nbytes = lib.mlora_lora_forward_workspace_bytes(M, K, N, r)
-    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x2d.device)
+    saved = None
+    if save_xa and dt != torch.float32:
+        saved = torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=dt, device=x2d.device)
+    ws = _workspace(lib.mlora_lora_forward_workspace_bytes(M, K, N, r, code), x2d.device)
     st = lib.mlora_lora_forward(_ptr(x2d), _ptr(w0), _ptr(a), _ptr(b), _ptr(y), _ptr(saved), M, K,
-                                N, r, float(alpha), _DT[dt], _ptr(ws), ws.numel(), _stream())
+                                N, r, float(alpha), code, _ptr(ws), ws.numel(), _stream())
     _lib.check(st, "mlora_lora_forward")
     return y, saved
 
@@ -108,15 +123,17 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
                     need_dx: bool = True):
     """(dx, dA, dB) of the LoRA linear for 2-D dy [M, N], x [M, K].
 
-    dA/dB are fp32; clip_value > 0 clips them elementwise (ops.py:155)."""
+    dA/dB are fp32 (master-gradient precision); clip_value > 0 clips them
+    elementwise after the full reduction (ops.py:155)."""
     _need_cuda(dy2d, x2d, a, b)
     dt = x2d.dtype
+    code = _dtype_code(x2d)
     M, K = x2d.shape
     N = dy2d.shape[1]
     r_orig = a.shape[0]
     a_p, b_p, alpha_p, r = _pad_rank(a, b, alpha)
-    if r != r_orig:
-        saved_xa = None  # computed for the unpadded problem layout; recompute
+    if dt == torch.float32:
+        saved_xa = None
     _check_2d("grad_output", dy2d, (M, N), dt)
     _check_2d("A", a_p, (r, K), dt)
     _check_2d("B", b_p, (N, r), dt)
@@ -130,16 +147,52 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
     dx = torch.empty((M, K), dtype=dt, device=x2d.device) if need_dx else None
     da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
     db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
-    nbytes = lib.mlora_lora_backward_workspace_bytes(M, K, N, r)
-    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x2d.device)
+    ws = _workspace(lib.mlora_lora_backward_workspace_bytes(M, K, N, r, code), x2d.device)
     st = lib.mlora_lora_backward(_ptr(dy2d), _ptr(x2d), _ptr(w0) if need_dx else None, _ptr(a_p),
                                  _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da), _ptr(db), M, K, N,
-                                 r, float(alpha_p), float(clip_value), _DT[dt], _ptr(ws),
+                                 r, float(alpha_p), float(clip_value), code, _ptr(ws),
                                  ws.numel(), _stream())
     _lib.check(st, "mlora_lora_backward")
     if r != r_orig:
         da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
     return dx, da, db
+
+
+def linear(x2d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """y = x.W^T (merged-weight forward, ops.py:106-114)."""
+    _need_cuda(x2d, w)
+    code = _dtype_code(x2d)
+    M, K = x2d.shape
+    N = w.shape[0]
+    _check_2d("W", w, (N, K), x2d.dtype)
+    x2d, w = x2d.contiguous(), w.contiguous()
+    lib = _lib.load()
+    y = torch.empty((M, N), dtype=x2d.dtype, device=x2d.device)
+    ws = _workspace(lib.mlora_linear_workspace_bytes(M, K, N, code), x2d.device)
+    st = lib.mlora_linear(_ptr(x2d), _ptr(w), _ptr(y), M, K, N, code, _ptr(ws), ws.numel(),
+                          _stream())
+    _lib.check(st, "mlora_linear")
+    return y
+
+
+def merge(w0: torch.Tensor, a: torch.Tensor, b: torch.Tensor, alpha: float,
+          out: torch.Tensor | None = None) -> torch.Tensor:
+    """W0 + (alpha/r).B.A (ops.py:162-172); ``out`` may be ``w0`` (in place)."""
+    _need_cuda(w0, a, b)
+    code = _dtype_code(w0)
+    N, K = w0.shape
+    a_p, b_p, alpha_p, r = _pad_rank(a, b, alpha)
+    _check_2d("A", a_p, (r, K), w0.dtype)
+    _check_2d("B", b_p, (N, r), w0.dtype)
+    w0, a_p, b_p = w0.contiguous(), a_p.contiguous(), b_p.contiguous()
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty_like(w0)
+    ws = _workspace(lib.mlora_merge_workspace_bytes(N, K, r, code), w0.device)
+    st = lib.mlora_merge(_ptr(w0), _ptr(a_p), _ptr(b_p), _ptr(out), N, K, r, float(alpha_p), code,
+                         _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_merge")
+    return out
 
 
 def lora_forward_metal(x, w0, a, b, alpha: float = 16.0, batch_size=None, seq_len=None,

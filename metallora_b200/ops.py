@@ -1,0 +1,112 @@
+"""LoRA operations (reference: python/metal_lora/ops.py), on sm_100a kernels.
+
+Same function names, arguments and defaults as the reference so callers can
+switch imports.  ``use_metal``/``kernel_kwargs`` are accepted and ignored: there
+is exactly one implementation, the CUDA one, and no fallback.  All tensors must
+be CUDA tensors; bf16, fp16 or fp32 (fp32 runs as split-precision bf16
+tensor-core GEMMs, see ``kernels``).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import kernels as _k
+from .exceptions import ShapeError
+
+
+class _LoRALinearFn(torch.autograd.Function):
+    """y = x.W0^T + s.(x.A^T).B^T with the fused backward (dx, dA, dB in one
+    launch sequence).  W0 gets a gradient only when it requires one (the
+    reference freezes it by default, layers.py:77-78)."""
+
+    @staticmethod
+    def forward(ctx, x2d, w0, a, b, alpha):
+        y, saved = _k.lora_linear_fwd(x2d, w0, a, b, alpha, save_xa=True)
+        ctx.save_for_backward(x2d, w0, a, b, saved)
+        ctx.alpha = alpha
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, w0, a, b, saved = ctx.saved_tensors
+        need_dx = ctx.needs_input_grad[0]
+        dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a, b,
+                                        ctx.alpha, saved, 0.0, need_dx=need_dx)
+        dw0 = None
+        if ctx.needs_input_grad[1]:
+            # trainable base weight (freeze_base=False): plain library GEMM
+            dw0 = (dy.t().float() @ x2d.float()).to(w0.dtype)
+        if dx is not None and not ctx.needs_input_grad[0]:
+            dx = None
+        da = da.to(a.dtype) if ctx.needs_input_grad[2] else None
+        db = db.to(b.dtype) if ctx.needs_input_grad[3] else None
+        return dx, dw0, da, db, None
+
+
+def _apply(x2d, W0, A, B, alpha):
+    return _LoRALinearFn.apply(x2d, W0, A, B, float(alpha))
+
+
+def lora_forward(x, W0, A, B, alpha: float = 16.0, dropout: float = 0.0,  # noqa: N803
+                 training: bool = False, use_metal: bool = True, kernel_kwargs: dict | None = None):
+    """LoRA forward ``h = x.W0^T + (alpha/rank).(x.A^T).B^T`` (ops.py:32-103).
+
+    x is [batch, seq, in] or [seq, in] (any leading shape works); rank is read
+    from ``B.shape[1]`` (ops.py:73).  With ``training`` and ``dropout > 0`` the
+    dropout mask multiplies the LoRA term only, as at ops.py:96-98.
+    """
+    if x.shape[-1] != W0.shape[1]:
+        raise ShapeError(f"x last dim {x.shape[-1]} != in_features {W0.shape[1]}")
+    shp = x.shape
+    x2d = x.reshape(-1, shp[-1])
+    if training and dropout > 0:
+        # ops.py:96-98: output = w0x + scale * bax * mask / (1 - dropout)
+        zero_b = torch.zeros_like(B)
+        w0x = _apply(x2d, W0, A, zero_b, alpha)
+        scale = alpha / B.shape[1]
+        bax = (x2d @ A.t()) @ B.t()
+        mask = torch.bernoulli(torch.full_like(bax, 1.0 - dropout))
+        out = w0x + scale * bax * mask / (1.0 - dropout)
+    else:
+        out = _apply(x2d, W0, A, B, alpha)
+    return out.reshape(*shp[:-1], W0.shape[0])
+
+
+def lora_forward_inference(x, w_merged):
+    """Merged-weight forward (ops.py:106-114): ``x.W'^T`` with no adapter."""
+    shp = x.shape
+    y = _k.linear(x.reshape(-1, shp[-1]), w_merged)
+    return y.reshape(*shp[:-1], w_merged.shape[0])
+
+
+def lora_backward(grad_output, x, A, B, alpha: float = 16.0, clip_value: float = 1.0,  # noqa: N803
+                  use_metal: bool = True):
+    """Gradients of A and B (ops.py:117-155), clipped elementwise to
+    +-clip_value after the full reduction, returned in A's/B's dtype."""
+    g = grad_output.reshape(-1, grad_output.shape[-1])
+    xx = x.reshape(-1, x.shape[-1])
+    clip = float(clip_value) if clip_value is not None else 0.0
+    _, da, db = _k.lora_linear_bwd(g, xx, None, A, B, alpha, None, clip, need_dx=False)
+    return da.to(A.dtype), db.to(B.dtype)
+
+
+# ops.py:158-159
+lora_backward_efficient = lora_backward
+
+
+def merge_lora_weights(W0, A, B, alpha: float = 16.0):  # noqa: N803
+    """``W0 + (alpha/A.shape[0]) . B.A`` (ops.py:162-172) on the merge kernel."""
+    return _k.merge(W0, A, B, alpha)
+
+
+def unmerge_lora_weights(w_merged, W0, A, B, alpha: float = 16.0):  # noqa: N803
+    """Recovers (A, B) from merged weights by truncated SVD (ops.py:175-193).
+    Not on the hot path: uses torch.linalg.svd."""
+    rank = A.shape[0]
+    scale = alpha / rank
+    delta = (w_merged.float() - W0.float()) / scale
+    u, s, vt = torch.linalg.svd(delta, full_matrices=False)
+    sqrt_s = torch.sqrt(s[:rank])
+    a_rec = torch.diag(sqrt_s) @ vt[:rank, :]
+    b_rec = u[:, :rank] @ torch.diag(sqrt_s)
+    return a_rec.to(A.dtype), b_rec.to(B.dtype)

@@ -13,7 +13,7 @@ authoritative path of Wilbatronic/MetalLora -- in the same op order:
 * merge             ``python/metal_lora/ops.py:162-172``
 * layer wrapper     ``python/metal_lora/layers.py:83-106`` (reshape, bias after)
 * global-norm clip  ``python/metal_lora/trainer.py:237-240``
-* AdamW step        ``tests/test_parity.py:57-64`` (== kernels.py:333-343)
+* AdamW step        ``kernels.py:333-343`` (pinned by tests/test_parity.py:57-64)
 
 Parity status: pinned.  ``tests/test_oracle_pin.py`` checks every function here
 against the reference's own kernels run on the CPU (``oracle/_ref``, built by
@@ -119,17 +119,19 @@ def clip_grad_norm(grads, max_norm, acc=np.float32):
 
 
 def adamw_step(param, grad, m, v, lr, beta1, beta2, eps, wd, step, acc=np.float32):
-    """AdamW with bias correction, as pinned by tests/test_parity.py:57-64 and
-    written in the live kernel kernels.py:333-343:
-    m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*g*g;
+    """AdamW with bias correction, as written in the live kernel
+    kernels.py:333-343 (and, up to the order of the g*g product, in
+    tests/test_parity.py:57-64):
+    m = b1*m + (1-b1)*g; v = b2*v + ((1-b2)*g)*g;
     p -= lr*(m/(1-b1^t) / (sqrt(v/(1-b2^t)) + eps) + wd*p).
+    The operation order is the kernel's, so fp32 results are bit-identical to it.
     Returns (param, m, v)."""
     p, g = _as(param, acc), _as(grad, acc)
     m, v = _as(m, acc), _as(v, acc)
     b1t = acc(beta1) ** acc(step)
     b2t = acc(beta2) ** acc(step)
     m = acc(beta1) * m + (acc(1) - acc(beta1)) * g
-    v = acc(beta2) * v + (acc(1) - acc(beta2)) * (g * g)
+    v = acc(beta2) * v + ((acc(1) - acc(beta2)) * g) * g
     m_hat = m / (acc(1) - b1t)
     v_hat = v / (acc(1) - b2t)
     p = p - acc(lr) * (m_hat / (np.sqrt(v_hat) + acc(eps)) + acc(wd) * p)

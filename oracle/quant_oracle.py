@@ -27,8 +27,9 @@ bit-exact against them):
 * NF4: per (row, block of ``bs`` along K) ``absmax = max|w|``; code =
   argmin_i |w/absmax - LEVELS[i]|, ties to the lower index; an all-zero block
   gets absmax 0 and code 7 (level 0.0).
-* int<b> asymmetric: per (row, group) ``scale = fp16((max-min)/(2^b-1))`` (1.0
-  when that is 0), ``zero = clamp(rint(-min/scale), 0, 2^b-1)`` stored fp16,
+* int<b> asymmetric: per (row, group) ``scale = (max-min)/(2^b-1)`` computed in
+  fp32 and rounded UP to fp16 (so the group's range always fits; 1.0 when it
+  is 0), ``zero = clamp(rint(-min/scale), 0, 2^b-1)`` stored fp16,
   ``q = clamp(rint(w/scale) + zero, 0, 2^b-1)`` with round-half-even.
 
 Dequantisation is pinned bit-exact against the reference's own
@@ -122,14 +123,17 @@ def quantize_int_grouped(W, bits, group=128):
     qmax = np.float32(2 ** bits - 1)
     pad = ng * group - K
     if pad:
-        # padded lanes repeat the group's first element so they do not move min/max
+        # padded lanes repeat the row's last element so they do not move min/max
         Wp = np.concatenate([W, np.repeat(W[:, -1:], pad, axis=1)], axis=1)
     else:
         Wp = W
     g = Wp.reshape(N, ng, group)
     wmin = g.min(axis=2)
     wmax = g.max(axis=2)
-    scale = ((wmax - wmin) / qmax).astype(np.float32).astype(np.float16)
+    s32 = ((wmax - wmin) / qmax).astype(np.float32)
+    scale = s32.astype(np.float16)
+    low = scale.astype(np.float32) < s32
+    scale[low] = np.nextafter(scale[low], np.float16(np.inf))  # round up
     scale = np.where(scale == 0, np.float16(1.0), scale)
     s32 = scale.astype(np.float32)
     zero = np.clip(np.rint((-wmin) / s32), 0, qmax).astype(np.float32)
