@@ -20,9 +20,10 @@
  *   - Kernels bound every internal wait.  A wait that runs out records a code
  *     in a per-device status word (mlora_device_status) instead of hanging.
  *   - Shapes: M tokens, K in_features, N out_features, r LoRA rank (1..256).
- *     The tensor-core paths need K % 8 == 0, N % 8 == 0 and r % 8 == 0 (16-byte
- *     TMA row alignment); the Python layer zero-pads the rank to a multiple of 8,
- *     which leaves every result unchanged.
+ *     The tensor-core paths need K % 8 == 0 and r % 8 == 0 (16-byte TMA row
+ *     alignment), and N % 8 == 0 for the backward (rows of dy); the Python
+ *     layer zero-pads the rank to a multiple of 8, which leaves every result
+ *     unchanged.
  */
 #ifndef METALLORA_B200_H_
 #define METALLORA_B200_H_

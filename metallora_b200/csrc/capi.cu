@@ -107,13 +107,16 @@ int check_device() {
   return MLORA_OK;
 }
 
-int check_shapes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype) {
+// need_n8: N is the row length of an operand read by TMA (backward: dy).
+int check_shapes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype, bool need_n8 = true) {
   if (M <= 0 || K <= 0 || N <= 0) return fail(MLORA_ERR_INVALID_ARG, "M, K, N must be positive");
   if (r < 1 || r > 256) return fail(MLORA_ERR_INVALID_ARG, "rank must be in [1, 256]");
   if (dtype != MLORA_DTYPE_BF16 && dtype != MLORA_DTYPE_F16 && dtype != MLORA_DTYPE_F32)
     return fail(MLORA_ERR_UNSUPPORTED, "dtype must be BF16, F16 or F32");
-  if (K % 8 || N % 8 || r % 8)
-    return fail(MLORA_ERR_UNSUPPORTED, "K, N and r must be multiples of 8 (16-byte rows)");
+  if (K % 8 || r % 8)
+    return fail(MLORA_ERR_UNSUPPORTED, "K and r must be multiples of 8 (16-byte rows)");
+  if (need_n8 && N % 8)
+    return fail(MLORA_ERR_UNSUPPORTED, "N must be a multiple of 8 for the backward (16-byte rows of dy)");
   if (M > (int64_t(1) << 31) - 1 || K > (1 << 24) || N > (1 << 24))
     return fail(MLORA_ERR_UNSUPPORTED, "shape too large");
   return MLORA_OK;
@@ -588,7 +591,7 @@ size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64
 int mlora_lora_forward(const void* x, const void* w0, const void* a, const void* b, void* y,
                        void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                        int dtype, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_shapes(M, K, N, r, dtype);
+  int rc = check_shapes(M, K, N, r, dtype, false);
   if (rc) return rc;
   if (!x || !w0 || !a || !b || !y) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(x) || !aligned16(w0) || !aligned16(a) || !aligned16(b) || !aligned16(y) ||
@@ -826,7 +829,7 @@ size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) 
 
 int mlora_linear(const void* x, const void* w, void* y, int64_t M, int64_t K, int64_t N, int dtype,
                  void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_shapes(M, K, N, 8, dtype);
+  int rc = check_shapes(M, K, N, 8, dtype, false);
   if (rc) return rc;
   if (!x || !w || !y) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
   if ((rc = check_ptrs16({x, w, y, workspace}))) return rc;

@@ -49,6 +49,7 @@ struct GemmParams {
   const void* c;  // optional addend, same type/layout as d (ldc)
   long long ldc;
   float acc_scale;
+  int vec_ok;     // rows of d (and c) allow 16-byte vector access
   uint32_t* status;
 };
 
@@ -212,6 +213,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.acc_scale;
+          if (!p.vec_ok) {
+            // ragged or unaligned rows: element-wise, bounds-checked
+            const OutT* crow = p.c != nullptr ? reinterpret_cast<const OutT*>(p.c) +
+                                                    static_cast<long long>(m) * p.ldc + n0
+                                              : nullptr;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (n0 + i < p.N) {
+                float o = v[i];
+                if (crow != nullptr) o += static_cast<float>(crow[i]);
+                out_row[c * 32 + i] = static_cast<OutT>(o);
+              }
+            }
+            continue;
+          }
           if (p.c != nullptr) {
             const OutT* crow = reinterpret_cast<const OutT*>(p.c) +
                                static_cast<long long>(m) * p.ldc + n0;
@@ -306,6 +322,14 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.c = a.c;
   p.ldc = a.ldc;
   p.acc_scale = a.acc_scale;
+  {
+    const int64_t vec = 16 / static_cast<int64_t>(sizeof(OutT));
+    const bool d_ok = a.N % vec == 0 && a.ldd % vec == 0 &&
+                      (reinterpret_cast<uintptr_t>(a.d) & 15u) == 0;
+    const bool c_ok = a.c == nullptr ||
+                      (a.ldc % vec == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15u) == 0);
+    p.vec_ok = (d_ok && c_ok) ? 1 : 0;
+  }
   p.status = device_status_ptr();
 
   auto kern = lora_gemm_kernel<kWMN, kBF16, OutT>;

@@ -76,6 +76,20 @@ def test_forward_and_backward_parity(cuda, dtype, shape):
     assert status_ok()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(130, 256, 300, 16), (64, 128, 7, 8), (33, 512, 1001, 24)])
+def test_forward_ragged_out_features(cuda, dtype, shape):
+    """out_features need not be a multiple of 8 for the forward (scalar
+    epilogue stores for ragged/unaligned rows of y)."""
+    from metallora_b200 import kernels as K
+    M, Kd, N, r = shape
+    (x, W, A, B, _), (xh, Wh, Ah, Bh, _) = make(M, Kd, N, r, dtype, cuda, seed=11)
+    y, _ = K.lora_linear_fwd(x, W, A, B, 16.0)
+    torch.cuda.synchronize()
+    assert_close(y, lo.lora_forward(xh, Wh, Ah, Bh, 16.0, np.float64), TOL[dtype])
+    assert status_ok()
+
+
 def test_saved_intermediate_matches_recompute(cuda):
     from metallora_b200 import kernels as K
     (x, W, A, B, dy), _ = make(200, 256, 256, 16, torch.bfloat16, cuda, seed=4)
