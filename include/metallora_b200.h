@@ -154,6 +154,30 @@ MLORA_API int mlora_merge(const void* w0, const void* a, const void* b, void* w_
                           int64_t K, int64_t r, float alpha, int dtype, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* ---- allocation-free weight gradients -------------------------------------
+ * No counterpart in the reference: an addition of this library for callers
+ * that cannot allocate device memory when the backward runs (a process whose
+ * device memory is all owned by its own pool, or a loop that must not call
+ * cudaMalloc because it can wait on the whole device).  It computes what
+ * mlora_lora_backward computes with w0 = dx = saved_xa = NULL (da, db, the
+ * same clip), taking its scratch from a 32 MiB array built into the library
+ * instead of a caller workspace; every GPU that loads the library holds that
+ * array until the process exits.
+ *   - Shapes whose scratch exceeds the array (see
+ *     mlora_lora_grads_static_scratch_bytes) return MLORA_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's device address (once
+ *     per device, with that device current); make that first call before any
+ *     stream capture.
+ *   - All calls on a device share the array: calls whose work overlaps on the
+ *     GPU (different streams, no ordering between them) race and corrupt each
+ *     other's results.  Each call clears the parts that must start at zero.
+ *   - BF16 or F16 only. */
+MLORA_API size_t mlora_lora_grads_static_scratch_bytes(void);
+MLORA_API int mlora_lora_grads_static(const void* dy, const void* x, const void* a, const void* b,
+                                      float* da, float* db, int64_t M, int64_t K, int64_t N,
+                                      int64_t r, float alpha, float clip_value, int dtype,
+                                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_linear": (i32, [vp, vp, vp, i64, i64, i64, i32, vp, sz, vp]),
     "mlora_merge_workspace_bytes": (sz, [i64, i64, i64, i32]),
     "mlora_merge": (i32, [vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp]),
+    "mlora_lora_grads_static_scratch_bytes": (sz, []),
+    "mlora_lora_grads_static": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, f32, i32,
+                                      vp]),
 }
 
 
