@@ -130,6 +130,18 @@ MLORA_API int mlora_lora_backward(const void* dy, const void* x, const void* w0,
                         float clip_value, int dtype, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Flags of mlora_lora_backward_ex. */
+#define MLORA_BWD_ACCUMULATE 1 /* da += result, db += result (after the clip) */
+
+/* mlora_lora_backward with flags; with MLORA_BWD_ACCUMULATE the weight
+ * gradients are added into da/db (gradient accumulation across micro-batches,
+ * the reference trainer's gradient_accumulation_steps, trainer.py:82). */
+MLORA_API int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const void* a,
+                                     const void* b, const void* saved_xa, void* dx, float* da,
+                                     float* db, int64_t M, int64_t K, int64_t N, int64_t r,
+                                     float alpha, float clip_value, int dtype, int flags,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- merged weights ------------------------------------------------------ */
 
 /* Bytes of workspace mlora_linear needs (0 except for F32). */
@@ -153,6 +165,40 @@ MLORA_API size_t mlora_merge_workspace_bytes(int64_t N, int64_t K, int64_t r, in
 MLORA_API int mlora_merge(const void* w0, const void* a, const void* b, void* w_out, int64_t N,
                           int64_t K, int64_t r, float alpha, int dtype, void* workspace,
                           size_t workspace_bytes, void* stream);
+
+/* ---- optimizer --------------------------------------------------------- */
+
+/* One AdamW step over a flat buffer of n parameters (reference:
+ * kernels.lora_adamw_step_metal, python/metal_lora/kernels.py:615-643, kernel
+ * :314-344, same operation order, bit-identical in fp32):
+ *   g = grad * (*grad_scale or 1);  grad := 0
+ *   m = b1 m + (1-b1) g;  v = b2 v + ((1-b2) g) g
+ *   p -= lr (m/(1-b1^t) / (sqrt(v/(1-b2^t)) + eps) + wd p)
+ * state is the device array [t, b1^t, b2^t] (kernels.py:471-481).  param may be
+ * BF16, F16 or F32; grad, m, v are F32.  weight_decay 0 gives Adam. */
+MLORA_API int mlora_adamw_step(void* param, float* grad, float* m, float* v, const float* state,
+                               int64_t n, float lr, float beta1, float beta2, float eps,
+                               float weight_decay, int param_dtype, const float* grad_scale,
+                               void* stream);
+
+/* p -= lr * g * (*grad_scale or 1); grad := 0 (the trainer's "sgd" optimizer,
+ * python/metal_lora/trainer.py:213-214). */
+MLORA_API int mlora_sgd_step(void* param, float* grad, int64_t n, float lr, int param_dtype,
+                             const float* grad_scale, void* stream);
+
+/* state := [t+1, b1^(t+1), b2^(t+1)] on the device (reference:
+ * kernels.persistent_gpu_state_step, kernels.py:484-499, kernel :351-362). */
+MLORA_API int mlora_adam_state_step(float* state, float beta1, float beta2, void* stream);
+
+/* Bytes of workspace mlora_grad_norm_clip needs. */
+MLORA_API size_t mlora_grad_norm_workspace_bytes(void);
+
+/* Global-norm clip factor of a flat gradient buffer (trainer.py:237-240):
+ * out[1] = ||grad||_2, out[0] = min(1, max_norm / (out[1] + 1e-6)), or 1 when
+ * max_norm <= 0.  out is a device float[2]; pass out as grad_scale to the
+ * optimizer step.  Deterministic (fixed reduction order). */
+MLORA_API int mlora_grad_norm_clip(const float* grad, int64_t n, float max_norm, float* out,
+                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- allocation-free weight gradients -------------------------------------
  * No counterpart in the reference: an addition of this library for callers

@@ -21,6 +21,8 @@ MLORA_ERR_CUDA = -3
 MLORA_ERR_WORKSPACE = -4
 MLORA_ERR_DEVICE = -5
 
+BWD_ACCUMULATE = 1
+
 DTYPE_BF16 = 0
 DTYPE_F16 = 1
 DTYPE_F32 = 2
@@ -49,10 +51,17 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_lora_backward_workspace_bytes": (sz, [i64, i64, i64, i64, i32]),
     "mlora_lora_backward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, f32,
                                   i32, vp, sz, vp]),
+    "mlora_lora_backward_ex": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32,
+                                     f32, i32, i32, vp, sz, vp]),
     "mlora_linear_workspace_bytes": (sz, [i64, i64, i64, i32]),
     "mlora_linear": (i32, [vp, vp, vp, i64, i64, i64, i32, vp, sz, vp]),
     "mlora_merge_workspace_bytes": (sz, [i64, i64, i64, i32]),
     "mlora_merge": (i32, [vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp]),
+    "mlora_adamw_step": (i32, [vp, vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp]),
+    "mlora_sgd_step": (i32, [vp, vp, i64, f32, i32, vp, vp]),
+    "mlora_adam_state_step": (i32, [vp, f32, f32, vp]),
+    "mlora_grad_norm_workspace_bytes": (sz, []),
+    "mlora_grad_norm_clip": (i32, [vp, i64, f32, vp, vp, sz, vp]),
     "mlora_lora_grads_static_scratch_bytes": (sz, []),
     "mlora_lora_grads_static": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, f32, i32,
                                       vp]),

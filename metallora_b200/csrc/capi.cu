@@ -344,8 +344,8 @@ int lora_forward_f32(const float* x, const float* w0, const float* a, const floa
 
 int lora_backward_f32(const float* dy, const float* x, const float* w0, const float* a,
                       const float* b, float* dx, float* da, float* db, int64_t M, int64_t K,
-                      int64_t N, int64_t r, float alpha, float clip, void* workspace,
-                      size_t workspace_bytes, cudaStream_t s) {
+                      int64_t N, int64_t r, float alpha, float clip, bool accumulate,
+                      void* workspace, size_t workspace_bytes, cudaStream_t s) {
   const bool want_dx = dx != nullptr;
   const F32BwdPlan need = plan_backward_f32(nullptr, M, K, N, r, want_dx);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
@@ -438,6 +438,7 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   w[0].out = db;
   w[0].ldo = r;
   w[0].transposed = false;
+  w[0].accumulate = accumulate;
   w[0].clip = clip;
   w[0].partials = p.wpart_db;
   w[0].counters = p.counters + 2 * tm;
@@ -668,6 +669,17 @@ int mlora_lora_backward(const void* dy, const void* x, const void* w0, const voi
                         int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                         float clip_value, int dtype, void* workspace, size_t workspace_bytes,
                         void* stream) {
+  return mlora_lora_backward_ex(dy, x, w0, a, b, saved_xa, dx, da, db, M, K, N, r, alpha,
+                                clip_value, dtype, 0, workspace, workspace_bytes, stream);
+}
+
+int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const void* a,
+                           const void* b, const void* saved_xa, void* dx, float* da, float* db,
+                           int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                           float clip_value, int dtype, int flags, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  const bool accumulate = (flags & MLORA_BWD_ACCUMULATE) != 0;
+  if (flags & ~MLORA_BWD_ACCUMULATE) return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
   int rc = check_shapes(M, K, N, r, dtype);
   if (rc) return rc;
   if (!dy || !x || !a || !b || !da || !db) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
@@ -681,7 +693,7 @@ int mlora_lora_backward(const void* dy, const void* x, const void* w0, const voi
     return lora_backward_f32(static_cast<const float*>(dy), static_cast<const float*>(x),
                              static_cast<const float*>(w0), static_cast<const float*>(a),
                              static_cast<const float*>(b), static_cast<float*>(dx), da, db, M, K,
-                             N, r, alpha, clip_value, workspace, workspace_bytes,
+                             N, r, alpha, clip_value, accumulate, workspace, workspace_bytes,
                              static_cast<cudaStream_t>(stream));
   const BwdPlan need = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
@@ -773,6 +785,7 @@ int mlora_lora_backward(const void* dy, const void* x, const void* w0, const voi
   w[0].out = db;
   w[0].ldo = r;
   w[0].transposed = false;
+  w[0].accumulate = accumulate;
   w[0].clip = clip_value;
   w[0].partials = p.wpart_db;
   w[0].counters = p.counters + 2 * tm;
@@ -820,6 +833,62 @@ int mlora_profile_read(double* total_ms, long long* launches, int nkinds, int re
     g_prof_recs.clear();
   }
   return MLORA_OK;
+}
+
+// ---- optimizer ---------------------------------------------------------------
+
+int mlora_adamw_step(void* param, float* grad, float* m, float* v, const float* state, int64_t n,
+                     float lr, float beta1, float beta2, float eps, float weight_decay,
+                     int param_dtype, const float* grad_scale, void* stream) {
+  if (!param || !grad || !m || !v || !state) return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if (n <= 0) return fail(MLORA_ERR_INVALID_ARG, "n must be positive");
+  if (param_dtype < MLORA_DTYPE_BF16 || param_dtype > MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_UNSUPPORTED, "param dtype must be BF16, F16 or F32");
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_adamw(param, param_dtype, grad, m, v, state, n, lr, beta1, beta2, eps,
+                      weight_decay, grad_scale, 0, static_cast<cudaStream_t>(stream));
+}
+
+int mlora_sgd_step(void* param, float* grad, int64_t n, float lr, int param_dtype,
+                   const float* grad_scale, void* stream) {
+  if (!param || !grad) return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if (n <= 0) return fail(MLORA_ERR_INVALID_ARG, "n must be positive");
+  if (param_dtype < MLORA_DTYPE_BF16 || param_dtype > MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_UNSUPPORTED, "param dtype must be BF16, F16 or F32");
+  int rc = check_device();
+  if (rc) return rc;
+  // m, v and state are not touched in SGD mode.
+  return launch_adamw(param, param_dtype, grad, nullptr, nullptr, nullptr, n, lr, 0.f, 0.f, 0.f,
+                      0.f, grad_scale, 1, static_cast<cudaStream_t>(stream));
+}
+
+int mlora_adam_state_step(float* state, float beta1, float beta2, void* stream) {
+  if (!state) return fail(MLORA_ERR_INVALID_ARG, "NULL state");
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_adam_state_step(state, beta1, beta2, static_cast<cudaStream_t>(stream));
+}
+
+size_t mlora_grad_norm_workspace_bytes(void) {
+  return 256 + align_up(static_cast<size_t>(2 * 1024) * 4, 256);
+}
+
+int mlora_grad_norm_clip(const float* grad, int64_t n, float max_norm, float* out,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (!grad || !out) return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if (n <= 0) return fail(MLORA_ERR_INVALID_ARG, "n must be positive");
+  int rc = check_device();
+  if (rc) return rc;
+  if (norm_grid() > 2 * 1024) return fail(MLORA_ERR_UNSUPPORTED, "too many SMs");
+  if (!workspace || workspace_bytes < mlora_grad_norm_workspace_bytes() || !aligned16(workspace))
+    return fail(MLORA_ERR_WORKSPACE, "grad-norm workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* counter = static_cast<uint32_t*>(workspace);
+  float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  cudaError_t e = cudaMemsetAsync(counter, 0, 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  return launch_grad_norm(grad, n, max_norm, partials, counter, out, s);
 }
 
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {

@@ -116,6 +116,7 @@ struct WgradArgs {
   float* out;
   int64_t ldo;
   bool transposed;
+  bool accumulate = false;  // out += result (after the clip) instead of out = result
   float clip;       // <= 0: no clip
   float* partials;  // [splits, P, R]
   uint32_t* counters;  // [ceil(P/128)] zeroed
@@ -140,5 +141,14 @@ int launch_split3_rows(const float* src, int64_t rows, int64_t cols, int64_t ld_
 int launch_split3_cols_t(const float* src, int64_t N, int64_t r, int64_t ld_src, void* dst,
                          int64_t R, int64_t seg, int64_t ld_dst, uint32_t pattern,
                          cudaStream_t stream);
+
+// ---------------------------------------------------------------- optimizer --
+int norm_grid();
+int launch_grad_norm(const float* g, int64_t n, float max_norm, float* partials,
+                     uint32_t* counter, float* out, cudaStream_t s);
+int launch_adamw(void* param, int dtype, float* grad, float* m, float* v, const float* state,
+                 int64_t n, float lr, float b1, float b2, float eps, float wd,
+                 const float* grad_scale, int mode, cudaStream_t s);
+int launch_adam_state_step(float* state, float b1, float b2, cudaStream_t s);
 
 }  // namespace mlora

@@ -332,6 +332,7 @@ struct WgradProblem {
   float* out;
   long long ldo;
   int transposed;
+  int accumulate;
   float clip;
   float* partials;
   uint32_t* counters;
@@ -407,10 +408,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (j < q.r) {
           float v = acc[j];
           if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
-          if (q.transposed)
-            q.out[static_cast<long long>(j) * q.ldo + prow] = v;
-          else
-            q.out[prow * q.ldo + j] = v;
+          float* dst = q.transposed ? q.out + static_cast<long long>(j) * q.ldo + prow
+                                    : q.out + prow * q.ldo + j;
+          *dst = q.accumulate ? *dst + v : v;
         }
       }
     }
@@ -487,6 +487,7 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
     q.out = a.out;
     q.ldo = a.ldo;
     q.transposed = a.transposed ? 1 : 0;
+    q.accumulate = a.accumulate ? 1 : 0;
     q.clip = a.clip;
     q.partials = a.partials;
     q.counters = a.counters;

@@ -120,11 +120,14 @@ def lora_linear_fwd(x2d: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: tor
 def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | None,
                     a: torch.Tensor, b: torch.Tensor, alpha: float,
                     saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
-                    need_dx: bool = True):
+                    need_dx: bool = True, da_out: torch.Tensor | None = None,
+                    db_out: torch.Tensor | None = None):
     """(dx, dA, dB) of the LoRA linear for 2-D dy [M, N], x [M, K].
 
     dA/dB are fp32 (master-gradient precision); clip_value > 0 clips them
-    elementwise after the full reduction (ops.py:155)."""
+    elementwise after the full reduction (ops.py:155).  With ``da_out`` and
+    ``db_out`` (contiguous fp32 [r, K] / [N, r], rank a multiple of 8) the
+    gradients are ADDED into those buffers and returned."""
     _need_cuda(dy2d, x2d, a, b)
     dt = x2d.dtype
     code = _dtype_code(x2d)
@@ -145,14 +148,27 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
     dy2d, x2d, a_p, b_p = (t.contiguous() for t in (dy2d, x2d, a_p, b_p))
     lib = _lib.load()
     dx = torch.empty((M, K), dtype=dt, device=x2d.device) if need_dx else None
-    da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
-    db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
+    flags = 0
+    if da_out is not None or db_out is not None:
+        if r != r_orig:
+            raise ShapeError("gradient accumulation buffers need a rank that is a multiple of 8")
+        for name, t, shp in (("da_out", da_out, (r, K)), ("db_out", db_out, (N, r))):
+            if t is None or t.dtype != torch.float32 or tuple(t.shape) != shp or \
+                    not t.is_contiguous():
+                raise ShapeError(f"{name} must be a contiguous fp32 tensor of shape {shp}")
+        da, db = da_out, db_out
+        flags = _lib.BWD_ACCUMULATE
+    else:
+        da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
+        db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
     ws = _workspace(lib.mlora_lora_backward_workspace_bytes(M, K, N, r, code), x2d.device)
-    st = lib.mlora_lora_backward(_ptr(dy2d), _ptr(x2d), _ptr(w0) if need_dx else None, _ptr(a_p),
-                                 _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da), _ptr(db), M, K, N,
-                                 r, float(alpha_p), float(clip_value), code, _ptr(ws),
-                                 ws.numel(), _stream())
+    st = lib.mlora_lora_backward_ex(_ptr(dy2d), _ptr(x2d), _ptr(w0) if need_dx else None,
+                                    _ptr(a_p), _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da),
+                                    _ptr(db), M, K, N, r, float(alpha_p), float(clip_value), code,
+                                    flags, _ptr(ws), ws.numel(), _stream())
     _lib.check(st, "mlora_lora_backward")
+    if flags:
+        return dx, da, db
     if r != r_orig:
         da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
     return dx, da, db
@@ -211,3 +227,63 @@ def lora_backward_metal(grad_output, x, a, b, alpha: float = 16.0, clip_value: f
     xx = x.reshape(-1, x.shape[-1])
     _, da, db = lora_linear_bwd(g, xx, None, a, b, alpha, None, clip_value, need_dx=False)
     return da.to(a.dtype), db.to(b.dtype)
+
+
+# ------------------------------------------------------------------ optimizer --
+
+def persistent_gpu_state_init(beta1: float = 0.9, beta2: float = 0.999, device=None):
+    """Device Adam state [step, beta1^step, beta2^step] (kernels.py:471-481).
+
+    Starts at step 0 ([0, 1, 1]); ``persistent_gpu_state_step`` advances it
+    before each update, so the first update uses step 1 and beta^1 -- the
+    formula tests/test_parity.py:57-64 pins.  (The reference initialises to
+    [1, b1, b2] and also steps before the first update, so its first update
+    uses beta^2.)"""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return torch.tensor([0.0, 1.0, 1.0], dtype=torch.float32, device=dev)
+
+
+def persistent_gpu_state_step(gpu_state: torch.Tensor, beta1: float = 0.9, beta2: float = 0.999):
+    """state := [t+1, b1^(t+1), b2^(t+1)] on the device (kernels.py:484-499)."""
+    _need_cuda(gpu_state)
+    _lib.check(_lib.load().mlora_adam_state_step(_ptr(gpu_state), beta1, beta2, _stream()),
+               "mlora_adam_state_step")
+
+
+def lora_adamw_step_metal(param, grad, m, v, gpu_state, lr: float, beta1: float, beta2: float,
+                          eps: float, wd: float, grad_scale: torch.Tensor | None = None):
+    """In-place AdamW step (kernels.py:615-643): updates param, m, v and zeroes
+    grad.  param bf16/fp16/fp32; grad, m, v fp32 and contiguous."""
+    _need_cuda(param, grad, m, v, gpu_state)
+    for name, t in (("grad", grad), ("m", m), ("v", v)):
+        if t.dtype != torch.float32 or t.numel() != param.numel() or not t.is_contiguous():
+            raise ShapeError(f"{name} must be contiguous fp32 with param's size")
+    if not param.is_contiguous():
+        raise ShapeError("param must be contiguous")
+    st = _lib.load().mlora_adamw_step(_ptr(param), _ptr(grad), _ptr(m), _ptr(v), _ptr(gpu_state),
+                                      param.numel(), lr, beta1, beta2, eps, wd,
+                                      _dtype_code(param), _ptr(grad_scale), _stream())
+    _lib.check(st, "mlora_adamw_step")
+
+
+def sgd_step(param, grad, lr: float, grad_scale: torch.Tensor | None = None):
+    """In-place p -= lr * g (zeroes grad)."""
+    _need_cuda(param, grad)
+    st = _lib.load().mlora_sgd_step(_ptr(param), _ptr(grad), param.numel(), lr, _dtype_code(param),
+                                    _ptr(grad_scale), _stream())
+    _lib.check(st, "mlora_sgd_step")
+
+
+def grad_norm_clip(grad: torch.Tensor, max_norm: float, out: torch.Tensor | None = None):
+    """Device [clip scale, norm] of a flat fp32 gradient (trainer.py:237-240)."""
+    _need_cuda(grad)
+    if grad.dtype != torch.float32 or not grad.is_contiguous():
+        raise ShapeError("grad must be contiguous fp32")
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty(2, dtype=torch.float32, device=grad.device)
+    ws = _workspace(lib.mlora_grad_norm_workspace_bytes(), grad.device)
+    st = lib.mlora_grad_norm_clip(_ptr(grad), grad.numel(), float(max_norm), _ptr(out), _ptr(ws),
+                                  ws.numel(), _stream())
+    _lib.check(st, "mlora_grad_norm_clip")
+    return out

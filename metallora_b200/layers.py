@@ -59,6 +59,10 @@ class LoRALinear(nn.Module):
         else:
             self.register_parameter("bias", None)
         self._best_config = None
+        # Set by a trainer that keeps fp32 master factors in flat buffers:
+        # (A, B) in the compute dtype, and (gA, gB) fp32 gradient sinks.
+        self._compute_ab = None
+        self._grad_sink = None
         logger.debug(f"LoRALinear: {in_features}→{out_features}, rank={rank}")
 
     @property
@@ -72,12 +76,11 @@ class LoRALinear(nn.Module):
                                                                          self.out_features)
         else:
             out = lora_forward(x, self.W0, self.A, self.B, alpha=self.alpha, dropout=self.dropout,
-                               training=self.training)
+                               training=self.training, _compute=self._compute_ab,
+                               _sink=self._grad_sink)
         if self.bias is not None:
             out = out + self.bias
         return out
-
-    __call__ = nn.Module.__call__
 
     @torch.no_grad()
     def merge_weights(self) -> torch.Tensor:

@@ -17,38 +17,53 @@ from .exceptions import ShapeError
 class _LoRALinearFn(torch.autograd.Function):
     """y = x.W0^T + s.(x.A^T).B^T with the fused backward (dx, dA, dB in one
     launch sequence).  W0 gets a gradient only when it requires one (the
-    reference freezes it by default, layers.py:77-78)."""
+    reference freezes it by default, layers.py:77-78).
+
+    A/B may be kept in a wider dtype than x (fp32 master factors with bf16
+    compute): they are cast for the kernels and their gradients returned in
+    their own dtype.  ``compute`` optionally supplies ready-made casts, and
+    ``sink`` = (gA, gB) fp32 buffers receives the LoRA gradients by in-kernel
+    accumulation instead of autograd (the trainer's flat gradient buffer)."""
 
     @staticmethod
-    def forward(ctx, x2d, w0, a, b, alpha):
-        y, saved = _k.lora_linear_fwd(x2d, w0, a, b, alpha, save_xa=True)
-        ctx.save_for_backward(x2d, w0, a, b, saved)
+    def forward(ctx, x2d, w0, a, b, alpha, compute, sink):
+        a_c, b_c = compute if compute is not None else (a.to(x2d.dtype), b.to(x2d.dtype))
+        y, saved = _k.lora_linear_fwd(x2d, w0, a_c, b_c, alpha, save_xa=True)
+        ctx.save_for_backward(x2d, w0, a_c, b_c, saved)
         ctx.alpha = alpha
+        ctx.sink = sink
+        ctx.ab_dtypes = (a.dtype, b.dtype)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x2d, w0, a, b, saved = ctx.saved_tensors
+        x2d, w0, a_c, b_c, saved = ctx.saved_tensors
         need_dx = ctx.needs_input_grad[0]
-        dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a, b,
-                                        ctx.alpha, saved, 0.0, need_dx=need_dx)
+        sink = ctx.sink
+        dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a_c, b_c,
+                                        ctx.alpha, saved, 0.0, need_dx=need_dx,
+                                        da_out=sink[0] if sink else None,
+                                        db_out=sink[1] if sink else None)
         dw0 = None
         if ctx.needs_input_grad[1]:
             # trainable base weight (freeze_base=False): plain library GEMM
             dw0 = (dy.t().float() @ x2d.float()).to(w0.dtype)
-        if dx is not None and not ctx.needs_input_grad[0]:
+        if dx is not None and not need_dx:
             dx = None
-        da = da.to(a.dtype) if ctx.needs_input_grad[2] else None
-        db = db.to(b.dtype) if ctx.needs_input_grad[3] else None
-        return dx, dw0, da, db, None
+        if sink is not None:
+            return dx, dw0, None, None, None, None, None
+        da = da.to(ctx.ab_dtypes[0]) if ctx.needs_input_grad[2] else None
+        db = db.to(ctx.ab_dtypes[1]) if ctx.needs_input_grad[3] else None
+        return dx, dw0, da, db, None, None, None
 
 
-def _apply(x2d, W0, A, B, alpha):
-    return _LoRALinearFn.apply(x2d, W0, A, B, float(alpha))
+def _apply(x2d, W0, A, B, alpha, compute=None, sink=None):
+    return _LoRALinearFn.apply(x2d, W0, A, B, float(alpha), compute, sink)
 
 
 def lora_forward(x, W0, A, B, alpha: float = 16.0, dropout: float = 0.0,  # noqa: N803
-                 training: bool = False, use_metal: bool = True, kernel_kwargs: dict | None = None):
+                 training: bool = False, use_metal: bool = True, kernel_kwargs: dict | None = None,
+                 _compute=None, _sink=None):
     """LoRA forward ``h = x.W0^T + (alpha/rank).(x.A^T).B^T`` (ops.py:32-103).
 
     x is [batch, seq, in] or [seq, in] (any leading shape works); rank is read
@@ -68,7 +83,7 @@ def lora_forward(x, W0, A, B, alpha: float = 16.0, dropout: float = 0.0,  # noqa
         mask = torch.bernoulli(torch.full_like(bax, 1.0 - dropout))
         out = w0x + scale * bax * mask / (1.0 - dropout)
     else:
-        out = _apply(x2d, W0, A, B, alpha)
+        out = _apply(x2d, W0, A, B, alpha, _compute, _sink)
     return out.reshape(*shp[:-1], W0.shape[0])
 
 

@@ -118,18 +118,20 @@ def clip_grad_norm(grads, max_norm, acc=np.float32):
     return [g * scale for g in gs], float(norm)
 
 
-def adamw_step(param, grad, m, v, lr, beta1, beta2, eps, wd, step, acc=np.float32):
+def adamw_step(param, grad, m, v, lr, beta1, beta2, eps, wd, step, acc=np.float32, b1t=None,
+               b2t=None):
     """AdamW with bias correction, as written in the live kernel
     kernels.py:333-343 (and, up to the order of the g*g product, in
     tests/test_parity.py:57-64):
     m = b1*m + (1-b1)*g; v = b2*v + ((1-b2)*g)*g;
     p -= lr*(m/(1-b1^t) / (sqrt(v/(1-b2^t)) + eps) + wd*p).
     The operation order is the kernel's, so fp32 results are bit-identical to it.
-    Returns (param, m, v)."""
+    ``b1t``/``b2t`` override beta^step (the kernel reads them from its device
+    state, where they are running products).  Returns (param, m, v)."""
     p, g = _as(param, acc), _as(grad, acc)
     m, v = _as(m, acc), _as(v, acc)
-    b1t = acc(beta1) ** acc(step)
-    b2t = acc(beta2) ** acc(step)
+    b1t = acc(beta1) ** acc(step) if b1t is None else acc(b1t)
+    b2t = acc(beta2) ** acc(step) if b2t is None else acc(b2t)
     m = acc(beta1) * m + (acc(1) - acc(beta1)) * g
     v = acc(beta2) * v + ((acc(1) - acc(beta2)) * g) * g
     m_hat = m / (acc(1) - b1t)

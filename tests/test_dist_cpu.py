@@ -1,0 +1,64 @@
+"""Multi-rank logic of the data-parallel layer on CPU ranks (gloo, world 2):
+token sharding, gradient averaging and replica-sync checks."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from metallora_b200.distributed import (average_gradients, replicas_in_sync, shard_bounds,
+                                        shard_tokens)
+
+
+def test_shard_bounds_cover_all_tokens():
+    for n in (1, 7, 8192, 8193):
+        for world in (1, 2, 3, 8):
+            spans = [shard_bounds(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            sizes = [e - b for b, e in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_bounds(10, 2, 2)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=30))
+    try:
+        x = torch.arange(4 * 6 * 3, dtype=torch.float32).reshape(4, 6, 3)
+        mine = shard_tokens(x, rank, world)
+        g = torch.full((10,), float(rank + 1))
+        average_gradients(g)
+        same = replicas_in_sync(g)
+        p = torch.full((5,), 1.0 + rank)  # deliberately different
+        diff = replicas_in_sync(p)
+        q.put((rank, mine.shape[0], g.tolist(), same, diff))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_average_and_sync():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [r[1] for r in res] == [12, 12]           # 24 tokens over 2 ranks
+    for r in res:
+        assert r[2] == [1.5] * 10                    # mean of 1 and 2
+        assert r[3] is True and r[4] is False
