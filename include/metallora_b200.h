@@ -166,6 +166,65 @@ MLORA_API int mlora_merge(const void* w0, const void* a, const void* b, void* w_
                           int64_t K, int64_t r, float alpha, int dtype, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* ---- quantised base weights ---------------------------------------------
+ * Layouts (the reference shaders' conventions, kernels/lora_quantized.metal):
+ *   NF4 : codes uint8 [N, K/2], low nibble = even k, high nibble = odd k
+ *         (:70-74); scales = absmax fp32 [N, ceil(K/group)] (:122,:135);
+ *         w = NF4_LEVELS[code] * absmax with the 4-decimal levels (:10-15).
+ *   INT4: codes as NF4; scales and zeros fp16 [N, ceil(K/group)];
+ *         w = (q - zero) * scale (:17-20; the reference uses one fp32 scale and
+ *         zero per row, which is group = K here).
+ *   INT8: codes uint8 [N, K]; scales/zeros as INT4.  (The reference promises
+ *         int8 but has no kernel for it.) */
+#define MLORA_QUANT_NF4 1
+#define MLORA_QUANT_INT4 2
+#define MLORA_QUANT_INT8 3
+
+/* Quantises w [N,K] (BF16/F16/F32) into codes/scales/zeros (zeros unused for
+ * NF4).  NF4: per (row, block of `group`) absmax, nearest level (first on
+ * ties).  INT4/INT8: asymmetric per (row, group): scale = (max-min)/(2^b-1)
+ * rounded up to fp16, zero = rint(-min/scale), q = rint(w/scale) + zero, both
+ * clamped to [0, 2^b-1].  The reference has no quantiser; this is the format's
+ * producer for the kernels below. */
+MLORA_API int mlora_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int scheme,
+                             int64_t group, void* codes, void* scales, void* zeros, void* stream);
+
+/* out [N,K] = dequantised weights in out_dtype.  F32 output is bit-identical to
+ * the reference's dequant_nf4 / dequant_int4 (lora_quantized.metal:17-25);
+ * BF16/F16 output is that value rounded to nearest even -- exactly the operand
+ * the quantised GEMMs feed the tensor cores. */
+MLORA_API int mlora_dequantize(int scheme, const void* codes, const void* scales,
+                               const void* zeros, int64_t N, int64_t K, int64_t group, void* out,
+                               int out_dtype, void* stream);
+
+/* Bytes of workspace mlora_qlora_forward / mlora_qlora_backward need. */
+MLORA_API size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                                     int scheme, int64_t group);
+MLORA_API size_t mlora_qlora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                                      int scheme, int64_t group);
+
+/* y[M,N] = x . deq(W)^T + (alpha/r)(x . a^T) . b^T over a quantised base weight
+ * (codes/scales/zeros as above; x, a, b, y BF16).  Replaces qlora_forward_nf4
+ * (kernels/lora_quantized.metal:97-164) and qlora_forward_int4 (:29-93);
+ * dequantisation happens inside the tensor-core main loop.  group (NF4 block
+ * size / INT group) must be 64, 128 or 256; K a multiple of 32 (4-bit) or 16
+ * (INT8).  saved_xa as for mlora_lora_forward. */
+MLORA_API int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void* scales,
+                                  const void* zeros, int64_t group, const void* a, const void* b,
+                                  void* y, void* saved_xa, int64_t M, int64_t K, int64_t N,
+                                  int64_t r, float alpha, int dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* Gradients through the quantised base (frozen, as in QLoRA): dx = dy . deq(W)
+ * + s (dy . b) . a (dequantised in the main loop; dx may be NULL), da, db as
+ * mlora_lora_backward_ex (flags: MLORA_BWD_ACCUMULATE). */
+MLORA_API int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* codes,
+                                   const void* scales, const void* zeros, int64_t group,
+                                   const void* a, const void* b, const void* saved_xa, void* dx,
+                                   float* da, float* db, int64_t M, int64_t K, int64_t N,
+                                   int64_t r, float alpha, float clip_value, int dtype, int flags,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- optimizer --------------------------------------------------------- */
 
 /* One AdamW step over a flat buffer of n parameters (reference:

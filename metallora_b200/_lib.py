@@ -23,6 +23,10 @@ MLORA_ERR_DEVICE = -5
 
 BWD_ACCUMULATE = 1
 
+QUANT_NF4 = 1
+QUANT_INT4 = 2
+QUANT_INT8 = 3
+
 DTYPE_BF16 = 0
 DTYPE_F16 = 1
 DTYPE_F32 = 2
@@ -57,6 +61,14 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_linear": (i32, [vp, vp, vp, i64, i64, i64, i32, vp, sz, vp]),
     "mlora_merge_workspace_bytes": (sz, [i64, i64, i64, i32]),
     "mlora_merge": (i32, [vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp]),
+    "mlora_quantize": (i32, [vp, i32, i64, i64, i32, i64, vp, vp, vp, vp]),
+    "mlora_dequantize": (i32, [i32, vp, vp, vp, i64, i64, i64, vp, i32, vp]),
+    "mlora_qlora_forward_workspace_bytes": (sz, [i64, i64, i64, i64, i32, i64]),
+    "mlora_qlora_backward_workspace_bytes": (sz, [i64, i64, i64, i64, i32, i64]),
+    "mlora_qlora_forward": (i32, [vp, i32, vp, vp, vp, i64, vp, vp, vp, vp, i64, i64, i64, i64,
+                                  f32, i32, vp, sz, vp]),
+    "mlora_qlora_backward": (i32, [vp, vp, i32, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, i64, i64,
+                                   i64, i64, f32, f32, i32, i32, vp, sz, vp]),
     "mlora_adamw_step": (i32, [vp, vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp]),
     "mlora_sgd_step": (i32, [vp, vp, i64, f32, i32, vp, vp]),
     "mlora_adam_state_step": (i32, [vp, f32, f32, vp]),

@@ -457,6 +457,141 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   return launch_wgrad(w, 2, s);
 }
 
+// Backward of the 16-bit LoRA linear (dense W0, or a quantised W0 described
+// by qdx): rank projections, dx GEMM, dA/dB weight gradients.
+int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* qdx,
+               const void* a, const void* b, const void* saved_xa, void* dx, float* da,
+               float* db, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+               float clip_value, bool accumulate, int dtype, void* workspace,
+               size_t workspace_bytes, cudaStream_t s) {
+  int rc;
+  const BwdPlan need = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr);
+  if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
+    return fail(MLORA_ERR_WORKSPACE, "backward workspace needs " + std::to_string(need.bytes) + " bytes");
+  const BwdPlan p = plan_backward(workspace, M, K, N, r, saved_xa == nullptr);
+  const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
+  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
+  const float scale = alpha / static_cast<float>(r);
+
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
+  if (e != cudaSuccess) return fail(MLORA_ERR_CUDA, std::string("memset: ") + cudaGetErrorString(e));
+
+  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection.
+  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s))) return rc;
+
+  RankArgs ra;
+  ra.x = dy;
+  ra.l = p.bt;
+  ra.M = M;
+  ra.K = N;
+  ra.r = p.R;
+  ra.R = p.R;
+  ra.ldx = N;
+  ra.ldl = N;
+  ra.scale = scale;
+  ra.out_rows = dx ? p.u_rows : nullptr;
+  ra.ld_rows = p.R64;
+  ra.out_t = p.u_t;
+  ra.ld_t = pad8(M);
+  ra.partials = p.rpartials;
+  ra.counters = p.counters;
+  ra.splits = rank_splits(M, N);
+  ra.elt = elt;
+  if (ra.splits > p.rsplits) ra.splits = p.rsplits;
+  if ((rc = launch_rank(ra, s))) return rc;
+
+  const void* xa_t = saved_xa;
+  if (xa_t == nullptr) {
+    RankArgs rt = ra;
+    rt.x = x;
+    rt.l = a;
+    rt.K = K;
+    rt.r = r;
+    rt.ldx = K;
+    rt.ldl = K;
+    rt.out_rows = nullptr;
+    rt.out_t = p.xa_t;
+    rt.counters = p.counters + tm;
+    rt.splits = rank_splits(M, K);
+    if (rt.splits > p.rsplits) rt.splits = p.rsplits;
+    if ((rc = launch_rank(rt, s))) return rc;
+    xa_t = p.xa_t;
+  }
+
+  if (dx != nullptr && qdx != nullptr) {
+    QGemmArgs q = *qdx;
+    q.w_mn_major = true;
+    q.x = dy;
+    q.x2 = p.u_rows;
+    q.up = a;
+    q.d = dx;
+    q.M = M;
+    q.N = K;
+    q.K = N;
+    q.R = p.R;
+    q.ldx = N;
+    q.ldx2 = p.R64;
+    q.ldd = K;
+    q.up_rows = r;
+    q.up_ld = K;
+    q.up_cols = K;
+    if ((rc = launch_qgemm(q, s))) return rc;
+  } else if (dx != nullptr) {
+    GemmArgs ga;
+    ga.x = dy;
+    ga.w = w0;
+    ga.x2 = p.u_rows;
+    ga.w2 = a;
+    ga.d = dx;
+    ga.M = M;
+    ga.N = K;  // output columns of dx
+    ga.K = N;  // reduction over out_features
+    ga.R = p.R;
+    ga.w2_rows = r;
+    ga.ldx = N;
+    ga.ldw = K;
+    ga.ldx2 = p.R64;
+    ga.ldw2 = K;
+    ga.ldd = K;
+    ga.w_mn_major = true;
+    ga.elt = elt;
+    ga.out_dtype = dtype;
+    if ((rc = launch_gemm(ga, s))) return rc;
+  }
+
+  WgradArgs w[2];
+  // db[n, j] = sum_m dy[m, n] * (s x A^T)[m, j]
+  w[0].big = dy;
+  w[0].st = xa_t;
+  w[0].ld_st = pad8(M);
+  w[0].M = M;
+  w[0].P = N;
+  w[0].r = r;
+  w[0].R = p.R;
+  w[0].ldb = N;
+  w[0].out = db;
+  w[0].ldo = r;
+  w[0].transposed = false;
+  w[0].accumulate = accumulate;
+  w[0].clip = clip_value;
+  w[0].partials = p.wpart_db;
+  w[0].counters = p.counters + 2 * tm;
+  w[0].splits = p.wsplits;
+  w[0].elt = elt;
+  // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
+  w[1] = w[0];
+  w[1].big = x;
+  w[1].st = p.u_t;
+  w[1].P = K;
+  w[1].ldb = K;
+  w[1].out = da;
+  w[1].ldo = K;
+  w[1].transposed = true;
+  w[1].partials = p.wpart_da;
+  w[1].counters = p.counters + 2 * tm + tn;
+  return launch_wgrad(w, 2, s);
+}
+
 // ---- plain linear and merge plans ----------------------------------------
 size_t linear_ws(int64_t M, int64_t K, int64_t N, int dtype) {
   if (dtype != MLORA_DTYPE_F32) return 0;
@@ -513,17 +648,26 @@ void set_error(const std::string& msg) { t_last_error = msg; }
 
 bool make_tmap_2d_16b(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                       uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, inner, outer,
+                      row_stride_elems * 2, box_inner, box_outer, true);
+}
+
+bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base,
+                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                  uint32_t box_outer, bool swizzle128) {
+  (void)esize;
   auto fn = encode_fn();
   if (fn == nullptr) {
     set_error("cuTensorMapEncodeTiled entry point unavailable");
     return false;
   }
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) +
@@ -695,114 +839,8 @@ int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const 
                              static_cast<const float*>(b), static_cast<float*>(dx), da, db, M, K,
                              N, r, alpha, clip_value, accumulate, workspace, workspace_bytes,
                              static_cast<cudaStream_t>(stream));
-  const BwdPlan need = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr);
-  if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
-    return fail(MLORA_ERR_WORKSPACE, "backward workspace needs " + std::to_string(need.bytes) + " bytes");
-  const BwdPlan p = plan_backward(workspace, M, K, N, r, saved_xa == nullptr);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
-  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
-  const float scale = alpha / static_cast<float>(r);
-
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
-  if (e != cudaSuccess) return fail(MLORA_ERR_CUDA, std::string("memset: ") + cudaGetErrorString(e));
-
-  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection.
-  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s))) return rc;
-
-  RankArgs ra;
-  ra.x = dy;
-  ra.l = p.bt;
-  ra.M = M;
-  ra.K = N;
-  ra.r = p.R;
-  ra.R = p.R;
-  ra.ldx = N;
-  ra.ldl = N;
-  ra.scale = scale;
-  ra.out_rows = dx ? p.u_rows : nullptr;
-  ra.ld_rows = p.R64;
-  ra.out_t = p.u_t;
-  ra.ld_t = pad8(M);
-  ra.partials = p.rpartials;
-  ra.counters = p.counters;
-  ra.splits = rank_splits(M, N);
-  ra.elt = elt;
-  if (ra.splits > p.rsplits) ra.splits = p.rsplits;
-  if ((rc = launch_rank(ra, s))) return rc;
-
-  const void* xa_t = saved_xa;
-  if (xa_t == nullptr) {
-    RankArgs rt = ra;
-    rt.x = x;
-    rt.l = a;
-    rt.K = K;
-    rt.r = r;
-    rt.ldx = K;
-    rt.ldl = K;
-    rt.out_rows = nullptr;
-    rt.out_t = p.xa_t;
-    rt.counters = p.counters + tm;
-    rt.splits = rank_splits(M, K);
-    if (rt.splits > p.rsplits) rt.splits = p.rsplits;
-    if ((rc = launch_rank(rt, s))) return rc;
-    xa_t = p.xa_t;
-  }
-
-  if (dx != nullptr) {
-    GemmArgs ga;
-    ga.x = dy;
-    ga.w = w0;
-    ga.x2 = p.u_rows;
-    ga.w2 = a;
-    ga.d = dx;
-    ga.M = M;
-    ga.N = K;  // output columns of dx
-    ga.K = N;  // reduction over out_features
-    ga.R = p.R;
-    ga.w2_rows = r;
-    ga.ldx = N;
-    ga.ldw = K;
-    ga.ldx2 = p.R64;
-    ga.ldw2 = K;
-    ga.ldd = K;
-    ga.w_mn_major = true;
-    ga.elt = elt;
-    ga.out_dtype = dtype;
-    if ((rc = launch_gemm(ga, s))) return rc;
-  }
-
-  WgradArgs w[2];
-  // db[n, j] = sum_m dy[m, n] * (s x A^T)[m, j]
-  w[0].big = dy;
-  w[0].st = xa_t;
-  w[0].ld_st = pad8(M);
-  w[0].M = M;
-  w[0].P = N;
-  w[0].r = r;
-  w[0].R = p.R;
-  w[0].ldb = N;
-  w[0].out = db;
-  w[0].ldo = r;
-  w[0].transposed = false;
-  w[0].accumulate = accumulate;
-  w[0].clip = clip_value;
-  w[0].partials = p.wpart_db;
-  w[0].counters = p.counters + 2 * tm;
-  w[0].splits = p.wsplits;
-  w[0].elt = elt;
-  // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
-  w[1] = w[0];
-  w[1].big = x;
-  w[1].st = p.u_t;
-  w[1].P = K;
-  w[1].ldb = K;
-  w[1].out = da;
-  w[1].ldo = K;
-  w[1].transposed = true;
-  w[1].partials = p.wpart_da;
-  w[1].counters = p.counters + 2 * tm + tn;
-  return launch_wgrad(w, 2, s);
+  return backward16(dy, x, w0, nullptr, a, b, saved_xa, dx, da, db, M, K, N, r, alpha, clip_value,
+                    accumulate, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 long long mlora_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
@@ -889,6 +927,186 @@ int mlora_grad_norm_clip(const float* grad, int64_t n, float max_norm, float* ou
   cudaError_t e = cudaMemsetAsync(counter, 0, 4, s);
   if (e != cudaSuccess) return cuda_fail(e, "memset");
   return launch_grad_norm(grad, n, max_norm, partials, counter, out, s);
+}
+
+// ---- quantised base weights ----------------------------------------------------
+
+namespace {
+int check_quant(int scheme, int64_t N, int64_t K, int64_t group) {
+  if (scheme != MLORA_QUANT_NF4 && scheme != MLORA_QUANT_INT4 && scheme != MLORA_QUANT_INT8)
+    return fail(MLORA_ERR_INVALID_ARG, "scheme must be NF4, INT4 or INT8");
+  if (N <= 0 || K <= 0 || group <= 0) return fail(MLORA_ERR_INVALID_ARG, "N, K, group must be positive");
+  if (scheme != MLORA_QUANT_INT8 && (K % 2))
+    return fail(MLORA_ERR_INVALID_ARG, "4-bit codes pack two per byte: K must be even");
+  return MLORA_OK;
+}
+}  // namespace
+
+int mlora_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int scheme, int64_t group,
+                   void* codes, void* scales, void* zeros, void* stream) {
+  int rc = check_quant(scheme, N, K, group);
+  if (rc) return rc;
+  if (!w || !codes || !scales || (scheme != MLORA_QUANT_NF4 && !zeros))
+    return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if (w_dtype < MLORA_DTYPE_BF16 || w_dtype > MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_INVALID_ARG, "weight dtype must be BF16, F16 or F32");
+  if ((rc = check_device())) return rc;
+  return launch_quantize(w, w_dtype, N, K, scheme, group, codes, scales, zeros,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int mlora_dequantize(int scheme, const void* codes, const void* scales, const void* zeros,
+                     int64_t N, int64_t K, int64_t group, void* out, int out_dtype, void* stream) {
+  int rc = check_quant(scheme, N, K, group);
+  if (rc) return rc;
+  if (!codes || !scales || !out || (scheme != MLORA_QUANT_NF4 && !zeros))
+    return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if (out_dtype < MLORA_DTYPE_BF16 || out_dtype > MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_INVALID_ARG, "out dtype must be BF16, F16 or F32");
+  if ((rc = check_device())) return rc;
+  return launch_dequantize(scheme, codes, scales, zeros, N, K, group, out, out_dtype,
+                           static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+int check_qlora(int scheme, int64_t M, int64_t K, int64_t N, int64_t r, int64_t group, int dtype) {
+  int rc = check_shapes(M, K, N, r, dtype);
+  if (rc) return rc;
+  if ((rc = check_quant(scheme, N, K, group))) return rc;
+  if (dtype != MLORA_DTYPE_BF16)
+    return fail(MLORA_ERR_UNSUPPORTED, "quantised-base paths take BF16 activations");
+  if (group != 64 && group != 128 && group != 256)
+    return fail(MLORA_ERR_UNSUPPORTED, "tensor-core quantised paths take group 64, 128 or 256");
+  if (scheme != MLORA_QUANT_INT8 ? (K % 32) : (K % 16))
+    return fail(MLORA_ERR_UNSUPPORTED, "code rows must be a multiple of 16 bytes (K % 32 for 4-bit)");
+  return MLORA_OK;
+}
+
+size_t qscales_bytes(int64_t N, int64_t K, int64_t group) {
+  return align_up(static_cast<size_t>((K + group - 1) / group) * N * 4, 256);
+}
+
+// Re-lays the per-row scales as [groups, N] (fp32 absmax, or (scale, zero) fp16 pairs).
+int prep_scales(int scheme, const void* scales, const void* zeros, int64_t N, int64_t K,
+                int64_t group, void* scales_t, cudaStream_t s) {
+  const int64_t G = (K + group - 1) / group;
+  if (scheme == MLORA_QUANT_NF4)
+    return launch_transpose_f32(static_cast<const float*>(scales), N, G,
+                                static_cast<float*>(scales_t), s);
+  return launch_pack_scale_zero(scales, zeros, N, G, scales_t, s);
+}
+}  // namespace
+
+size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme,
+                                           int64_t group) {
+  (void)scheme;
+  if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
+  return plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
+}
+
+int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void* scales,
+                        const void* zeros, int64_t group, const void* a, const void* b, void* y,
+                        void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                        int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_qlora(scheme, M, K, N, r, group, dtype);
+  if (rc) return rc;
+  if (!x || !codes || !scales || !a || !b || !y || (scheme != MLORA_QUANT_NF4 && !zeros))
+    return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({x, codes, scales, zeros, a, b, y, saved_xa, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  const size_t sbytes = qscales_bytes(N, K, group);
+  const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
+  if (workspace == nullptr || workspace_bytes < need.bytes + sbytes)
+    return fail(MLORA_ERR_WORKSPACE, "qlora forward workspace needs " +
+                                         std::to_string(need.bytes + sbytes) + " bytes");
+  const FwdPlan p = plan_forward(workspace, M, K, r, saved_xa == nullptr);
+  void* scales_t = static_cast<uint8_t*>(workspace) + p.bytes;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
+  RankArgs ra;
+  ra.x = x;
+  ra.l = a;
+  ra.M = M;
+  ra.K = K;
+  ra.r = r;
+  ra.R = p.R;
+  ra.ldx = K;
+  ra.ldl = K;
+  ra.scale = alpha / static_cast<float>(r);
+  ra.out_rows = p.xa_rows;
+  ra.ld_rows = p.R64;
+  ra.out_t = saved_xa ? saved_xa : p.xa_t;
+  ra.ld_t = pad8(M);
+  ra.partials = p.partials;
+  ra.counters = p.counters;
+  ra.splits = p.splits;
+  ra.elt = Elt::kBF16;
+  if ((rc = launch_rank(ra, s))) return rc;
+  QGemmArgs q;
+  q.scheme = scheme;
+  q.w_mn_major = false;
+  q.x = x;
+  q.x2 = p.xa_rows;
+  q.codes = codes;
+  q.scales_t = scales_t;
+  q.up = b;
+  q.d = y;
+  q.M = M;
+  q.N = N;
+  q.K = K;
+  q.R = p.R;
+  q.ldx = K;
+  q.ldx2 = p.R64;
+  q.ldd = N;
+  q.group = group;
+  q.up_rows = r;
+  q.up_ld = r;
+  q.up_cols = r;
+  return launch_qgemm(q, s);
+}
+
+size_t mlora_qlora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                            int scheme, int64_t group) {
+  (void)scheme;
+  if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
+  return plan_backward(nullptr, M, K, N, r, true).bytes + qscales_bytes(N, K, group);
+}
+
+int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* codes,
+                         const void* scales, const void* zeros, int64_t group, const void* a,
+                         const void* b, const void* saved_xa, void* dx, float* da, float* db,
+                         int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                         float clip_value, int dtype, int flags, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  int rc = check_qlora(scheme, M, K, N, r, group, dtype);
+  if (rc) return rc;
+  if (flags & ~MLORA_BWD_ACCUMULATE) return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
+  if (!dy || !x || !a || !b || !da || !db) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (dx && (!codes || !scales || (scheme != MLORA_QUANT_NF4 && !zeros)))
+    return fail(MLORA_ERR_INVALID_ARG, "dx needs the quantised weight");
+  if ((rc = check_ptrs16({dy, x, codes, scales, zeros, a, b, saved_xa, dx, da, db, workspace})))
+    return rc;
+  if ((rc = check_device())) return rc;
+  const size_t sbytes = qscales_bytes(N, K, group);
+  const size_t bytes = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr).bytes;
+  if (workspace == nullptr || workspace_bytes < bytes + sbytes)
+    return fail(MLORA_ERR_WORKSPACE, "qlora backward workspace needs " +
+                                         std::to_string(bytes + sbytes) + " bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  QGemmArgs q;
+  if (dx != nullptr) {
+    void* scales_t = static_cast<uint8_t*>(workspace) + bytes;
+    if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
+    q.scheme = scheme;
+    q.codes = codes;
+    q.scales_t = scales_t;
+    q.group = group;
+  }
+  return backward16(dy, x, nullptr, dx ? &q : nullptr, a, b, saved_xa, dx, da, db, M, K, N, r,
+                    alpha, clip_value, (flags & MLORA_BWD_ACCUMULATE) != 0, dtype, workspace,
+                    bytes, s);
 }
 
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {

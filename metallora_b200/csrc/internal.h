@@ -22,6 +22,10 @@ void set_error(const std::string& msg);
 // swizzle, zero fill out of bounds.  Returns false (with set_error) on failure.
 bool make_tmap_2d_16b(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                       uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
+// General 2-D tensor map (element type/size given; 128-byte swizzle or none).
+bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base,
+                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                  uint32_t box_outer, bool swizzle128);
 
 // ---- launch accounting / opt-in profiling ----------------------------------
 // Kernel kinds for mlora_profile_* (index into the per-kind totals).
@@ -77,6 +81,27 @@ struct GemmArgs {
   int out_dtype;   // MLORA_DTYPE_*
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
+
+// ------------------------------------------------------ quantised GEMM ------
+// D = X . deq(Wq)^T + X2 . up^T (forward, W K-major) or X . deq(Wq) + X2 . up
+// (backward dx, W MN-major).  Wq rows/cols are the weight's [out, in] axes; the
+// scales are pre-transposed to [groups, rows] (fp32 absmax or fp16 (scale,
+// zero) pairs).  x, x2, up, d are bf16.
+struct QGemmArgs {
+  int scheme = 0;
+  bool w_mn_major = false;
+  const void* x = nullptr;
+  const void* x2 = nullptr;
+  const void* codes = nullptr;
+  const void* scales_t = nullptr;
+  const void* up = nullptr;  // forward: B [N, r] ; backward: A [r, K]
+  void* d = nullptr;
+  int64_t M = 0, N = 0, K = 0, R = 0;  // GEMM sizes (N = output columns, K = reduction)
+  int64_t ldx = 0, ldx2 = 0, ldd = 0;
+  int64_t group = 64;
+  int64_t up_rows = 0, up_ld = 0, up_cols = 0;
+};
+int launch_qgemm(const QGemmArgs& a, cudaStream_t stream);
 
 // ------------------------------------------------------- rank projection -----
 // out[m, j] = scale * sum_k X[m, k] * L[j, k] for j < R (L rows >= r are zero).
@@ -141,6 +166,16 @@ int launch_split3_rows(const float* src, int64_t rows, int64_t cols, int64_t ld_
 int launch_split3_cols_t(const float* src, int64_t N, int64_t r, int64_t ld_src, void* dst,
                          int64_t R, int64_t seg, int64_t ld_dst, uint32_t pattern,
                          cudaStream_t stream);
+
+// ------------------------------------------------------------- quantisation --
+int launch_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int scheme, int64_t g,
+                    void* codes, void* scales, void* zeros, cudaStream_t s);
+int launch_dequantize(int scheme, const void* codes, const void* scales, const void* zeros,
+                      int64_t N, int64_t K, int64_t g, void* out, int out_dtype, cudaStream_t s);
+int launch_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
+                         cudaStream_t s);
+int launch_pack_scale_zero(const void* scales, const void* zeros, int64_t rows, int64_t cols,
+                           void* dst, cudaStream_t s);
 
 // ---------------------------------------------------------------- optimizer --
 int norm_grid();

@@ -287,3 +287,73 @@ def grad_norm_clip(grad: torch.Tensor, max_norm: float, out: torch.Tensor | None
                                   ws.numel(), _stream())
     _lib.check(st, "mlora_grad_norm_clip")
     return out
+
+
+# --------------------------------------------------------- quantised bases --
+
+def qlora_linear_fwd(x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor, alpha: float,
+                     save_xa: bool = False):
+    """y = x.deq(W)^T + (alpha/r).(x.A^T).B^T for a quantised base ``qw``
+    (metallora_b200.quant.QuantizedWeight); x, A, B bf16."""
+    _need_cuda(x2d, a, b)
+    if x2d.dtype != torch.bfloat16:
+        raise ShapeError("quantised-base LoRA takes bf16 activations")
+    M, K = x2d.shape
+    N = qw.shape[0]
+    if qw.shape[1] != K:
+        raise ShapeError(f"x has {K} features, the quantised weight {qw.shape[1]}")
+    a, b, alpha, r = _pad_rank(a, b, alpha)
+    _check_2d("A", a, (r, K), torch.bfloat16)
+    _check_2d("B", b, (N, r), torch.bfloat16)
+    x2d, a, b = x2d.contiguous(), a.contiguous(), b.contiguous()
+    lib = _lib.load()
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x2d.device)
+    saved = (torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=torch.bfloat16,
+                         device=x2d.device) if save_xa else None)
+    ws = _workspace(lib.mlora_qlora_forward_workspace_bytes(M, K, N, r, qw.code, qw.group),
+                    x2d.device)
+    st = lib.mlora_qlora_forward(_ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
+                                 _ptr(qw.zeros), qw.group, _ptr(a), _ptr(b), _ptr(y), _ptr(saved),
+                                 M, K, N, r, float(alpha), _lib.DTYPE_BF16, _ptr(ws), ws.numel(),
+                                 _stream())
+    _lib.check(st, "mlora_qlora_forward")
+    return y, saved
+
+
+def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor,
+                     alpha: float, saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
+                     need_dx: bool = True, da_out: torch.Tensor | None = None,
+                     db_out: torch.Tensor | None = None):
+    """(dx, dA, dB) through a frozen quantised base (dx dequantises in the main loop)."""
+    _need_cuda(dy2d, x2d, a, b)
+    M, K = x2d.shape
+    N = dy2d.shape[1]
+    r_orig = a.shape[0]
+    a_p, b_p, alpha_p, r = _pad_rank(a, b, alpha)
+    _check_2d("grad_output", dy2d, (M, N), torch.bfloat16)
+    _check_2d("A", a_p, (r, K), torch.bfloat16)
+    _check_2d("B", b_p, (N, r), torch.bfloat16)
+    dy2d, x2d, a_p, b_p = (t.contiguous() for t in (dy2d, x2d, a_p, b_p))
+    lib = _lib.load()
+    dx = torch.empty((M, K), dtype=torch.bfloat16, device=x2d.device) if need_dx else None
+    flags = 0
+    if da_out is not None or db_out is not None:
+        if r != r_orig:
+            raise ShapeError("gradient accumulation buffers need a rank that is a multiple of 8")
+        da, db, flags = da_out, db_out, _lib.BWD_ACCUMULATE
+    else:
+        da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
+        db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
+    ws = _workspace(lib.mlora_qlora_backward_workspace_bytes(M, K, N, r, qw.code, qw.group),
+                    x2d.device)
+    st = lib.mlora_qlora_backward(_ptr(dy2d), _ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
+                                  _ptr(qw.zeros), qw.group, _ptr(a_p), _ptr(b_p), _ptr(saved_xa),
+                                  _ptr(dx), _ptr(da), _ptr(db), M, K, N, r, float(alpha_p),
+                                  float(clip_value), _lib.DTYPE_BF16, flags, _ptr(ws), ws.numel(),
+                                  _stream())
+    _lib.check(st, "mlora_qlora_backward")
+    if flags:
+        return dx, da, db
+    if r != r_orig:
+        da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
+    return dx, da, db

@@ -16,7 +16,7 @@ from torch import nn
 from . import kernels as _k
 from .exceptions import ConfigurationError, validate_alpha, validate_probability, validate_rank
 from .logging import logger
-from .ops import lora_forward, merge_lora_weights
+from .ops import lora_forward, merge_lora_weights, qlora_forward
 
 
 class LoRALinear(nn.Module):
@@ -63,6 +63,7 @@ class LoRALinear(nn.Module):
         # (A, B) in the compute dtype, and (gA, gB) fp32 gradient sinks.
         self._compute_ab = None
         self._grad_sink = None
+        self.qweight = None  # quantised base (quantize_base); W0 is then dropped
         logger.debug(f"LoRALinear: {in_features}→{out_features}, rank={rank}")
 
     @property
@@ -71,7 +72,10 @@ class LoRALinear(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """layers.py:83-106: any leading shape; the bias is added after the op."""
-        if self.merged:
+        if self.qweight is not None:
+            out = qlora_forward(x, self.qweight, self.A, self.B, alpha=self.alpha,
+                                _compute=self._compute_ab, _sink=self._grad_sink)
+        elif self.merged:
             out = _k.linear(x.reshape(-1, x.shape[-1]), self.W0).reshape(*x.shape[:-1],
                                                                          self.out_features)
         else:
@@ -113,6 +117,19 @@ class LoRALinear(nn.Module):
                 lora.bias.copy_(linear.bias)
         return lora
 
+    @torch.no_grad()
+    def quantize_base(self, scheme: str = "nf4", group: int | None = None) -> "LoRALinear":
+        """Replaces the frozen base W0 by its quantised form (QLoRA): NF4 with
+        per-block absmax, or group-wise INT4/INT8 (the formats of
+        kernels/lora_quantized.metal).  The dense W0 is released."""
+        from .quant import quantize
+        if self.merged:
+            raise ConfigurationError("quantize_base needs an unmerged layer")
+        self.qweight = quantize(self.W0.detach(), scheme, group)
+        self.W0 = nn.Parameter(torch.empty(0, device=self.W0.device, dtype=self.W0.dtype),
+                               requires_grad=False)
+        return self
+
     def trainable_parameters(self) -> dict:
         """layers.py:141-146: A and B (plus bias if the base is not frozen)."""
         params = {"A": self.A, "B": self.B}
@@ -127,7 +144,8 @@ class LoRALinear(nn.Module):
         return count
 
     def num_total_params(self) -> int:
-        count = self.W0.numel() + self.A.numel() + self.B.numel()
+        base = self.in_features * self.out_features if self.qweight is not None else self.W0.numel()
+        count = base + self.A.numel() + self.B.numel()
         if self.bias is not None:
             count += self.bias.numel()
         return count

@@ -57,6 +57,45 @@ class _LoRALinearFn(torch.autograd.Function):
         return dx, dw0, da, db, None, None, None
 
 
+class _QLoRALinearFn(torch.autograd.Function):
+    """The LoRA linear over a frozen quantised base (QLoRA): no gradient for
+    the base; A/B handled as in _LoRALinearFn."""
+
+    @staticmethod
+    def forward(ctx, x2d, a, b, qw, alpha, compute, sink):
+        a_c, b_c = compute if compute is not None else (a.to(x2d.dtype), b.to(x2d.dtype))
+        y, saved = _k.qlora_linear_fwd(x2d, qw, a_c, b_c, alpha, save_xa=True)
+        ctx.save_for_backward(x2d, a_c, b_c, saved)
+        ctx.qw, ctx.alpha, ctx.sink = qw, alpha, sink
+        ctx.ab_dtypes = (a.dtype, b.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, a_c, b_c, saved = ctx.saved_tensors
+        sink = ctx.sink
+        need_dx = ctx.needs_input_grad[0]
+        dx, da, db = _k.qlora_linear_bwd(dy.contiguous(), x2d, ctx.qw, a_c, b_c, ctx.alpha, saved,
+                                         0.0, need_dx=need_dx,
+                                         da_out=sink[0] if sink else None,
+                                         db_out=sink[1] if sink else None)
+        if sink is not None:
+            return dx, None, None, None, None, None, None
+        da = da.to(ctx.ab_dtypes[0]) if ctx.needs_input_grad[1] else None
+        db = db.to(ctx.ab_dtypes[1]) if ctx.needs_input_grad[2] else None
+        return dx, da, db, None, None, None, None
+
+
+def qlora_forward(x, qweight, A, B, alpha: float = 16.0, _compute=None, _sink=None):  # noqa: N803
+    """LoRA forward over a quantised base (``quant.QuantizedWeight``):
+    ``x.deq(W)^T + (alpha/rank).(x.A^T).B^T`` with the dequantisation fused
+    into the GEMM (replaces qlora_forward_nf4/int4, lora_quantized.metal:29-164)."""
+    shp = x.shape
+    out = _QLoRALinearFn.apply(x.reshape(-1, shp[-1]), A, B, qweight, float(alpha), _compute,
+                               _sink)
+    return out.reshape(*shp[:-1], qweight.shape[0])
+
+
 def _apply(x2d, W0, A, B, alpha, compute=None, sink=None):
     return _LoRALinearFn.apply(x2d, W0, A, B, float(alpha), compute, sink)
 

@@ -1,0 +1,104 @@
+"""Quantised base weights (NF4, group-wise INT4/INT8) for QLoRA.
+
+Storage follows the reference shaders' layout (kernels/lora_quantized.metal):
+packed codes ``[N, K/2]`` bytes with the low nibble holding the even k
+(:70-74) -- ``[N, K]`` for INT8 -- and per-row, per-block scales:
+fp32 absmax ``[N, ceil(K/group)]`` for NF4 (:122, :135), fp16 scale and zero
+``[N, ceil(K/group)]`` for INT4/INT8 (the reference's per-row int4 is
+``group = K``).  ``quantize`` runs on the GPU (the reference ships no
+quantiser); ``dequantize`` returns fp32 values bit-identical to the
+reference's ``dequant_nf4``/``dequant_int4``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .exceptions import QuantizationError, ShapeError
+from .kernels import _dtype_code, _need_cuda, _ptr, _stream
+
+SCHEMES = {"nf4": _lib.QUANT_NF4, "int4": _lib.QUANT_INT4, "int8": _lib.QUANT_INT8}
+DEFAULT_GROUP = {"nf4": 64, "int4": 128, "int8": 128}
+
+
+@dataclass
+class QuantizedWeight:
+    """A quantised [out_features, in_features] weight."""
+    scheme: str
+    codes: torch.Tensor
+    scales: torch.Tensor
+    zeros: torch.Tensor | None
+    group: int
+    shape: tuple[int, int]
+
+    @property
+    def code(self) -> int:
+        return SCHEMES[self.scheme]
+
+    @property
+    def device(self):
+        return self.codes.device
+
+    def nbytes(self) -> int:
+        n = self.codes.numel() + self.scales.numel() * self.scales.element_size()
+        if self.zeros is not None:
+            n += self.zeros.numel() * self.zeros.element_size()
+        return n
+
+    def dequantize(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        return dequantize(self, dtype)
+
+    def state_dict(self) -> dict[str, torch.Tensor]:
+        d = {"codes": self.codes, "scales": self.scales}
+        if self.zeros is not None:
+            d["zeros"] = self.zeros
+        return d
+
+
+def quantize(w: torch.Tensor, scheme: str = "nf4", group: int | None = None) -> QuantizedWeight:
+    """Quantises a 2-D CUDA weight [N, K] (bf16/fp16/fp32)."""
+    if scheme not in SCHEMES:
+        raise QuantizationError(f"unknown scheme {scheme!r}; use one of {sorted(SCHEMES)}")
+    _need_cuda(w)
+    if w.dim() != 2:
+        raise ShapeError("quantize takes a 2-D weight [out_features, in_features]")
+    group = group or DEFAULT_GROUP[scheme]
+    N, K = w.shape
+    if scheme != "int8" and K % 2:
+        raise QuantizationError("4-bit codes pack two per byte: in_features must be even")
+    G = -(-K // group)
+    w = w.contiguous()
+    dev = w.device
+    codes = torch.empty((N, K if scheme == "int8" else K // 2), dtype=torch.uint8, device=dev)
+    if scheme == "nf4":
+        scales = torch.empty((N, G), dtype=torch.float32, device=dev)
+        zeros = None
+    else:
+        scales = torch.empty((N, G), dtype=torch.float16, device=dev)
+        zeros = torch.empty((N, G), dtype=torch.float16, device=dev)
+    st = _lib.load().mlora_quantize(_ptr(w), _dtype_code(w), N, K, SCHEMES[scheme], group,
+                                    _ptr(codes), _ptr(scales), _ptr(zeros), _stream())
+    _lib.check(st, "mlora_quantize")
+    return QuantizedWeight(scheme, codes, scales, zeros, group, (N, K))
+
+
+def dequantize(qw: QuantizedWeight, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Dense [N, K] weights: fp32 = the reference's dequantised values (bit
+    exact); bf16/fp16 = those values rounded, the operand the GEMMs use."""
+    N, K = qw.shape
+    out = torch.empty((N, K), dtype=dtype, device=qw.device)
+    st = _lib.load().mlora_dequantize(qw.code, _ptr(qw.codes), _ptr(qw.scales), _ptr(qw.zeros), N,
+                                      K, qw.group, _ptr(out), _dtype_code(out), _stream())
+    _lib.check(st, "mlora_dequantize")
+    return out
+
+
+def from_reference_layout(scheme: str, codes, scales, zeros, shape, group) -> QuantizedWeight:
+    """Wraps tensors already in the reference layout (e.g. loaded from disk)."""
+    if scheme not in SCHEMES:
+        raise QuantizationError(f"unknown scheme {scheme!r}")
+    return QuantizedWeight(scheme, codes.contiguous(), scales.contiguous(),
+                           None if zeros is None else zeros.contiguous(), int(group),
+                           (int(shape[0]), int(shape[1])))
