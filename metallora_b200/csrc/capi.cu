@@ -3,6 +3,7 @@
 // include/metallora_b200.h for the contract of each entry point.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <initializer_list>
 #include <mutex>
@@ -280,6 +281,67 @@ int check_ptrs16(std::initializer_list<const void*> ptrs) {
   for (const void* q : ptrs)
     if (q && !aligned16(q)) return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
   return MLORA_OK;
+}
+
+// ---- decode plan (M <= 16, bf16, K % 32 == 0) ------------------------------
+struct GemvPlan {
+  int splits;
+  uint32_t* counters;
+  size_t counter_bytes;
+  float* st;
+  float* partials;
+  size_t bytes;
+};
+
+bool use_gemv(int64_t M, int64_t K, int dtype) {
+  return M <= kGemvMaxTokens && K % 32 == 0 && dtype == MLORA_DTYPE_BF16;
+}
+
+GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r) {
+  GemvPlan p;
+  p.splits = gemv_splits(N, K);
+  Carve c(ws);
+  p.counter_bytes = static_cast<size_t>(gemv_row_blocks(N)) * 4;
+  p.counters = static_cast<uint32_t*>(c.take(p.counter_bytes));
+  p.st = static_cast<float*>(
+      c.take(static_cast<size_t>(rank_small_splits(K)) * M * (r > 0 ? r : 1) * 4));
+  p.partials = static_cast<float*>(c.take(static_cast<size_t>(p.splits) * M * N * 4));
+  p.bytes = align_up(c.off, 256);
+  return p;
+}
+
+// Decode-size forward: counters, sT = s.x.A^T (if a), split-K GEMV + rank term.
+int run_gemv(int scheme, const void* x, const void* w, const void* scales, const void* zeros,
+             int64_t group, const void* a, const void* b, void* y, int64_t M, int64_t K,
+             int64_t N, int64_t r, float alpha, void* workspace, size_t workspace_bytes,
+             cudaStream_t s) {
+  const GemvPlan need = plan_gemv(nullptr, M, K, N, r);
+  if (workspace == nullptr || workspace_bytes < need.bytes)
+    return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
+  const GemvPlan p = plan_gemv(workspace, M, K, N, r);
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  int rc;
+  if (a != nullptr && (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, s)))
+    return rc;
+  GemvArgs g;
+  g.scheme = scheme;
+  g.x = x;
+  g.w = w;
+  g.scales = scales;
+  g.zeros = zeros;
+  g.b = a != nullptr ? b : nullptr;
+  g.st = p.st;
+  g.y = y;
+  g.partials = p.partials;
+  g.counters = p.counters;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.r = r;
+  g.group = group;
+  g.splits = p.splits;
+  return launch_gemv(g, s);
 }
 
 int lora_forward_f32(const float* x, const float* w0, const float* a, const float* b, float* y,
@@ -594,6 +656,7 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
 
 // ---- plain linear and merge plans ----------------------------------------
 size_t linear_ws(int64_t M, int64_t K, int64_t N, int dtype) {
+  if (use_gemv(M, K, dtype)) return plan_gemv(nullptr, M, K, N, 0).bytes;
   if (dtype != MLORA_DTYPE_F32) return 0;
   return plan_forward_f32(nullptr, M, K, N, 1, false).bytes;
 }
@@ -730,7 +793,9 @@ int mlora_device_status(uint32_t* out, int reset) {
 size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype) {
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0) return 0;
   if (dtype == MLORA_DTYPE_F32) return plan_forward_f32(nullptr, M, K, N, r, true).bytes;
-  return plan_forward(nullptr, M, K, r, true).bytes;
+  size_t bytes = plan_forward(nullptr, M, K, r, true).bytes;
+  if (use_gemv(M, K, dtype)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r).bytes);
+  return bytes;
 }
 
 int mlora_lora_forward(const void* x, const void* w0, const void* a, const void* b, void* y,
@@ -750,6 +815,9 @@ int mlora_lora_forward(const void* x, const void* w0, const void* a, const void*
                             static_cast<float*>(y), M, K, N, r, alpha, workspace, workspace_bytes,
                             static_cast<cudaStream_t>(stream));
   }
+  if (saved_xa == nullptr && use_gemv(M, K, dtype))
+    return run_gemv(0, x, w0, nullptr, nullptr, 64, a, b, y, M, K, N, r, alpha, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
   const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
     return fail(MLORA_ERR_WORKSPACE, "forward workspace needs " + std::to_string(need.bytes) + " bytes");
@@ -1001,7 +1069,9 @@ size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int6
                                            int64_t group) {
   (void)scheme;
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
-  return plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
+  size_t bytes = plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
+  if (use_gemv(M, K, MLORA_DTYPE_BF16)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r).bytes);
+  return bytes;
 }
 
 int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void* scales,
@@ -1014,6 +1084,9 @@ int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void
     return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
   if ((rc = check_ptrs16({x, codes, scales, zeros, a, b, y, saved_xa, workspace}))) return rc;
   if ((rc = check_device())) return rc;
+  if (saved_xa == nullptr && use_gemv(M, K, dtype))
+    return run_gemv(scheme, x, codes, scales, zeros, group, a, b, y, M, K, N, r, alpha, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
   const size_t sbytes = qscales_bytes(N, K, group);
   const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes + sbytes)
@@ -1122,6 +1195,9 @@ int mlora_linear(const void* x, const void* w, void* y, int64_t M, int64_t K, in
   if ((rc = check_ptrs16({x, w, y, workspace}))) return rc;
   if ((rc = check_device())) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (use_gemv(M, K, dtype))
+    return run_gemv(0, x, w, nullptr, nullptr, 64, nullptr, nullptr, y, M, K, N, 0, 1.f, workspace,
+                    workspace_bytes, s);
   if (dtype == MLORA_DTYPE_F32)
     return lora_forward_f32(static_cast<const float*>(x), static_cast<const float*>(w), nullptr,
                             nullptr, static_cast<float*>(y), M, K, N, 1, 1.f, workspace,

@@ -103,6 +103,31 @@ struct QGemmArgs {
 };
 int launch_qgemm(const QGemmArgs& a, cudaStream_t stream);
 
+// ----------------------------------------------------------- decode (M <= 16) --
+// y = x . deq(W)^T (+ B . sT^T) for at most 16 tokens; scheme 0 = dense bf16.
+struct GemvArgs {
+  int scheme = 0;
+  const void* x = nullptr;       // bf16 [M, K]
+  const void* w = nullptr;       // codes or bf16 weights, rows of the [N, K] weight
+  const void* scales = nullptr;  // reference layout [N, G]
+  const void* zeros = nullptr;
+  const void* b = nullptr;       // bf16 [N, r] or nullptr
+  const float* st = nullptr;     // fp32 [rank_small_splits(K), M, r] partials of s.x.A^T
+  void* y = nullptr;             // bf16 [M, N]
+  float* partials = nullptr;     // [splits, M, N]
+  uint32_t* counters = nullptr;  // [gemv_row_blocks(N)] zeroed
+  int64_t M = 0, N = 0, K = 0, r = 0, group = 64;
+  int splits = 1;
+};
+constexpr int64_t kGemvMaxTokens = 16;
+int gemv_splits(int64_t N, int64_t K);
+int64_t gemv_row_blocks(int64_t N);
+int64_t gemv_k_per_split(int64_t K, int splits);
+int launch_gemv(const GemvArgs& a, cudaStream_t s);
+int rank_small_splits(int64_t K);
+int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
+                      float* st, cudaStream_t s);
+
 // ------------------------------------------------------- rank projection -----
 // out[m, j] = scale * sum_k X[m, k] * L[j, k] for j < R (L rows >= r are zero).
 // Writes rows [M, ld_rows] (columns [R, ld_rows) zeroed) and/or the transpose

@@ -90,6 +90,23 @@ def test_forward_ragged_out_features(cuda, dtype, shape):
     assert status_ok()
 
 
+@pytest.mark.parametrize("M", [1, 3, 8, 16])
+@pytest.mark.parametrize("shape", [(4096, 4096, 16), (4096, 11008, 64), (11008, 4096, 16),
+                                   (512, 1000, 8)])
+def test_decode_sizes(cuda, M, shape):
+    """M <= 16 tokens (bf16) run the split-K decode kernel: forward with the
+    rank term, and the plain merged-weight linear."""
+    from metallora_b200 import kernels as K
+    Kd, N, r = shape
+    (x, W, A, B, _), (xh, Wh, Ah, Bh, _) = make(M, Kd, N, r, torch.bfloat16, cuda, seed=12)
+    y, _ = K.lora_linear_fwd(x, W, A, B, 32.0)
+    yl = K.linear(x, W)
+    torch.cuda.synchronize()
+    assert_close(y, lo.lora_forward(xh, Wh, Ah, Bh, 32.0, np.float64), 2e-2)
+    assert_close(yl, xh.astype(np.float64) @ Wh.astype(np.float64).T, 2e-2)
+    assert status_ok()
+
+
 def test_saved_intermediate_matches_recompute(cuda):
     from metallora_b200 import kernels as K
     (x, W, A, B, dy), _ = make(200, 256, 256, 16, torch.bfloat16, cuda, seed=4)

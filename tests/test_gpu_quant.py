@@ -81,14 +81,20 @@ def test_qlora_forward_backward(cuda, scheme, group, shape):
     A = ((torch.rand(r, Kd, generator=g) * 2 - 1) / Kd ** 0.5).to(torch.bfloat16).to(cuda)
     B = (torch.randn(N, r, generator=g) * 0.1).to(torch.bfloat16).to(cuda)
     dy = torch.randn(M, N, generator=g).to(torch.bfloat16).to(cuda)
-    y, saved = K.qlora_linear_fwd(x, qw, A, B, 32.0, save_xa=True)
     Wb = quant.dequantize(qw, torch.bfloat16)
-    y_dense, _ = K.lora_linear_fwd(x, Wb, A, B, 32.0)
-    torch.cuda.synchronize()
-    assert torch.equal(y, y_dense)  # the fused dequant feeds exactly bf16(deq(W))
     h = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
     Wf = quant.dequantize(qw, torch.float32).cpu().numpy()
-    assert rel_err(h(y), lo.lora_forward(h(x), Wf, h(A), h(B), 32.0, np.float64)) < 2e-2
+    ref = lo.lora_forward(h(x), Wf, h(A), h(B), 32.0, np.float64)
+    # both kernel families (decode path without a saved intermediate for M <= 16,
+    # tensor-core path when the intermediate is saved): the fused dequant feeds
+    # exactly bf16(deq(W)), so each equals the dense kernel on that weight
+    y_fast, _ = K.qlora_linear_fwd(x, qw, A, B, 32.0)
+    y, saved = K.qlora_linear_fwd(x, qw, A, B, 32.0, save_xa=True)
+    y_dense_fast, _ = K.lora_linear_fwd(x, Wb, A, B, 32.0)
+    y_dense, _ = K.lora_linear_fwd(x, Wb, A, B, 32.0, save_xa=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_dense) and torch.equal(y_fast, y_dense_fast)
+    assert rel_err(h(y), ref) < 2e-2 and rel_err(h(y_fast), ref) < 2e-2
     dx, da, db = K.qlora_linear_bwd(dy, x, qw, A, B, 32.0, saved, 0.0, True)
     dxd, dad, dbd = K.lora_linear_bwd(dy, x, Wb, A, B, 32.0, saved, 0.0, True)
     torch.cuda.synchronize()
