@@ -13,6 +13,22 @@ uniform draws with the reference configuration's distributions); they total
 ``--impl reference`` times the reference's CPU path instead: the numpy
 restatement of its pure-MLX op sequence (oracle/lora_oracle.py) on the host
 cores, on bounded token samples of the same workload.
+
+Other configurations of the same path (one JSON line per case):
+
+    --workload stack   32 Llama-7B-shaped layers of projections (q,k,v,o 4096->4096,
+                       gate,up 4096->11008, down 11008->4096), NF4 bases, rank 16,
+                       one training step (fwd + bwd + clip + AdamW on A/B) over
+                       8 x 4096 tokens, MSE to an N(0,1) target; tokens shard
+                       across GPUs (strong scaling), LoRA grads all-reduced.
+                       Per layer (n = per-token RMS norm, no weight):
+                       a = (q(n(h))+k(n(h))+v(n(h)))/sqrt3; h = h + o(a);
+                       h = h + down(gate(n(h))*up(n(h))).
+    --workload nf4     NF4 11008x4096 base (block 64), rank 64, alpha 128:
+                       forward and backward at 1, 16, 512, 4096 tokens.
+    --workload int     INT4/INT8 group-128 bases, 4096->4096 and 4096->14336,
+                       rank 16: forward unmerged and merged, 1..4096 tokens.
+    --workload fp32    fp32 forward 4096->4096, rank 16, 2048 tokens, and merged.
 """
 from __future__ import annotations
 
@@ -346,6 +362,245 @@ def run_e2e(args, layer, M, K, N, dev, world):
             "path": "LoRALinear forward+backward, pinned host buffers, copies overlapped"}
 
 
+# ------------------------------------------------------------ stack (cfg4) --
+
+STACK = {"workload": "llama7b_proj_stack_nf4_train_step", "layers": 32, "hidden": 4096,
+         "intermediate": 11008, "rank": 16, "alpha": 32.0, "tokens": 32768, "quant": "nf4",
+         "group": 64}
+
+
+def stack_flops_per_token():
+    h, i, r, L = STACK["hidden"], STACK["intermediate"], STACK["rank"], STACK["layers"]
+
+    def lin(K, N):
+        return flops_per_token(K, N, r)
+    return L * (4 * lin(h, h) + 2 * lin(h, i) + lin(i, h))
+
+
+def build_stack(dev, seed=0):
+    import torch
+    from torch import nn
+
+    from metallora_b200.layers import LoRALinear
+    h, i, r, a = STACK["hidden"], STACK["intermediate"], STACK["rank"], STACK["alpha"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def proj(K, N):
+        lin = LoRALinear(K, N, rank=r, alpha=a, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            lin.W0.copy_(torch.randn(N, K, device=dev, generator=g) / K ** 0.5)
+            lin.B.copy_(torch.randn(N, r, device=dev, generator=g) * 0.02 ** 0.5)
+        return lin.quantize_base(STACK["quant"], STACK["group"])
+
+    class Layer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q_proj, self.k_proj, self.v_proj, self.o_proj = (proj(h, h) for _ in range(4))
+            self.gate_proj, self.up_proj = proj(h, i), proj(h, i)
+            self.down_proj = proj(i, h)
+
+        def forward(self, x):
+            # Llama-style pre-norm (per-token RMS, no weight): gate*up is quadratic
+            # in its input, so without it the residual stream overflows bf16
+            # within a few layers
+            n = nn.functional.rms_norm(x, (h,), eps=1e-6)
+            a_ = (self.q_proj(n) + self.k_proj(n) + self.v_proj(n)) * (1.0 / 3 ** 0.5)
+            x = x + self.o_proj(a_)
+            n = nn.functional.rms_norm(x, (h,), eps=1e-6)
+            return x + self.down_proj(self.gate_proj(n) * self.up_proj(n))
+
+    class Stack(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.layers = nn.ModuleList(Layer() for _ in range(STACK["layers"]))
+
+        def forward(self, x):
+            for layer in self.layers:
+                x = layer(x)
+            return x
+
+    return Stack()
+
+
+def run_stack(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from metallora_b200 import _lib
+    from metallora_b200.distributed import shard_bounds
+    from metallora_b200.trainer import LoRATrainer, TrainingConfig
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    model = build_stack(dev)
+    cfg = TrainingConfig(rank=STACK["rank"], alpha=STACK["alpha"], learning_rate=1e-4,
+                         output_dir="/tmp/mlora_bench_out", log_interval=10 ** 9,
+                         save_interval=10 ** 9)
+    tr = LoRATrainer(model, cfg)
+    b, e = shard_bounds(STACK["tokens"], rank, world)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    x = torch.randn(1, e - b, STACK["hidden"], device=dev, generator=g).to(torch.bfloat16)
+    tgt = torch.randn(1, e - b, STACK["hidden"], device=dev, generator=g).to(torch.bfloat16)
+    batch = {"input_ids": x, "target_output": tgt}
+    for _ in range(args.warmup):
+        tr._training_step(batch)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    _lib.profile_read(reset=True)
+    _lib.profile_enable(True)
+    launches0 = _lib.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ev0.record()
+    losses = []
+    for _ in range(args.steps):
+        losses.append(tr._training_step(batch)["loss"])
+    ev1.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    if world > 1:
+        dist.barrier()
+    launches = _lib.launch_count() - launches0
+    _lib.profile_enable(False)
+    prof = _lib.profile_read(reset=True)
+    sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = STACK["tokens"] * args.steps
+    value = tokens / (ms / 1e3)
+    tflops = stack_flops_per_token() * value / 1e12
+    peaks = load_peaks()
+    g_ms, g_n = prof["gemm"]
+    line = {
+        "metric": "LoRA projection-stack training step tokens/s (NF4 bases, bf16)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {**STACK, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)"},
+        "tflops": round(tflops, 1),
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1),
+                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops_sustained"], 4),
+                     "peak_source": f"{peaks['source']} bf16_tflops_sustained"},
+        "kernels": {k: {"ms_total": round(v[0], 2), "launches": v[1]} for k, v in prof.items() if v[1]},
+        "gemm_share": round(g_ms / max(1e-9, sum(v[0] for v in prof.values())), 3),
+        "gpu_launches": launches, "loss_first_last": [losses[0], losses[-1]],
+        "clocks": sampler.summary(t0, t1),
+        "mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------ config sweeps ----
+
+def graph_ms(fn, reps=20, inner=5):
+    """Mean device time of fn() replayed from a CUDA graph (launch overhead hidden)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(inner):
+            fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps / inner
+
+
+def run_sweep(args):
+    import torch
+
+    from metallora_b200 import kernels as K
+    from metallora_b200 import quant
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = load_peaks()
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def lora_bytes(qw, W, A, B, M, Kd, N):
+        wb = qw.nbytes() if qw is not None else W.numel() * 2
+        return wb + (A.numel() + B.numel()) * 2 + 2 * M * (Kd + N)
+
+    def emit(d):
+        print(json.dumps(d), flush=True)
+
+    if args.workload == "fp32":
+        M, Kd, N, r = 2048, 4096, 4096, 16
+        x = torch.randn(M, Kd, device=dev, generator=gen)
+        W = torch.randn(N, Kd, device=dev, generator=gen) / 64
+        A = (torch.rand(r, Kd, device=dev, generator=gen) * 2 - 1) / 64
+        B = torch.randn(N, r, device=dev, generator=gen) * 0.02 ** 0.5
+        t = graph_ms(lambda: K.lora_linear_fwd(x, W, A, B, 32.0))
+        Wm = K.merge(W, A, B, 32.0)
+        tm = graph_ms(lambda: K.linear(x, Wm))
+        y, _ = K.lora_linear_fwd(x, W, A, B, 32.0)
+        ref = x.double() @ W.double().t() + 2.0 * (x.double() @ A.double().t()) @ B.double().t()
+        rel = float((y.double() - ref).norm() / ref.norm())
+        fl = 2.0 * M * (Kd * N + Kd * r + r * N)
+        emit({"workload": "fp32_fwd_4096x4096_r16_2048tok", "ms": round(t, 4),
+              "tflops": round(fl / t / 1e9, 1), "merged_ms": round(tm, 4),
+              "rel_err_vs_fp64": rel, "tokens_per_s": round(M / t * 1e3, 1)})
+        return
+    if args.workload == "nf4":
+        cases = [("nf4", 64, 4096, 11008, 64, 128.0, M) for M in (1, 16, 512, 4096)]
+    else:
+        cases = [(s, 128, 4096, N, 16, 32.0, M) for s in ("int4", "int8") for N in (4096, 14336)
+                 for M in (1, 16, 128, 512, 4096)]
+    for scheme, group, Kd, N, r, alpha, M in cases:
+        W = (torch.randn(N, Kd, device=dev, generator=gen) / Kd ** 0.5).to(torch.bfloat16)
+        qw = quant.quantize(W, scheme, group)
+        A = ((torch.rand(r, Kd, device=dev, generator=gen) * 2 - 1) / Kd ** 0.5).to(torch.bfloat16)
+        B = (torch.randn(N, r, device=dev, generator=gen) * 0.1).to(torch.bfloat16)
+        x = torch.randn(M, Kd, device=dev, generator=gen).to(torch.bfloat16)
+        dy = torch.randn(M, N, device=dev, generator=gen).to(torch.bfloat16)
+        fl = 2.0 * M * (Kd * N + Kd * r + r * N)
+        d = {"workload": f"{scheme}_g{group}_{Kd}x{N}_r{r}", "tokens": M}
+        tf = graph_ms(lambda: K.qlora_linear_fwd(x, qw, A, B, alpha))
+        byts = lora_bytes(qw, W, A, B, M, Kd, N)
+        d.update({"fwd_ms": round(tf, 4), "fwd_tflops": round(fl / tf / 1e9, 1),
+                  "fwd_gbs": round(byts / tf / 1e6, 1)})
+        if M > 16:  # the fused in-loop-dequant kernel (lean workspace), for comparison
+            import dataclasses
+            ql = dataclasses.replace(qw, lean=True)
+            d["lean_fwd_ms"] = round(graph_ms(lambda: K.qlora_linear_fwd(x, ql, A, B, alpha)), 4)
+        if M <= 16:
+            d["fwd_roofline"] = {"bound": "hbm", "frac": round(byts / tf / 1e6 / peaks["hbm_gbs"], 4)}
+        else:
+            d["fwd_roofline"] = {"bound": "tensor",
+                                 "frac": round(fl / tf / 1e9 / peaks["bf16_tflops"], 4)}
+        if args.workload == "nf4":
+            _, saved = K.qlora_linear_fwd(x, qw, A, B, alpha, save_xa=True)
+            tb = graph_ms(lambda: K.qlora_linear_bwd(dy, x, qw, A, B, alpha, saved))
+            flb = 2.0 * M * (N * Kd + 2 * N * r + 2 * r * Kd)
+            d.update({"bwd_ms": round(tb, 4), "bwd_tflops": round(flb / tb / 1e9, 1)})
+        else:
+            Wm = K.merge(quant.dequantize(qw, torch.bfloat16), A, B, alpha)
+            tm = graph_ms(lambda: K.linear(x, Wm))
+            d.update({"merged_fwd_ms": round(tm, 4),
+                      "merged_gbs": round((Wm.numel() * 2 + 2 * M * (Kd + N)) / tm / 1e6, 1)})
+        emit(d)
+
+
 # -------------------------------------------------------- reference arm ----
 
 def run_reference(args, rank):
@@ -387,6 +642,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["lora", "stack", "nf4", "int", "fp32"], default="lora")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--ref-tokens", type=int, default=256)
@@ -408,7 +664,13 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "stack":
+            run_stack(args, rank, world, local_rank)
+        elif args.workload in ("nf4", "int", "fp32"):
+            if rank == 0:
+                run_sweep(args)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -197,18 +197,28 @@ MLORA_API int mlora_dequantize(int scheme, const void* codes, const void* scales
                                const void* zeros, int64_t N, int64_t K, int64_t group, void* out,
                                int out_dtype, void* stream);
 
-/* Bytes of workspace mlora_qlora_forward / mlora_qlora_backward need. */
+/* Bytes of workspace mlora_qlora_forward / mlora_qlora_backward need for the
+ * staged path (the fastest): it includes a bf16 [N, K] copy of the
+ * dequantised weight, made by one HBM-bound pass at the start of each call. */
 MLORA_API size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
                                                      int scheme, int64_t group);
 MLORA_API size_t mlora_qlora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
                                                       int scheme, int64_t group);
+/* The smallest workspace the quantised paths accept (backward != 0: for
+ * mlora_qlora_backward).  With less than the staged size and at least this
+ * much, the fused kernel runs instead: it dequantises inside the tensor-core
+ * main loop and keeps no dense copy of the weight.  Results are identical. */
+MLORA_API size_t mlora_qlora_lean_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                                  int scheme, int64_t group, int backward);
 
 /* y[M,N] = x . deq(W)^T + (alpha/r)(x . a^T) . b^T over a quantised base weight
  * (codes/scales/zeros as above; x, a, b, y BF16).  Replaces qlora_forward_nf4
- * (kernels/lora_quantized.metal:97-164) and qlora_forward_int4 (:29-93);
- * dequantisation happens inside the tensor-core main loop.  group (NF4 block
- * size / INT group) must be 64, 128 or 256; K a multiple of 32 (4-bit) or 16
- * (INT8).  saved_xa as for mlora_lora_forward. */
+ * (kernels/lora_quantized.metal:97-164) and qlora_forward_int4 (:29-93).  The
+ * GEMM operand is bf16(dequant(W)) -- staged in the workspace, or formed in
+ * the fused kernel's main loop (lean workspace); up to 16 tokens without
+ * saved_xa, a GEMV dequantises in registers.  group (NF4 block size / INT
+ * group) must be 64, 128 or 256; K a multiple of 32 (4-bit) or 16 (INT8).
+ * saved_xa as for mlora_lora_forward. */
 MLORA_API int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void* scales,
                                   const void* zeros, int64_t group, const void* a, const void* b,
                                   void* y, void* saved_xa, int64_t M, int64_t K, int64_t N,
@@ -216,8 +226,9 @@ MLORA_API int mlora_qlora_forward(const void* x, int scheme, const void* codes, 
                                   size_t workspace_bytes, void* stream);
 
 /* Gradients through the quantised base (frozen, as in QLoRA): dx = dy . deq(W)
- * + s (dy . b) . a (dequantised in the main loop; dx may be NULL), da, db as
- * mlora_lora_backward_ex (flags: MLORA_BWD_ACCUMULATE). */
+ * + s (dy . b) . a (staged or lean as for the forward; dx may be NULL, then
+ * the codes are not read), da, db as mlora_lora_backward_ex (flags:
+ * MLORA_BWD_ACCUMULATE). */
 MLORA_API int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* codes,
                                    const void* scales, const void* zeros, int64_t group,
                                    const void* a, const void* b, const void* saved_xa, void* dx,

@@ -65,6 +65,7 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_dequantize": (i32, [i32, vp, vp, vp, i64, i64, i64, vp, i32, vp]),
     "mlora_qlora_forward_workspace_bytes": (sz, [i64, i64, i64, i64, i32, i64]),
     "mlora_qlora_backward_workspace_bytes": (sz, [i64, i64, i64, i64, i32, i64]),
+    "mlora_qlora_lean_workspace_bytes": (sz, [i64, i64, i64, i64, i32, i64, i32]),
     "mlora_qlora_forward": (i32, [vp, i32, vp, vp, vp, i64, vp, vp, vp, vp, i64, i64, i64, i64,
                                   f32, i32, vp, sz, vp]),
     "mlora_qlora_backward": (i32, [vp, vp, i32, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, i64, i64,

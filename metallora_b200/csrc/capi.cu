@@ -1065,13 +1065,43 @@ int prep_scales(int scheme, const void* scales, const void* zeros, int64_t N, in
 }
 }  // namespace
 
+// Two ways to run a quantised base on the tensor cores:
+//  * staged (default): one HBM-bound pass dequantises W into a bf16 [N, K]
+//    copy at the front of the workspace (2.5 B/weight for 4-bit; ~18 us for
+//    11008 x 4096), then the dense kernels run on it.  The fused kernel
+//    dequantises each weight once per 128-token tile instead, so staging wins
+//    from the first tile on.
+//  * lean: the fused kernel dequantises inside its main loop and no dense copy
+//    is made; chosen when the caller's workspace is below the staged size but
+//    at least mlora_qlora_lean_workspace_bytes().
+// Both give bitwise-identical results (the operands are bf16(dequant(W)) either way).
+namespace {
+size_t staged_w_bytes(int64_t N, int64_t K) { return align_up(static_cast<size_t>(N * K) * 2, 256); }
+
+size_t qfwd_lean_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int64_t group) {
+  size_t bytes = plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
+  if (use_gemv(M, K, MLORA_DTYPE_BF16)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r).bytes);
+  return bytes;
+}
+
+size_t qbwd_lean_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int64_t group) {
+  return plan_backward(nullptr, M, K, N, r, true).bytes + qscales_bytes(N, K, group);
+}
+}  // namespace
+
+size_t mlora_qlora_lean_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme,
+                                        int64_t group, int backward) {
+  (void)scheme;
+  if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
+  return backward ? qbwd_lean_bytes(M, K, N, r, group) : qfwd_lean_bytes(M, K, N, r, group);
+}
+
 size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme,
                                            int64_t group) {
   (void)scheme;
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
-  size_t bytes = plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
-  if (use_gemv(M, K, MLORA_DTYPE_BF16)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r).bytes);
-  return bytes;
+  const size_t staged = staged_w_bytes(N, K) + plan_forward(nullptr, M, K, r, true).bytes;
+  return std::max(staged, qfwd_lean_bytes(M, K, N, r, group));
 }
 
 int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void* scales,
@@ -1084,17 +1114,28 @@ int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void
     return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
   if ((rc = check_ptrs16({x, codes, scales, zeros, a, b, y, saved_xa, workspace}))) return rc;
   if ((rc = check_device())) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (saved_xa == nullptr && use_gemv(M, K, dtype))
     return run_gemv(scheme, x, codes, scales, zeros, group, a, b, y, M, K, N, r, alpha, workspace,
-                    workspace_bytes, static_cast<cudaStream_t>(stream));
+                    workspace_bytes, s);
+  const size_t wbytes = staged_w_bytes(N, K);
+  const size_t staged = wbytes + plan_forward(nullptr, M, K, r, saved_xa == nullptr).bytes;
+  if (workspace != nullptr && workspace_bytes >= staged) {
+    if ((rc = launch_dequantize(scheme, codes, scales, zeros, N, K, group, workspace,
+                                MLORA_DTYPE_BF16, s)))
+      return rc;
+    return mlora_lora_forward(x, workspace, a, b, y, saved_xa, M, K, N, r, alpha, dtype,
+                              static_cast<uint8_t*>(workspace) + wbytes, workspace_bytes - wbytes,
+                              stream);
+  }
   const size_t sbytes = qscales_bytes(N, K, group);
   const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes + sbytes)
-    return fail(MLORA_ERR_WORKSPACE, "qlora forward workspace needs " +
-                                         std::to_string(need.bytes + sbytes) + " bytes");
+    return fail(MLORA_ERR_WORKSPACE, "qlora forward workspace needs " + std::to_string(staged) +
+                                         " bytes (or " + std::to_string(need.bytes + sbytes) +
+                                         " for the lean fused-dequant kernel)");
   const FwdPlan p = plan_forward(workspace, M, K, r, saved_xa == nullptr);
   void* scales_t = static_cast<uint8_t*>(workspace) + p.bytes;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
   if (e != cudaSuccess) return cuda_fail(e, "memset");
   if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
@@ -1144,7 +1185,8 @@ size_t mlora_qlora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int
                                             int scheme, int64_t group) {
   (void)scheme;
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
-  return plan_backward(nullptr, M, K, N, r, true).bytes + qscales_bytes(N, K, group);
+  const size_t staged = staged_w_bytes(N, K) + plan_backward(nullptr, M, K, N, r, true).bytes;
+  return std::max(staged, qbwd_lean_bytes(M, K, N, r, group));
 }
 
 int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* codes,
@@ -1162,24 +1204,36 @@ int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* 
   if ((rc = check_ptrs16({dy, x, codes, scales, zeros, a, b, saved_xa, dx, da, db, workspace})))
     return rc;
   if ((rc = check_device())) return rc;
-  const size_t sbytes = qscales_bytes(N, K, group);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool accumulate = (flags & MLORA_BWD_ACCUMULATE) != 0;
   const size_t bytes = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr).bytes;
+  if (dx == nullptr)  // weight gradients only: the base weight is not read
+    return backward16(dy, x, nullptr, nullptr, a, b, saved_xa, nullptr, da, db, M, K, N, r, alpha,
+                      clip_value, accumulate, dtype, workspace, workspace_bytes, s);
+  const size_t wbytes = staged_w_bytes(N, K);
+  if (workspace != nullptr && workspace_bytes >= wbytes + bytes) {
+    if ((rc = launch_dequantize(scheme, codes, scales, zeros, N, K, group, workspace,
+                                MLORA_DTYPE_BF16, s)))
+      return rc;
+    return backward16(dy, x, workspace, nullptr, a, b, saved_xa, dx, da, db, M, K, N, r, alpha,
+                      clip_value, accumulate, dtype, static_cast<uint8_t*>(workspace) + wbytes,
+                      workspace_bytes - wbytes, s);
+  }
+  const size_t sbytes = qscales_bytes(N, K, group);
   if (workspace == nullptr || workspace_bytes < bytes + sbytes)
     return fail(MLORA_ERR_WORKSPACE, "qlora backward workspace needs " +
-                                         std::to_string(bytes + sbytes) + " bytes");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+                                         std::to_string(wbytes + bytes) + " bytes (or " +
+                                         std::to_string(bytes + sbytes) +
+                                         " for the lean fused-dequant kernel)");
+  void* scales_t = static_cast<uint8_t*>(workspace) + bytes;
+  if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
   QGemmArgs q;
-  if (dx != nullptr) {
-    void* scales_t = static_cast<uint8_t*>(workspace) + bytes;
-    if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
-    q.scheme = scheme;
-    q.codes = codes;
-    q.scales_t = scales_t;
-    q.group = group;
-  }
-  return backward16(dy, x, nullptr, dx ? &q : nullptr, a, b, saved_xa, dx, da, db, M, K, N, r,
-                    alpha, clip_value, (flags & MLORA_BWD_ACCUMULATE) != 0, dtype, workspace,
-                    bytes, s);
+  q.scheme = scheme;
+  q.codes = codes;
+  q.scales_t = scales_t;
+  q.group = group;
+  return backward16(dy, x, nullptr, &q, a, b, saved_xa, dx, da, db, M, K, N, r, alpha, clip_value,
+                    accumulate, dtype, workspace, bytes, s);
 }
 
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {

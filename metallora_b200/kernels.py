@@ -291,10 +291,21 @@ def grad_norm_clip(grad: torch.Tensor, max_norm: float, out: torch.Tensor | None
 
 # --------------------------------------------------------- quantised bases --
 
+def _qlora_ws_bytes(lib, qw, M, K, N, r, backward, need_w=True):
+    """Staged workspace (a bf16 copy of deq(W), fastest) unless the weight asks
+    for the lean fused-dequant kernel, or the call does not read the weight."""
+    if getattr(qw, "lean", False) or not need_w:
+        return lib.mlora_qlora_lean_workspace_bytes(M, K, N, r, qw.code, qw.group, int(backward))
+    fn = (lib.mlora_qlora_backward_workspace_bytes if backward
+          else lib.mlora_qlora_forward_workspace_bytes)
+    return fn(M, K, N, r, qw.code, qw.group)
+
+
 def qlora_linear_fwd(x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor, alpha: float,
                      save_xa: bool = False):
     """y = x.deq(W)^T + (alpha/r).(x.A^T).B^T for a quantised base ``qw``
-    (metallora_b200.quant.QuantizedWeight); x, A, B bf16."""
+    (metallora_b200.quant.QuantizedWeight); x, A, B bf16.  ``qw.lean`` selects
+    the fused kernel that dequantises in its main loop (no dense copy of W)."""
     _need_cuda(x2d, a, b)
     if x2d.dtype != torch.bfloat16:
         raise ShapeError("quantised-base LoRA takes bf16 activations")
@@ -310,8 +321,7 @@ def qlora_linear_fwd(x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor, al
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x2d.device)
     saved = (torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=torch.bfloat16,
                          device=x2d.device) if save_xa else None)
-    ws = _workspace(lib.mlora_qlora_forward_workspace_bytes(M, K, N, r, qw.code, qw.group),
-                    x2d.device)
+    ws = _workspace(_qlora_ws_bytes(lib, qw, M, K, N, r, backward=False), x2d.device)
     st = lib.mlora_qlora_forward(_ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
                                  _ptr(qw.zeros), qw.group, _ptr(a), _ptr(b), _ptr(y), _ptr(saved),
                                  M, K, N, r, float(alpha), _lib.DTYPE_BF16, _ptr(ws), ws.numel(),
@@ -324,7 +334,7 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
                      alpha: float, saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
                      need_dx: bool = True, da_out: torch.Tensor | None = None,
                      db_out: torch.Tensor | None = None):
-    """(dx, dA, dB) through a frozen quantised base (dx dequantises in the main loop)."""
+    """(dx, dA, dB) through a frozen quantised base (staged or lean as the forward)."""
     _need_cuda(dy2d, x2d, a, b)
     M, K = x2d.shape
     N = dy2d.shape[1]
@@ -344,7 +354,7 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
     else:
         da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
         db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
-    ws = _workspace(lib.mlora_qlora_backward_workspace_bytes(M, K, N, r, qw.code, qw.group),
+    ws = _workspace(_qlora_ws_bytes(lib, qw, M, K, N, r, backward=True, need_w=need_dx),
                     x2d.device)
     st = lib.mlora_qlora_backward(_ptr(dy2d), _ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
                                   _ptr(qw.zeros), qw.group, _ptr(a_p), _ptr(b_p), _ptr(saved_xa),

@@ -118,14 +118,17 @@ class LoRALinear(nn.Module):
         return lora
 
     @torch.no_grad()
-    def quantize_base(self, scheme: str = "nf4", group: int | None = None) -> "LoRALinear":
+    def quantize_base(self, scheme: str = "nf4", group: int | None = None,
+                      lean: bool = False) -> "LoRALinear":
         """Replaces the frozen base W0 by its quantised form (QLoRA): NF4 with
         per-block absmax, or group-wise INT4/INT8 (the formats of
-        kernels/lora_quantized.metal).  The dense W0 is released."""
+        kernels/lora_quantized.metal).  The dense W0 is released.  ``lean``
+        keeps the per-call workspace free of a dequantised copy (see
+        metallora_b200.quant.quantize)."""
         from .quant import quantize
         if self.merged:
             raise ConfigurationError("quantize_base needs an unmerged layer")
-        self.qweight = quantize(self.W0.detach(), scheme, group)
+        self.qweight = quantize(self.W0.detach(), scheme, group, lean=lean)
         self.W0 = nn.Parameter(torch.empty(0, device=self.W0.device, dtype=self.W0.dtype),
                                requires_grad=False)
         return self

@@ -32,6 +32,7 @@ class QuantizedWeight:
     zeros: torch.Tensor | None
     group: int
     shape: tuple[int, int]
+    lean: bool = False  # fused in-loop dequant (no transient bf16 copy of W per call)
 
     @property
     def code(self) -> int:
@@ -57,8 +58,11 @@ class QuantizedWeight:
         return d
 
 
-def quantize(w: torch.Tensor, scheme: str = "nf4", group: int | None = None) -> QuantizedWeight:
-    """Quantises a 2-D CUDA weight [N, K] (bf16/fp16/fp32)."""
+def quantize(w: torch.Tensor, scheme: str = "nf4", group: int | None = None,
+             lean: bool = False) -> QuantizedWeight:
+    """Quantises a 2-D CUDA weight [N, K] (bf16/fp16/fp32).  ``lean`` makes the
+    LoRA kernels dequantise inside the GEMM main loop instead of staging a
+    bf16 copy of the weight in their workspace (less memory, slower)."""
     if scheme not in SCHEMES:
         raise QuantizationError(f"unknown scheme {scheme!r}; use one of {sorted(SCHEMES)}")
     _need_cuda(w)
@@ -81,7 +85,7 @@ def quantize(w: torch.Tensor, scheme: str = "nf4", group: int | None = None) -> 
     st = _lib.load().mlora_quantize(_ptr(w), _dtype_code(w), N, K, SCHEMES[scheme], group,
                                     _ptr(codes), _ptr(scales), _ptr(zeros), _stream())
     _lib.check(st, "mlora_quantize")
-    return QuantizedWeight(scheme, codes, scales, zeros, group, (N, K))
+    return QuantizedWeight(scheme, codes, scales, zeros, group, (N, K), lean)
 
 
 def dequantize(qw: QuantizedWeight, dtype: torch.dtype = torch.float32) -> torch.Tensor:
@@ -95,10 +99,11 @@ def dequantize(qw: QuantizedWeight, dtype: torch.dtype = torch.float32) -> torch
     return out
 
 
-def from_reference_layout(scheme: str, codes, scales, zeros, shape, group) -> QuantizedWeight:
+def from_reference_layout(scheme: str, codes, scales, zeros, shape, group,
+                          lean: bool = False) -> QuantizedWeight:
     """Wraps tensors already in the reference layout (e.g. loaded from disk)."""
     if scheme not in SCHEMES:
         raise QuantizationError(f"unknown scheme {scheme!r}")
     return QuantizedWeight(scheme, codes.contiguous(), scales.contiguous(),
                            None if zeros is None else zeros.contiguous(), int(group),
-                           (int(shape[0]), int(shape[1])))
+                           (int(shape[0]), int(shape[1])), lean)

@@ -45,6 +45,14 @@ def test_host_only_queries():
     f32 = lib.mlora_lora_forward_workspace_bytes(2048, 4096, 4096, 16, _lib.DTYPE_F32)
     assert f32 > 3 * 2048 * 4096 * 2
     assert lib.mlora_linear_workspace_bytes(128, 256, 256, _lib.DTYPE_BF16) == 0
+    # quantised bases: the staged workspace holds a bf16 copy of deq(W); the
+    # lean one (fused in-loop dequant) does not
+    for bwd_flag, fn in ((0, lib.mlora_qlora_forward_workspace_bytes),
+                         (1, lib.mlora_qlora_backward_workspace_bytes)):
+        staged = fn(4096, 4096, 11008, 64, _lib.QUANT_NF4, 64)
+        lean = lib.mlora_qlora_lean_workspace_bytes(4096, 4096, 11008, 64, _lib.QUANT_NF4, 64,
+                                                    bwd_flag)
+        assert 0 < lean < 11008 * 4096 * 2 <= staged < lean + 11008 * 4096 * 2 + (1 << 20)
 
 
 def test_invalid_arguments_rejected_before_launch():

@@ -68,15 +68,18 @@ SHAPES = [(256, 512, 768, 16), (300, 1024, 520, 8), (1, 4096, 1024, 64), (513, 2
           (130, 512, 264, 16)]
 
 
+@pytest.mark.parametrize("lean", [False, True], ids=["staged", "lean"])
 @pytest.mark.parametrize("scheme,group", [("nf4", 64), ("int4", 128), ("int8", 128),
                                           ("nf4", 256)])
 @pytest.mark.parametrize("shape", SHAPES)
-def test_qlora_forward_backward(cuda, scheme, group, shape):
+def test_qlora_forward_backward(cuda, scheme, group, shape, lean):
+    """staged = dequantise into the workspace + dense kernels; lean = the fused
+    kernel that dequantises in its main loop."""
     from metallora_b200 import kernels as K
     from metallora_b200 import quant
     M, Kd, N, r = shape
     g = torch.Generator().manual_seed(3)
-    qw = quant.quantize(_w(N, Kd, 2).to(cuda), scheme, group)
+    qw = quant.quantize(_w(N, Kd, 2).to(cuda), scheme, group, lean=lean)
     x = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(cuda)
     A = ((torch.rand(r, Kd, generator=g) * 2 - 1) / Kd ** 0.5).to(torch.bfloat16).to(cuda)
     B = (torch.randn(N, r, generator=g) * 0.1).to(torch.bfloat16).to(cuda)
