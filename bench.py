@@ -510,18 +510,24 @@ def run_stack(args, rank, world, local_rank):
 # ------------------------------------------------------ config sweeps ----
 
 def graph_ms(fn, reps=20, inner=5):
-    """Mean device time of fn() replayed from a CUDA graph (launch overhead hidden)."""
+    """Mean device time of one call replayed from a CUDA graph (launch overhead
+    hidden).  ``fn`` is a callable, or a list of callables captured in turn
+    (e.g. the same op on distinct weight copies, so that weights stream from
+    HBM rather than L2)."""
     import torch
+    fns = fn if isinstance(fn, (list, tuple)) else [fn]
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         for _ in range(3):
-            fn()
+            for f in fns:
+                f()
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for _ in range(inner):
-            fn()
+            for f in fns:
+                f()
     for _ in range(3):
         g.replay()
     torch.cuda.synchronize()
@@ -531,7 +537,10 @@ def graph_ms(fn, reps=20, inner=5):
         g.replay()
     e1.record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / reps / inner
+    return e0.elapsed_time(e1) / reps / inner / len(fns)
+
+
+L2_BYTES = 126 * 2 ** 20
 
 
 def run_sweep(args):
@@ -582,8 +591,17 @@ def run_sweep(args):
         dy = torch.randn(M, N, device=dev, generator=gen).to(torch.bfloat16)
         fl = 2.0 * M * (Kd * N + Kd * r + r * N)
         d = {"workload": f"{scheme}_g{group}_{Kd}x{N}_r{r}", "tokens": M}
-        tf = graph_ms(lambda: K.qlora_linear_fwd(x, qw, A, B, alpha))
         byts = lora_bytes(qw, W, A, B, M, Kd, N)
+        if M <= 16:
+            # decode: rotate over weight copies totalling > 1.5x L2 so every
+            # call streams its weight from HBM
+            copies = [qw] + [quant.quantize(W, scheme, group)
+                             for _ in range(int(1.5 * L2_BYTES // byts))]
+            tf = graph_ms([lambda c=c: K.qlora_linear_fwd(x, c, A, B, alpha) for c in copies],
+                          reps=10, inner=2)
+            d["weight_copies"] = len(copies)
+        else:
+            tf = graph_ms(lambda: K.qlora_linear_fwd(x, qw, A, B, alpha))
         d.update({"fwd_ms": round(tf, 4), "fwd_tflops": round(fl / tf / 1e9, 1),
                   "fwd_gbs": round(byts / tf / 1e6, 1)})
         if M > 16:  # the fused in-loop-dequant kernel (lean workspace), for comparison
@@ -602,7 +620,11 @@ def run_sweep(args):
             d.update({"bwd_ms": round(tb, 4), "bwd_tflops": round(flb / tb / 1e9, 1)})
         else:
             Wm = K.merge(quant.dequantize(qw, torch.bfloat16), A, B, alpha)
-            tm = graph_ms(lambda: K.linear(x, Wm))
+            if M <= 16:
+                wms = [Wm] + [Wm.clone() for _ in range(int(1.5 * L2_BYTES // (Wm.numel() * 2)))]
+                tm = graph_ms([lambda w=w: K.linear(x, w) for w in wms], reps=10, inner=2)
+            else:
+                tm = graph_ms(lambda: K.linear(x, Wm))
             d.update({"merged_fwd_ms": round(tm, 4),
                       "merged_gbs": round((Wm.numel() * 2 + 2 * M * (Kd + N)) / tm / 1e6, 1)})
         emit(d)

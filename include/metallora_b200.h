@@ -211,6 +211,18 @@ MLORA_API size_t mlora_qlora_backward_workspace_bytes(int64_t M, int64_t K, int6
 MLORA_API size_t mlora_qlora_lean_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
                                                   int scheme, int64_t group, int backward);
 
+/* The prepared scale table of a quantised weight: its per-row scales re-laid
+ * as [ceil(K/group), N rounded up to 4] -- fp32 absmax for NF4, (scale, zero)
+ * fp16 pairs for INT4/INT8 -- so that one TMA box holds a block of rows'
+ * scales.  The decode kernel and the fused kernel read scales only from it;
+ * without one, each call builds it in its workspace.  No reference
+ * counterpart (the reference reads its per-row scales directly,
+ * kernels/lora_quantized.metal:122, :64-65). */
+MLORA_API size_t mlora_qlora_prepared_scales_bytes(int scheme, int64_t N, int64_t K, int64_t group);
+MLORA_API int mlora_qlora_prepare_scales(int scheme, const void* scales, const void* zeros,
+                                         int64_t N, int64_t K, int64_t group, void* out,
+                                         void* stream);
+
 /* y[M,N] = x . deq(W)^T + (alpha/r)(x . a^T) . b^T over a quantised base weight
  * (codes/scales/zeros as above; x, a, b, y BF16).  Replaces qlora_forward_nf4
  * (kernels/lora_quantized.metal:97-164) and qlora_forward_int4 (:29-93).  The
@@ -224,6 +236,13 @@ MLORA_API int mlora_qlora_forward(const void* x, int scheme, const void* codes, 
                                   void* y, void* saved_xa, int64_t M, int64_t K, int64_t N,
                                   int64_t r, float alpha, int dtype, void* workspace,
                                   size_t workspace_bytes, void* stream);
+/* Same, with the weight's prepared scale table (may be NULL). */
+MLORA_API int mlora_qlora_forward_ex(const void* x, int scheme, const void* codes,
+                                     const void* scales, const void* zeros, const void* prepared,
+                                     int64_t group, const void* a, const void* b, void* y,
+                                     void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r,
+                                     float alpha, int dtype, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 
 /* Gradients through the quantised base (frozen, as in QLoRA): dx = dy . deq(W)
  * + s (dy . b) . a (staged or lean as for the forward; dx may be NULL, then
@@ -235,6 +254,14 @@ MLORA_API int mlora_qlora_backward(const void* dy, const void* x, int scheme, co
                                    float* da, float* db, int64_t M, int64_t K, int64_t N,
                                    int64_t r, float alpha, float clip_value, int dtype, int flags,
                                    void* workspace, size_t workspace_bytes, void* stream);
+/* Same, with the weight's prepared scale table (may be NULL). */
+MLORA_API int mlora_qlora_backward_ex(const void* dy, const void* x, int scheme, const void* codes,
+                                      const void* scales, const void* zeros, const void* prepared,
+                                      int64_t group, const void* a, const void* b,
+                                      const void* saved_xa, void* dx, float* da, float* db,
+                                      int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                                      float clip_value, int dtype, int flags, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /* ---- optimizer --------------------------------------------------------- */
 

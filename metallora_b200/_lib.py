@@ -70,6 +70,12 @@ SIGNATURES: dict[str, tuple] = {
                                   f32, i32, vp, sz, vp]),
     "mlora_qlora_backward": (i32, [vp, vp, i32, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, i64, i64,
                                    i64, i64, f32, f32, i32, i32, vp, sz, vp]),
+    "mlora_qlora_prepared_scales_bytes": (sz, [i32, i64, i64, i64]),
+    "mlora_qlora_prepare_scales": (i32, [i32, vp, vp, i64, i64, i64, vp, vp]),
+    "mlora_qlora_forward_ex": (i32, [vp, i32, vp, vp, vp, vp, i64, vp, vp, vp, vp, i64, i64, i64,
+                                     i64, f32, i32, vp, sz, vp]),
+    "mlora_qlora_backward_ex": (i32, [vp, vp, i32, vp, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp,
+                                      i64, i64, i64, i64, f32, f32, i32, i32, vp, sz, vp]),
     "mlora_adamw_step": (i32, [vp, vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp]),
     "mlora_sgd_step": (i32, [vp, vp, i64, f32, i32, vp, vp]),
     "mlora_adam_state_step": (i32, [vp, f32, f32, vp]),

@@ -297,9 +297,9 @@ bool use_gemv(int64_t M, int64_t K, int dtype) {
   return M <= kGemvMaxTokens && K % 32 == 0 && dtype == MLORA_DTYPE_BF16;
 }
 
-GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r) {
+GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int scheme) {
   GemvPlan p;
-  p.splits = gemv_splits(N, K);
+  p.splits = decode_config(scheme, M, N, K, r).splits;
   Carve c(ws);
   p.counter_bytes = static_cast<size_t>(gemv_row_blocks(N)) * 4;
   p.counters = static_cast<uint32_t*>(c.take(p.counter_bytes));
@@ -311,14 +311,14 @@ GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r) {
 }
 
 // Decode-size forward: counters, sT = s.x.A^T (if a), split-K GEMV + rank term.
-int run_gemv(int scheme, const void* x, const void* w, const void* scales, const void* zeros,
+int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
              int64_t group, const void* a, const void* b, void* y, int64_t M, int64_t K,
              int64_t N, int64_t r, float alpha, void* workspace, size_t workspace_bytes,
              cudaStream_t s) {
-  const GemvPlan need = plan_gemv(nullptr, M, K, N, r);
+  const GemvPlan need = plan_gemv(nullptr, M, K, N, r, scheme);
   if (workspace == nullptr || workspace_bytes < need.bytes)
     return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
-  const GemvPlan p = plan_gemv(workspace, M, K, N, r);
+  const GemvPlan p = plan_gemv(workspace, M, K, N, r, scheme);
   cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
   if (e != cudaSuccess) return cuda_fail(e, "memset");
   int rc;
@@ -328,8 +328,7 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales, const
   g.scheme = scheme;
   g.x = x;
   g.w = w;
-  g.scales = scales;
-  g.zeros = zeros;
+  g.scales_t = scales_t;
   g.b = a != nullptr ? b : nullptr;
   g.st = p.st;
   g.y = y;
@@ -656,7 +655,7 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
 
 // ---- plain linear and merge plans ----------------------------------------
 size_t linear_ws(int64_t M, int64_t K, int64_t N, int dtype) {
-  if (use_gemv(M, K, dtype)) return plan_gemv(nullptr, M, K, N, 0).bytes;
+  if (use_gemv(M, K, dtype)) return plan_gemv(nullptr, M, K, N, 0, 0).bytes;
   if (dtype != MLORA_DTYPE_F32) return 0;
   return plan_forward_f32(nullptr, M, K, N, 1, false).bytes;
 }
@@ -794,7 +793,7 @@ size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0) return 0;
   if (dtype == MLORA_DTYPE_F32) return plan_forward_f32(nullptr, M, K, N, r, true).bytes;
   size_t bytes = plan_forward(nullptr, M, K, r, true).bytes;
-  if (use_gemv(M, K, dtype)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r).bytes);
+  if (use_gemv(M, K, dtype)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r, 0).bytes);
   return bytes;
 }
 
@@ -816,7 +815,7 @@ int mlora_lora_forward(const void* x, const void* w0, const void* a, const void*
                             static_cast<cudaStream_t>(stream));
   }
   if (saved_xa == nullptr && use_gemv(M, K, dtype))
-    return run_gemv(0, x, w0, nullptr, nullptr, 64, a, b, y, M, K, N, r, alpha, workspace,
+    return run_gemv(0, x, w0, nullptr, 64, a, b, y, M, K, N, r, alpha, workspace,
                     workspace_bytes, static_cast<cudaStream_t>(stream));
   const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
@@ -1051,17 +1050,19 @@ int check_qlora(int scheme, int64_t M, int64_t K, int64_t N, int64_t r, int64_t 
 }
 
 size_t qscales_bytes(int64_t N, int64_t K, int64_t group) {
-  return align_up(static_cast<size_t>((K + group - 1) / group) * N * 4, 256);
+  return align_up(static_cast<size_t>((K + group - 1) / group) * prepared_ld(N) * 4, 256);
 }
 
-// Re-lays the per-row scales as [groups, N] (fp32 absmax, or (scale, zero) fp16 pairs).
+// The prepared scale table: per-row scales re-laid as [groups, prepared_ld(N)]
+// (fp32 absmax, or (scale, zero) fp16 pairs), so a TMA box of it is a block of
+// rows' scales for a range of k.
 int prep_scales(int scheme, const void* scales, const void* zeros, int64_t N, int64_t K,
                 int64_t group, void* scales_t, cudaStream_t s) {
   const int64_t G = (K + group - 1) / group;
   if (scheme == MLORA_QUANT_NF4)
-    return launch_transpose_f32(static_cast<const float*>(scales), N, G,
+    return launch_transpose_f32(static_cast<const float*>(scales), N, G, prepared_ld(N),
                                 static_cast<float*>(scales_t), s);
-  return launch_pack_scale_zero(scales, zeros, N, G, scales_t, s);
+  return launch_pack_scale_zero(scales, zeros, N, G, prepared_ld(N), scales_t, s);
 }
 }  // namespace
 
@@ -1078,9 +1079,10 @@ int prep_scales(int scheme, const void* scales, const void* zeros, int64_t N, in
 namespace {
 size_t staged_w_bytes(int64_t N, int64_t K) { return align_up(static_cast<size_t>(N * K) * 2, 256); }
 
-size_t qfwd_lean_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int64_t group) {
+size_t qfwd_lean_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme, int64_t group) {
   size_t bytes = plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
-  if (use_gemv(M, K, MLORA_DTYPE_BF16)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r).bytes);
+  if (use_gemv(M, K, MLORA_DTYPE_BF16))
+    bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r, scheme).bytes + qscales_bytes(N, K, group));
   return bytes;
 }
 
@@ -1091,9 +1093,8 @@ size_t qbwd_lean_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int64_t group
 
 size_t mlora_qlora_lean_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme,
                                         int64_t group, int backward) {
-  (void)scheme;
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
-  return backward ? qbwd_lean_bytes(M, K, N, r, group) : qfwd_lean_bytes(M, K, N, r, group);
+  return backward ? qbwd_lean_bytes(M, K, N, r, group) : qfwd_lean_bytes(M, K, N, r, scheme, group);
 }
 
 size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme,
@@ -1101,23 +1102,62 @@ size_t mlora_qlora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int6
   (void)scheme;
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0 || group <= 0) return 0;
   const size_t staged = staged_w_bytes(N, K) + plan_forward(nullptr, M, K, r, true).bytes;
-  return std::max(staged, qfwd_lean_bytes(M, K, N, r, group));
+  return std::max(staged, qfwd_lean_bytes(M, K, N, r, scheme, group));
+}
+
+size_t mlora_qlora_prepared_scales_bytes(int scheme, int64_t N, int64_t K, int64_t group) {
+  if (N <= 0 || K <= 0 || group <= 0) return 0;
+  (void)scheme;
+  return qscales_bytes(N, K, group);
+}
+
+int mlora_qlora_prepare_scales(int scheme, const void* scales, const void* zeros, int64_t N,
+                               int64_t K, int64_t group, void* out, void* stream) {
+  int rc = check_quant(scheme, N, K, group);
+  if (rc) return rc;
+  if (!scales || !out || (scheme != MLORA_QUANT_NF4 && !zeros))
+    return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if ((rc = check_ptrs16({scales, zeros, out}))) return rc;
+  if ((rc = check_device())) return rc;
+  return prep_scales(scheme, scales, zeros, N, K, group, out, static_cast<cudaStream_t>(stream));
 }
 
 int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void* scales,
                         const void* zeros, int64_t group, const void* a, const void* b, void* y,
                         void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return mlora_qlora_forward_ex(x, scheme, codes, scales, zeros, nullptr, group, a, b, y, saved_xa,
+                                M, K, N, r, alpha, dtype, workspace, workspace_bytes, stream);
+}
+
+int mlora_qlora_forward_ex(const void* x, int scheme, const void* codes, const void* scales,
+                           const void* zeros, const void* prepared, int64_t group, const void* a,
+                           const void* b, void* y, void* saved_xa, int64_t M, int64_t K, int64_t N,
+                           int64_t r, float alpha, int dtype, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   int rc = check_qlora(scheme, M, K, N, r, group, dtype);
   if (rc) return rc;
   if (!x || !codes || !scales || !a || !b || !y || (scheme != MLORA_QUANT_NF4 && !zeros))
     return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
-  if ((rc = check_ptrs16({x, codes, scales, zeros, a, b, y, saved_xa, workspace}))) return rc;
+  if ((rc = check_ptrs16({x, codes, scales, zeros, prepared, a, b, y, saved_xa, workspace})))
+    return rc;
   if ((rc = check_device())) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (saved_xa == nullptr && use_gemv(M, K, dtype))
-    return run_gemv(scheme, x, codes, scales, zeros, group, a, b, y, M, K, N, r, alpha, workspace,
-                    workspace_bytes, s);
+  if (saved_xa == nullptr && use_gemv(M, K, dtype)) {
+    const void* table = prepared;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    size_t ws_bytes = workspace_bytes;
+    if (table == nullptr) {  // build the scale table in the workspace
+      const size_t sb = qscales_bytes(N, K, group);
+      if (ws == nullptr || ws_bytes < sb)
+        return fail(MLORA_ERR_WORKSPACE, "decode workspace too small for the scale table");
+      if ((rc = prep_scales(scheme, scales, zeros, N, K, group, ws, s))) return rc;
+      table = ws;
+      ws += sb;
+      ws_bytes -= sb;
+    }
+    return run_gemv(scheme, x, codes, table, group, a, b, y, M, K, N, r, alpha, ws, ws_bytes, s);
+  }
   const size_t wbytes = staged_w_bytes(N, K);
   const size_t staged = wbytes + plan_forward(nullptr, M, K, r, saved_xa == nullptr).bytes;
   if (workspace != nullptr && workspace_bytes >= staged) {
@@ -1135,10 +1175,14 @@ int mlora_qlora_forward(const void* x, int scheme, const void* codes, const void
                                          " bytes (or " + std::to_string(need.bytes + sbytes) +
                                          " for the lean fused-dequant kernel)");
   const FwdPlan p = plan_forward(workspace, M, K, r, saved_xa == nullptr);
-  void* scales_t = static_cast<uint8_t*>(workspace) + p.bytes;
+  const void* scales_t = prepared;
   cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
   if (e != cudaSuccess) return cuda_fail(e, "memset");
-  if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
+  if (scales_t == nullptr) {
+    void* tab = static_cast<uint8_t*>(workspace) + p.bytes;
+    if ((rc = prep_scales(scheme, scales, zeros, N, K, group, tab, s))) return rc;
+    scales_t = tab;
+  }
   RankArgs ra;
   ra.x = x;
   ra.l = a;
@@ -1195,13 +1239,25 @@ int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* 
                          int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                          float clip_value, int dtype, int flags, void* workspace,
                          size_t workspace_bytes, void* stream) {
+  return mlora_qlora_backward_ex(dy, x, scheme, codes, scales, zeros, nullptr, group, a, b,
+                                 saved_xa, dx, da, db, M, K, N, r, alpha, clip_value, dtype, flags,
+                                 workspace, workspace_bytes, stream);
+}
+
+int mlora_qlora_backward_ex(const void* dy, const void* x, int scheme, const void* codes,
+                            const void* scales, const void* zeros, const void* prepared,
+                            int64_t group, const void* a, const void* b, const void* saved_xa,
+                            void* dx, float* da, float* db, int64_t M, int64_t K, int64_t N,
+                            int64_t r, float alpha, float clip_value, int dtype, int flags,
+                            void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_qlora(scheme, M, K, N, r, group, dtype);
   if (rc) return rc;
   if (flags & ~MLORA_BWD_ACCUMULATE) return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
   if (!dy || !x || !a || !b || !da || !db) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
   if (dx && (!codes || !scales || (scheme != MLORA_QUANT_NF4 && !zeros)))
     return fail(MLORA_ERR_INVALID_ARG, "dx needs the quantised weight");
-  if ((rc = check_ptrs16({dy, x, codes, scales, zeros, a, b, saved_xa, dx, da, db, workspace})))
+  if ((rc = check_ptrs16({dy, x, codes, scales, zeros, prepared, a, b, saved_xa, dx, da, db,
+                          workspace})))
     return rc;
   if ((rc = check_device())) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1225,8 +1281,12 @@ int mlora_qlora_backward(const void* dy, const void* x, int scheme, const void* 
                                          std::to_string(wbytes + bytes) + " bytes (or " +
                                          std::to_string(bytes + sbytes) +
                                          " for the lean fused-dequant kernel)");
-  void* scales_t = static_cast<uint8_t*>(workspace) + bytes;
-  if ((rc = prep_scales(scheme, scales, zeros, N, K, group, scales_t, s))) return rc;
+  const void* scales_t = prepared;
+  if (scales_t == nullptr) {
+    void* tab = static_cast<uint8_t*>(workspace) + bytes;
+    if ((rc = prep_scales(scheme, scales, zeros, N, K, group, tab, s))) return rc;
+    scales_t = tab;
+  }
   QGemmArgs q;
   q.scheme = scheme;
   q.codes = codes;
@@ -1250,7 +1310,7 @@ int mlora_linear(const void* x, const void* w, void* y, int64_t M, int64_t K, in
   if ((rc = check_device())) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_gemv(M, K, dtype))
-    return run_gemv(0, x, w, nullptr, nullptr, 64, nullptr, nullptr, y, M, K, N, 0, 1.f, workspace,
+    return run_gemv(0, x, w, nullptr, 64, nullptr, nullptr, y, M, K, N, 0, 1.f, workspace,
                     workspace_bytes, s);
   if (dtype == MLORA_DTYPE_F32)
     return lora_forward_f32(static_cast<const float*>(x), static_cast<const float*>(w), nullptr,

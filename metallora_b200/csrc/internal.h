@@ -107,10 +107,9 @@ int launch_qgemm(const QGemmArgs& a, cudaStream_t stream);
 // y = x . deq(W)^T (+ B . sT^T) for at most 16 tokens; scheme 0 = dense bf16.
 struct GemvArgs {
   int scheme = 0;
-  const void* x = nullptr;       // bf16 [M, K]
-  const void* w = nullptr;       // codes or bf16 weights, rows of the [N, K] weight
-  const void* scales = nullptr;  // reference layout [N, G]
-  const void* zeros = nullptr;
+  const void* x = nullptr;         // bf16 [M, K]
+  const void* w = nullptr;         // codes or bf16 weights, rows of the [N, K] weight
+  const void* scales_t = nullptr;  // prepared scale table [G, prepared_ld(N)] (quantised)
   const void* b = nullptr;       // bf16 [N, r] or nullptr
   const float* st = nullptr;     // fp32 [rank_small_splits(K), M, r] partials of s.x.A^T
   void* y = nullptr;             // bf16 [M, N]
@@ -120,9 +119,14 @@ struct GemvArgs {
   int splits = 1;
 };
 constexpr int64_t kGemvMaxTokens = 16;
-int gemv_splits(int64_t N, int64_t K);
+// Decode launch shape: k-splits per 128-row block, k per split, persistent CTAs.
+struct DecodeConfig {
+  int splits;
+  int kspan;
+  int ctas;
+};
+DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r);
 int64_t gemv_row_blocks(int64_t N);
-int64_t gemv_k_per_split(int64_t K, int splits);
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 int rank_small_splits(int64_t K);
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
@@ -197,10 +201,14 @@ int launch_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int scheme
                     void* codes, void* scales, void* zeros, cudaStream_t s);
 int launch_dequantize(int scheme, const void* codes, const void* scales, const void* zeros,
                       int64_t N, int64_t K, int64_t g, void* out, int out_dtype, cudaStream_t s);
-int launch_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
+// [rows, cols] -> [cols, ld] re-layouts (ld >= rows; padding columns zeroed).
+int launch_transpose_f32(const float* src, int64_t rows, int64_t cols, int64_t ld, float* dst,
                          cudaStream_t s);
 int launch_pack_scale_zero(const void* scales, const void* zeros, int64_t rows, int64_t cols,
-                           void* dst, cudaStream_t s);
+                           int64_t ld, void* dst, cudaStream_t s);
+// Row stride (elements) of the prepared scale table [groups, rows]: rows
+// rounded up to 4 so every table row starts on a 16-byte boundary (TMA).
+inline int64_t prepared_ld(int64_t rows) { return (rows + 3) / 4 * 4; }
 
 // ---------------------------------------------------------------- optimizer --
 int norm_grid();

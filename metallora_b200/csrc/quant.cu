@@ -233,9 +233,10 @@ __global__ void __launch_bounds__(256) dequantize_vec_kernel(
   }
 }
 
-// src [rows, cols] (row stride ld) -> dst [cols, rows] for 4-byte elements.
+// src [rows, cols] -> dst [cols, ld] (ld >= rows) for 4-byte elements;
+// columns rows..ld-1 of dst are zeroed.
 __global__ void transpose_f32_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
-                                     float* __restrict__ dst) {
+                                     int64_t ld, float* __restrict__ dst) {
   __shared__ float tile[32][33];
   const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -245,13 +246,14 @@ __global__ void transpose_f32_kernel(const float* __restrict__ src, int64_t rows
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int64_t c = c0 + i, r = r0 + threadIdx.x;
-    if (c < cols && r < rows) dst[c * rows + r] = tile[threadIdx.x][i];
+    if (c < cols && r < ld) dst[c * ld + r] = tile[threadIdx.x][i];
   }
 }
 
 // scale/zero fp16 [rows, cols] -> interleaved (scale, zero) pairs [cols, rows].
 __global__ void pack_scale_zero_kernel(const __half* __restrict__ s, const __half* __restrict__ z,
-                                       int64_t rows, int64_t cols, __half2* __restrict__ dst) {
+                                       int64_t rows, int64_t cols, int64_t ld,
+                                       __half2* __restrict__ dst) {
   __shared__ __half2 tile[32][33];
   const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -262,7 +264,7 @@ __global__ void pack_scale_zero_kernel(const __half* __restrict__ s, const __hal
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int64_t c = c0 + i, r = r0 + threadIdx.x;
-    if (c < cols && r < rows) dst[c * rows + r] = tile[threadIdx.x][i];
+    if (c < cols && r < ld) dst[c * ld + r] = tile[threadIdx.x][i];
   }
 }
 
@@ -378,21 +380,21 @@ int launch_dequantize(int scheme, const void* codes, const void* scales, const v
   return launched("dequantize");
 }
 
-int launch_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
+int launch_transpose_f32(const float* src, int64_t rows, int64_t cols, int64_t ld, float* dst,
                          cudaStream_t s) {
   LaunchScope scope(kKindElementwise, s);
-  dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
-  transpose_f32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, cols, dst);
+  dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((ld + 31) / 32));
+  transpose_f32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, cols, ld, dst);
   return launched("transpose_f32");
 }
 
 int launch_pack_scale_zero(const void* scales, const void* zeros, int64_t rows, int64_t cols,
-                           void* dst, cudaStream_t s) {
+                           int64_t ld, void* dst, cudaStream_t s) {
   LaunchScope scope(kKindElementwise, s);
-  dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+  dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((ld + 31) / 32));
   pack_scale_zero_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __half*>(scales),
                                                      static_cast<const __half*>(zeros), rows,
-                                                     cols, static_cast<__half2*>(dst));
+                                                     cols, ld, static_cast<__half2*>(dst));
   return launched("pack_scale_zero");
 }
 

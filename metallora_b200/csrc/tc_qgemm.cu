@@ -444,7 +444,7 @@ int launch_q(const QGemmArgs& a, cudaStream_t stream) {
     // scales_t [ngroups, w_rows]: box (64 rows of this k-block, the groups of 256 out-features)
     const uint32_t gbox = static_cast<uint32_t>(kBN / a.group);
     if (!make_tmap_raw(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, a.scales_t, w_rows, ngroups,
-                       w_rows * 4, kBK, gbox))
+                       prepared_ld(w_rows) * 4, kBK, gbox))
       return MLORA_ERR_INVALID_ARG;
     scale_box_bytes = kBK * gbox * 4;
   } else {
@@ -452,7 +452,7 @@ int launch_q(const QGemmArgs& a, cudaStream_t stream) {
                        code_cols, kBK * Tr::kBits / 8, kBN))
       return MLORA_ERR_INVALID_ARG;
     if (!make_tmap_raw(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, a.scales_t, w_rows, ngroups,
-                       w_rows * 4, kBN, 1))
+                       prepared_ld(w_rows) * 4, kBN, 1))
       return MLORA_ERR_INVALID_ARG;
     scale_box_bytes = kBN * 4;
   }

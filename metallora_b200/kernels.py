@@ -322,11 +322,11 @@ def qlora_linear_fwd(x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor, al
     saved = (torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=torch.bfloat16,
                          device=x2d.device) if save_xa else None)
     ws = _workspace(_qlora_ws_bytes(lib, qw, M, K, N, r, backward=False), x2d.device)
-    st = lib.mlora_qlora_forward(_ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
-                                 _ptr(qw.zeros), qw.group, _ptr(a), _ptr(b), _ptr(y), _ptr(saved),
-                                 M, K, N, r, float(alpha), _lib.DTYPE_BF16, _ptr(ws), ws.numel(),
-                                 _stream())
-    _lib.check(st, "mlora_qlora_forward")
+    st = lib.mlora_qlora_forward_ex(_ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
+                                    _ptr(qw.zeros), _ptr(qw.prepared_scales()), qw.group, _ptr(a),
+                                    _ptr(b), _ptr(y), _ptr(saved), M, K, N, r, float(alpha),
+                                    _lib.DTYPE_BF16, _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_qlora_forward_ex")
     return y, saved
 
 
@@ -356,12 +356,13 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
         db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
     ws = _workspace(_qlora_ws_bytes(lib, qw, M, K, N, r, backward=True, need_w=need_dx),
                     x2d.device)
-    st = lib.mlora_qlora_backward(_ptr(dy2d), _ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
-                                  _ptr(qw.zeros), qw.group, _ptr(a_p), _ptr(b_p), _ptr(saved_xa),
-                                  _ptr(dx), _ptr(da), _ptr(db), M, K, N, r, float(alpha_p),
-                                  float(clip_value), _lib.DTYPE_BF16, flags, _ptr(ws), ws.numel(),
-                                  _stream())
-    _lib.check(st, "mlora_qlora_backward")
+    st = lib.mlora_qlora_backward_ex(_ptr(dy2d), _ptr(x2d), qw.code, _ptr(qw.codes),
+                                     _ptr(qw.scales), _ptr(qw.zeros),
+                                     _ptr(qw.prepared_scales()) if need_dx else None, qw.group,
+                                     _ptr(a_p), _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da),
+                                     _ptr(db), M, K, N, r, float(alpha_p), float(clip_value),
+                                     _lib.DTYPE_BF16, flags, _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_qlora_backward_ex")
     if flags:
         return dx, da, db
     if r != r_orig:

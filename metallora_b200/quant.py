@@ -51,6 +51,21 @@ class QuantizedWeight:
     def dequantize(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         return dequantize(self, dtype)
 
+    def prepared_scales(self) -> torch.Tensor:
+        """The TMA-ready scale table [groups, rows rounded to 4] the GPU kernels
+        read (built once, on first use, and kept with the weight)."""
+        t = getattr(self, "_prepared", None)
+        if t is None or t.device != self.codes.device:
+            lib = _lib.load()
+            N, K = self.shape
+            nbytes = lib.mlora_qlora_prepared_scales_bytes(self.code, N, K, self.group)
+            t = torch.empty(nbytes, dtype=torch.uint8, device=self.codes.device)
+            st = lib.mlora_qlora_prepare_scales(self.code, _ptr(self.scales), _ptr(self.zeros), N,
+                                                K, self.group, _ptr(t), _stream())
+            _lib.check(st, "mlora_qlora_prepare_scales")
+            object.__setattr__(self, "_prepared", t)
+        return t
+
     def state_dict(self) -> dict[str, torch.Tensor]:
         d = {"codes": self.codes, "scales": self.scales}
         if self.zeros is not None:
