@@ -319,10 +319,16 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
   if (workspace == nullptr || workspace_bytes < need.bytes)
     return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
   const GemvPlan p = plan_gemv(workspace, M, K, N, r, scheme);
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
-  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  // split counters: zeroed by the rank kernel when there is one, else by a
+  // memset; a single split uses none
   int rc;
-  if (a != nullptr && (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, s)))
+  if (a == nullptr && p.splits > 1) {
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "memset");
+  }
+  if (a != nullptr &&
+      (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.counters,
+                              p.splits > 1 ? static_cast<int64_t>(p.counter_bytes / 4) : 0, s)))
     return rc;
   GemvArgs g;
   g.scheme = scheme;

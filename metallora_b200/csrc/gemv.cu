@@ -53,16 +53,18 @@ struct Dec {
   static constexpr int kQuads = kStageK / 64;            // 64-wide k quads per stage
   static constexpr int kQuadBytes = 64 * kBits / 8;      // bytes of one quad of one row
   static constexpr bool kScaled = kScheme != 0;
-  static constexpr int kStages = kScheme == kNF4 ? 6 : 4;
-  static constexpr int kLutBytes = kScheme == kNF4 ? 256 * 32 * 4 : 0;
+  static constexpr int kStages = 4;
+  // NF4 pair table: 256 entries, one copy per 16 lanes (at most 2-way bank
+  // conflicts), small enough for two CTAs per SM
+  static constexpr int kLutCopies = 16;
+  static constexpr int kLutBytes = kScheme == kNF4 ? 256 * kLutCopies * 4 : 0;
   static constexpr int kScaleSlot = 4 * kDecRows * 4;  // up to 4 groups x 128 rows x 4 bytes
   static constexpr int kScaleBytes = kScaled ? kStages * kScaleSlot : 0;
-  static constexpr int kXBytes = kScheme == kNF4 ? 32 * 1024 : 24 * 1024;
-  static constexpr int kMinBlocks = kScheme == kNF4 ? 1 : 2;
+  static constexpr int kMinBlocks = 2;  // registers sized for two CTAs per SM
   // k parts: the quads of each stage are dealt round-robin to kKS groups of
   // kRowGroups MMA warps (more warps to hide the table-lookup latency of NF4);
   // the groups' accumulators are summed in order at the end of each item
-  static constexpr int kKS = kScheme == kNF4 ? 2 : 1;
+  static constexpr int kKS = 1;
   static constexpr int kConsumers = kRowGroups * kKS;
   static constexpr int kThreads = 64 + 32 * kConsumers;
   static constexpr int kRedBytes = (kKS - 1) * kRowGroups * 32 * 16 * 4;
@@ -114,10 +116,11 @@ __device__ __forceinline__ void a_frags(const uint32_t (&w0)[kWords], const uint
     // word b/2 holds k 8(b/2)..+7; its bytes 2(b%2), 2(b%2)+1 are k+0,1 and k+2,3
     const uint32_t s0 = (b & 1) ? 0x4442u : 0x4440u, s1 = (b & 1) ? 0x4443u : 0x4441u;
     const uint32_t u0 = w0[b >> 1], u1 = w1[b >> 1];
-    a[0] = lut_lane[__byte_perm(u0, 0, s0) << 5];
-    a[2] = lut_lane[__byte_perm(u0, 0, s1) << 5];
-    a[1] = lut_lane[__byte_perm(u1, 0, s0) << 5];
-    a[3] = lut_lane[__byte_perm(u1, 0, s1) << 5];
+    constexpr int kC = Dec<kScheme>::kLutCopies;
+    a[0] = lut_lane[__byte_perm(u0, 0, s0) * kC];
+    a[2] = lut_lane[__byte_perm(u0, 0, s1) * kC];
+    a[1] = lut_lane[__byte_perm(u1, 0, s0) * kC];
+    a[3] = lut_lane[__byte_perm(u1, 0, s1) * kC];
   } else if constexpr (kScheme == kINT4) {
     const uint32_t sel = (b & 1) ? 0x4342u : 0x4140u;  // code bytes -> bits 0-7 and 16-23
     const uint32_t t0 = __byte_perm(w0[b >> 1], 0, sel), t1 = __byte_perm(w1[b >> 1], 0, sel);
@@ -182,16 +185,16 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
   constexpr int kWords = D::kQuadBytes / 16;  // 32-bit words per lane per row per quad: 2/4/8
   extern __shared__ uint8_t smem_raw[];
   // ring (1024-byte aligned for the 128-byte swizzle) | scale slots | lut |
-  // tokens | k-part partial sums | rank term per row | sT
+  // k-part partial sums | rank term per row | sT [M, r] | tokens [M, kspan + 4]
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t* scl = reinterpret_cast<const uint32_t*>(ring + D::kStages * kStageBytes);
   uint32_t* lut = reinterpret_cast<uint32_t*>(ring + D::kStages * kStageBytes + D::kScaleBytes);
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ring + D::kStages * kStageBytes +
-                                                      D::kScaleBytes + D::kLutBytes);
-  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + D::kXBytes);
-  float* rt = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + D::kXBytes + D::kRedBytes);
+  float* red = reinterpret_cast<float*>(ring + D::kStages * kStageBytes + D::kScaleBytes +
+                                        D::kLutBytes);
+  float* rt = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(red) + D::kRedBytes);
   float* sts = rt + kMaxTok * kDecRows;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sts + ((kMaxTok * p.r + 3) & ~3));
   __shared__ __align__(8) uint64_t full_bar[D::kStages];
   __shared__ __align__(8) uint64_t empty_bar[D::kStages];
   __shared__ __align__(8) uint64_t st_bar;    // sT folded into shared memory
@@ -214,9 +217,9 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
     fence_mbarrier_init();
   }
   if constexpr (kScheme == kNF4) {
-    // lut[e * 32 + c] = (bf16 L[e & 15], bf16 L[e >> 4]) for every lane copy c
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-      const int e = i >> 5;
+    // lut[e * kLutCopies + c] = (bf16 L[e & 15], bf16 L[e >> 4]) for every copy c
+    for (int i = threadIdx.x; i < 256 * D::kLutCopies; i += blockDim.x) {
+      const int e = i / D::kLutCopies;
       lut[i] = pack2<__nv_bfloat16>(kNF4Levels[e & 15], kNF4Levels[e >> 4]);
     }
   }
@@ -261,6 +264,16 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
     // wait for it, fold its k-slices in order into shared memory; then, with
     // a single k-split, the rank term sum_j B[n, j] sT[m, j] of each item's
     // rows (4 rows per lane), concurrently with the consumers' stage loop.
+    // B's rows of this CTA's first item go to L2 before the wait.
+    auto prefetch_b = [&](int item) {
+      if (p.b == nullptr || p.splits != 1 || item >= p.items) return;
+      const int rb = item % p.row_blocks;
+      const int rows = min(kDecRows, p.N - rb * kDecRows);
+      const char* base = reinterpret_cast<const char*>(p.b + static_cast<long long>(rb) * kDecRows * p.r);
+      for (int off = lane * 128; off < rows * p.r * 2; off += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+    };
+    prefetch_b(blockIdx.x);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (p.b != nullptr) {
       for (int i = lane; i < p.M * p.r; i += 32) {
@@ -284,6 +297,7 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
       uint32_t k = 0;
       for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++k) {
         const int rb = item % p.row_blocks;
+        prefetch_b(item + gridDim.x);
         if (!mbar_wait(&rt_empty, (k & 1) ^ 1, p.status, kDevTimeoutEmpty)) break;
         for (int rr = lane; rr < kDecRows; rr += 32) {
           float out[kMaxTok];
@@ -313,7 +327,7 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
   const int kp = cw / kRowGroups;           // k part
   const int ct = threadIdx.x - 64;          // k part 0: 0..127 = row within the block
   const int g = lane >> 2, q = lane & 3;
-  const uint32_t* lut_lane = lut + lane;
+  const uint32_t* lut_lane = lut + (lane % D::kLutCopies);
   bool ok = true;
   uint32_t it = 0;
   uint32_t items_done = 0;  // this CTA's items so far (rt_full parity)
@@ -550,6 +564,8 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
     __threadfence();
     named_bar_sync(2, kLead);
     if (ct == 0) {
+      // counters are zeroed by the programmatic primary (or a memset before it)
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       const uint32_t ticket = atomicAdd(&p.counters[rb], 1u);
       last_flag = ticket == static_cast<uint32_t>(p.splits - 1) ? 1u : 0u;
       if (last_flag) p.counters[rb] = 0;
@@ -595,8 +611,13 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
 // grid streams weights meanwhile; the decode kernel adds the slices in order.
 __global__ void __launch_bounds__(256) lora_rank_small_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ a, int M, int K, int r,
-    int kslice, float scale, float* __restrict__ st) {
+    int kslice, float scale, float* __restrict__ st, uint32_t* __restrict__ counters,
+    int n_counters) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // the decode kernel's split counters (it waits for this grid before its
+  // first ticket, so zeroing here needs no separate memset)
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
   __shared__ float red[8][kMaxTok];
   const int j = blockIdx.x, split = blockIdx.y;
   const int k0 = split * kslice, k1 = min(K, k0 + kslice);
@@ -647,24 +668,24 @@ __global__ void __launch_bounds__(256) lora_rank_small_kernel(
 int bits_of(int scheme) { return scheme == 0 ? 16 : (scheme == kINT8 ? 8 : 4); }
 int stage_k_of(int scheme) { return kBoxBytes * 8 / bits_of(scheme); }
 
+// Shared memory of one CTA: fixed regions, sT [16, r], tokens [M, kspan + 4].
 template <int kScheme>
-size_t smem_bytes_t(int64_t r) {
+size_t smem_bytes_t(int64_t M, int64_t r, int64_t kspan) {
   using D = Dec<kScheme>;
   return 1024 + static_cast<size_t>(D::kStages) * kStageBytes + D::kScaleBytes + D::kLutBytes +
-         D::kXBytes + D::kRedBytes + static_cast<size_t>(kMaxTok) * kDecRows * 4 +
-         static_cast<size_t>(kMaxTok) * (r > 0 ? r : 1) * 4;
+         D::kRedBytes + static_cast<size_t>(kMaxTok) * kDecRows * 4 +
+         static_cast<size_t>((kMaxTok * (r > 0 ? r : 1) + 3) & ~3) * 4 +
+         static_cast<size_t>(M * (kspan + 4) * 2 + 15) / 16 * 16;
 }
 
-size_t smem_bytes(int scheme, int64_t r) {
+size_t smem_bytes(int scheme, int64_t M, int64_t r, int64_t kspan) {
   switch (scheme) {
-    case 0: return smem_bytes_t<0>(r);
-    case kNF4: return smem_bytes_t<kNF4>(r);
-    case kINT4: return smem_bytes_t<kINT4>(r);
-    default: return smem_bytes_t<kINT8>(r);
+    case 0: return smem_bytes_t<0>(M, r, kspan);
+    case kNF4: return smem_bytes_t<kNF4>(M, r, kspan);
+    case kINT4: return smem_bytes_t<kINT4>(M, r, kspan);
+    default: return smem_bytes_t<kINT8>(M, r, kspan);
   }
 }
-
-int x_bytes(int scheme) { return scheme == kNF4 ? Dec<kNF4>::kXBytes : Dec<0>::kXBytes; }
 
 template <int kScheme, int kNT>
 int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t s) {
@@ -709,7 +730,7 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   p.row_blocks = static_cast<int>(gemv_row_blocks(a.N));
   p.items = p.row_blocks * cfg.splits;
   p.status = device_status_ptr();
-  const size_t smem = smem_bytes_t<kScheme>(a.r);
+  const size_t smem = static_cast<size_t>(cfg.smem);
   auto kern = lora_decode_kernel<kScheme, kNT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
@@ -749,36 +770,38 @@ int64_t gemv_row_blocks(int64_t N) { return (N + kDecRows - 1) / kDecRows; }
 
 DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r) {
   const int sk = stage_k_of(scheme);
-  const int64_t kspan_max = ((x_bytes(scheme) / (M * 2) - 4) / sk) * sk;  // whole stages
-  const int64_t total = (K + sk - 1) / sk;                                 // stages over K
+  const int64_t total = (K + sk - 1) / sk;  // stages over K
   const int64_t rb = gemv_row_blocks(N);
-  const int64_t per_sm = std::min<int64_t>(scheme == kNF4 ? 1 : 2,
-                                           kSmemPerSm / static_cast<int64_t>(smem_bytes(scheme, r) + 1024));
-  const int64_t slots = static_cast<int64_t>(num_sms()) * (per_sm > 0 ? per_sm : 1);
-  DecodeConfig best{1, static_cast<int>(total * sk), 1};
-  double best_cost = 1e30;
   const int sms = num_sms();
-  for (int64_t per = 1; per <= total; ++per) {  // stages per split
-    if (per * sk > kspan_max) break;
-    const int64_t splits = (total + per - 1) / per;
-    if (splits > 64) continue;
-    const int64_t items = rb * splits;
-    const int64_t ctas = items < slots ? items : slots;
-    const int64_t rounds = (items + ctas - 1) / ctas;
-    // Time in units of one stage at a fair share of HBM per SM: a CTA streams
-    // at most ~1.8x its share (ring depth / latency), so few CTAs stretch the
-    // stage time; each item also pays a fixed latency (token staging, first
-    // TMA, epilogue), larger with split partials (store, fence, atomic, read
-    // back); partial traffic is counted in stages.
-    const double active = static_cast<double>(ctas < sms ? ctas : sms);
-    const double stretch = std::max(1.0, 0.55 * sms / active);
-    const double fixed = splits == 1 ? 6.0 : 12.0;
-    const double part = 2.0 * splits * M * N * 4 / (kStageBytes * static_cast<double>(ctas));
-    const double cost = rounds * (per * stretch + fixed) + part;
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = DecodeConfig{static_cast<int>(splits), static_cast<int>(per * sk),
-                          static_cast<int>(ctas)};
+  const size_t fixed = smem_bytes(scheme, M, r, 0);  // everything but the token slice's k
+  DecodeConfig best{1, static_cast<int>(total * sk), 1, static_cast<int>(fixed)};
+  double best_cost = 1e30;
+  for (int per_sm = 2; per_sm >= 1; --per_sm) {  // CTAs per SM (shared memory decides)
+    const int64_t cap = std::min<int64_t>(227 * 1024, kSmemPerSm / per_sm - 1024);
+    if (static_cast<int64_t>(fixed) + M * sk * 2 > cap) continue;
+    const int64_t kspan_max = ((cap - static_cast<int64_t>(fixed)) / (M * 2) / sk) * sk;
+    const int64_t slots = static_cast<int64_t>(sms) * per_sm;
+    for (int64_t per = 1; per <= total; ++per) {  // stages per split
+      if (per * sk > kspan_max) break;
+      const int64_t splits = (total + per - 1) / per;
+      if (splits > 64) continue;
+      const int64_t items = rb * splits;
+      const int64_t ctas = items < slots ? items : slots;
+      const int64_t rounds = (items + ctas - 1) / ctas;
+      // Time in units of one stage of one CTA: the per-item fixed latency
+      // (token staging, first TMA, epilogue; larger with split partials), a
+      // stretch when few SMs stream, the split partials' traffic in stages
+      const double active = static_cast<double>(ctas < sms ? ctas : sms);
+      const double stretch = std::max(1.0, 0.55 * sms / active);
+      const double fixed_t = splits == 1 ? 6.0 : 12.0;
+      const double part = 2.0 * splits * M * N * 4 / (kStageBytes * static_cast<double>(ctas));
+      const double cost = rounds * (per * stretch + fixed_t) + part;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = DecodeConfig{static_cast<int>(splits), static_cast<int>(per * sk),
+                            static_cast<int>(ctas),
+                            static_cast<int>(smem_bytes(scheme, M, r, per * sk))};
+      }
     }
   }
   return best;
@@ -809,7 +832,13 @@ int rank_small_splits(int64_t K) {
 }
 
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
-                      float* st, cudaStream_t s) {
+                      float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s) {
+  // same shared-memory carveout as the decode kernel that follows, so SMs
+  // need no reconfiguration between the two
+  static const cudaError_t carve = cudaFuncSetAttribute(
+      lora_rank_small_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+      static_cast<int>(cudaSharedmemCarveoutMaxShared));
+  (void)carve;
   LaunchScope scope(kKindGemv, s);
   const int splits = rank_small_splits(K);
   const int64_t kslice = ((K + splits - 1) / splits + 7) / 8 * 8;
@@ -817,7 +846,8 @@ int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_
                            s>>>(static_cast<const __nv_bfloat16*>(x),
                                 static_cast<const __nv_bfloat16*>(a), static_cast<int>(M),
                                 static_cast<int>(K), static_cast<int>(r),
-                                static_cast<int>(kslice), scale, st);
+                                static_cast<int>(kslice), scale, st, counters,
+                                static_cast<int>(n_counters));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("rank_small launch: ") + cudaGetErrorString(e));

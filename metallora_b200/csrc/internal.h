@@ -124,13 +124,16 @@ struct DecodeConfig {
   int splits;
   int kspan;
   int ctas;
+  int smem;  // dynamic shared memory per CTA (bytes)
 };
 DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r);
 int64_t gemv_row_blocks(int64_t N);
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 int rank_small_splits(int64_t K);
+// sT partials for the decode path; also zeroes the decode kernel's n_counters
+// split counters.
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
-                      float* st, cudaStream_t s);
+                      float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s);
 
 // ------------------------------------------------------- rank projection -----
 // out[m, j] = scale * sum_k X[m, k] * L[j, k] for j < R (L rows >= r are zero).
