@@ -172,16 +172,25 @@ __device__ __forceinline__ bool split_reduce(float (&acc)[R], float* partials, u
   if (valid) {
 #pragma unroll
     for (int i = 0; i < R; ++i) acc[i] = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float4* src =
-          reinterpret_cast<const float4*>(partials + (static_cast<long long>(s) * rows_total + row) * R);
+    // splits in order, four splits' loads in flight together
+    for (int s0 = 0; s0 < splits; s0 += 4) {
 #pragma unroll
       for (int i = 0; i < R / 4; ++i) {
-        const float4 v = __ldcg(src + i);
-        acc[4 * i] += v.x;
-        acc[4 * i + 1] += v.y;
-        acc[4 * i + 2] += v.z;
-        acc[4 * i + 3] += v.w;
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = s0 + u < splits
+                     ? __ldcg(reinterpret_cast<const float4*>(
+                                  partials + (static_cast<long long>(s0 + u) * rows_total + row) * R) +
+                              i)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[4 * i] += v[u].x;
+          acc[4 * i + 1] += v[u].y;
+          acc[4 * i + 2] += v[u].z;
+          acc[4 * i + 3] += v[u].w;
+        }
       }
     }
   }
@@ -529,10 +538,12 @@ int wgrad_dispatch(const WgradArgs* probs, int n, cudaStream_t s) {
 
 }  // namespace
 
+// Split counts keep tiles x splits within one wave of resident CTAs (2 per SM):
+// a second, nearly empty wave would double the kernel's time.
 int rank_splits(int64_t M, int64_t K) {
   const int64_t tiles = (M + 127) / 128;
   const int64_t num_kb = (K + kBK - 1) / kBK;
-  int64_t splits = (2 * num_sms() + tiles - 1) / tiles;
+  int64_t splits = (2 * num_sms()) / tiles;
   const int64_t max_splits = num_kb / 4 > 0 ? num_kb / 4 : 1;  // >= 4 k-blocks per split
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
@@ -542,7 +553,7 @@ int rank_splits(int64_t M, int64_t K) {
 int wgrad_splits(int64_t M, int64_t P, int nproblems) {
   const int64_t tiles = (P + 127) / 128 * nproblems;
   const int64_t num_kb = (M + kBK - 1) / kBK;
-  int64_t splits = (2 * num_sms() + tiles - 1) / tiles;
+  int64_t splits = (2 * num_sms()) / tiles;
   const int64_t max_splits = num_kb / 4 > 0 ? num_kb / 4 : 1;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
