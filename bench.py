@@ -29,6 +29,9 @@ Other configurations of the same path (one JSON line per case):
     --workload int     INT4/INT8 group-128 bases, 4096->4096 and 4096->14336,
                        rank 16: forward unmerged and merged, 1..4096 tokens.
     --workload fp32    fp32 forward 4096->4096, rank 16, 2048 tokens, and merged.
+    --workload multi   per-sample adapters: 16 samples x 512 tokens, 4096->4096,
+                       r 16, 1/4/16/64 adapters (one rank pass over the stacked
+                       adapters + the tcgen05 GEMM), against one adapter.
 """
 from __future__ import annotations
 
@@ -543,6 +546,21 @@ def graph_ms(fn, reps=20, inner=5):
 L2_BYTES = 126 * 2 ** 20
 
 
+def events_ms(fn, reps=20, warm=3):
+    """Mean time of fn() between CUDA events (launch overhead included)."""
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
 def run_sweep(args):
     import torch
 
@@ -576,6 +594,25 @@ def run_sweep(args):
         emit({"workload": "fp32_fwd_4096x4096_r16_2048tok", "ms": round(t, 4),
               "tflops": round(fl / t / 1e9, 1), "merged_ms": round(tm, 4),
               "rel_err_vs_fp64": rel, "tokens_per_s": round(M / t * 1e3, 1)})
+        return
+    if args.workload == "multi":
+        # per-sample adapters (16 samples x 512 tokens, 4096 -> 4096, r 16)
+        from metallora_b200.ops import multi_adapter_forward
+        Kd, N, r, S, Bsz = 4096, 4096, 16, 512, 16
+        x = torch.randn(Bsz, S, Kd, device=dev, generator=gen).to(torch.bfloat16)
+        W = (torch.randn(N, Kd, device=dev, generator=gen) / 64).to(torch.bfloat16)
+        for n in (1, 4, 16, 64):
+            A = ((torch.rand(n, r, Kd, device=dev, generator=gen) * 2 - 1) / 64).to(torch.bfloat16)
+            Bm = (torch.randn(n, N, r, device=dev, generator=gen) * 0.1).to(torch.bfloat16)
+            ids = [b % n for b in range(Bsz)]
+            # host-side grouping of the ids: timed with events, not a graph
+            t = events_ms(lambda: multi_adapter_forward(x, W, A, Bm, ids, 32.0))
+            fl = 2.0 * Bsz * S * (Kd * N + Kd * r + r * N)
+            emit({"workload": "multi_adapter_fwd_4096x4096_r16", "tokens": Bsz * S,
+                  "adapters": n, "distinct_in_batch": min(n, Bsz), "ms": round(t, 4),
+                  "tflops": round(fl / t / 1e9, 1)})
+        t1 = events_ms(lambda: K.lora_linear_fwd(x.reshape(-1, Kd), W, A[0], Bm[0], 32.0))
+        emit({"workload": "single_adapter_fwd_4096x4096_r16", "tokens": Bsz * S, "ms": round(t1, 4)})
         return
     if args.workload == "nf4":
         cases = [("nf4", 64, 4096, 11008, 64, 128.0, M) for M in (1, 16, 512, 4096)]
@@ -671,7 +708,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["lora", "stack", "nf4", "int", "fp32"], default="lora")
+    ap.add_argument("--workload", choices=["lora", "stack", "nf4", "int", "fp32", "multi"],
+                    default="lora")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--ref-tokens", type=int, default=256)
@@ -695,7 +733,7 @@ def main():
     try:
         if args.workload == "stack":
             run_stack(args, rank, world, local_rank)
-        elif args.workload in ("nf4", "int", "fp32"):
+        elif args.workload in ("nf4", "int", "fp32", "multi"):
             if rank == 0:
                 run_sweep(args)
         else:

@@ -263,6 +263,27 @@ MLORA_API int mlora_qlora_backward_ex(const void* dy, const void* x, int scheme,
                                       float clip_value, int dtype, int flags, void* workspace,
                                       size_t workspace_bytes, void* stream);
 
+/* ---- multiple adapters in one batch ------------------------------------ */
+
+/* Token m uses adapter ids[m] of n adapters stacked in one pair of tensors:
+ *   y[m,:] = (w0 ? x[m] . w0^T : 0) + (alpha/r) (x[m] . A_g^T) . B_g^T,  g = ids[m]
+ * a_stack [n*r, K]: adapter g's A in rows g*r .. g*r+r-1; b_stack [N, n*r]:
+ * adapter g's B in columns g*r .. g*r+r-1; ids [M] int32 on the device (an id
+ * outside [0, n) adds no LoRA term).  n*r <= 256, r a multiple of 8, BF16 or
+ * F16.  One pass over x projects onto all n adapters (the rank kernel keeps
+ * each row's own adapter block), then the tcgen05 GEMM adds the stacked
+ * up-projection as extra k-blocks.  Replaces
+ * MultiAdapterManager.forward_batched (python/metal_lora/optimizations.py:193-217;
+ * w0 = NULL, alpha = r) and the lora_multi_adapter kernel
+ * (kernels/lora_kernels.metal:440-508). */
+MLORA_API size_t mlora_multi_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N,
+                                                          int64_t r, int64_t n, int dtype);
+MLORA_API int mlora_multi_lora_forward(const void* x, const void* w0, const void* a_stack,
+                                       const void* b_stack, const int32_t* ids, void* y,
+                                       int64_t M, int64_t K, int64_t N, int64_t r, int64_t n,
+                                       float alpha, int dtype, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /* ---- optimizer --------------------------------------------------------- */
 
 /* One AdamW step over a flat buffer of n parameters (reference:

@@ -71,6 +71,9 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_qlora_backward": (i32, [vp, vp, i32, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, i64, i64,
                                    i64, i64, f32, f32, i32, i32, vp, sz, vp]),
     "mlora_qlora_prepared_scales_bytes": (sz, [i32, i64, i64, i64]),
+    "mlora_multi_lora_forward_workspace_bytes": (sz, [i64, i64, i64, i64, i64, i32]),
+    "mlora_multi_lora_forward": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, f32, i32,
+                                       vp, sz, vp]),
     "mlora_qlora_prepare_scales": (i32, [i32, vp, vp, i64, i64, i64, vp, vp]),
     "mlora_qlora_forward_ex": (i32, [vp, i32, vp, vp, vp, vp, i64, vp, vp, vp, vp, i64, i64, i64,
                                      i64, f32, i32, vp, sz, vp]),

@@ -1302,6 +1302,88 @@ int mlora_qlora_backward_ex(const void* dy, const void* x, int scheme, const voi
                     accumulate, dtype, workspace, bytes, s);
 }
 
+size_t mlora_multi_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r,
+                                                int64_t n, int dtype) {
+  (void)N;
+  (void)dtype;
+  if (M <= 0 || K <= 0 || r <= 0 || n <= 0) return 0;
+  return plan_forward(nullptr, M, K, n * r, false).bytes;
+}
+
+int mlora_multi_lora_forward(const void* x, const void* w0, const void* a_stack,
+                             const void* b_stack, const int32_t* ids, void* y, int64_t M,
+                             int64_t K, int64_t N, int64_t r, int64_t n, float alpha, int dtype,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (n < 1 || n * r > 256)
+    return fail(MLORA_ERR_UNSUPPORTED, "stacked adapters: need 1 <= n and n * r <= 256");
+  int rc = check_shapes(M, K, N, n * r, dtype, false);
+  if (rc) return rc;
+  if (dtype == MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_UNSUPPORTED, "multi-adapter forward takes BF16 or F16");
+  if (!x || !a_stack || !b_stack || !ids || !y) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({x, w0, a_stack, b_stack, y, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  const int64_t R = n * r;
+  const FwdPlan need = plan_forward(nullptr, M, K, R, false);
+  if (workspace == nullptr || workspace_bytes < need.bytes)
+    return fail(MLORA_ERR_WORKSPACE, "multi-adapter workspace needs " + std::to_string(need.bytes) + " bytes");
+  const FwdPlan p = plan_forward(workspace, M, K, R, false);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  // one pass over x projects onto every stacked adapter; each row keeps its own
+  RankArgs ra;
+  ra.x = x;
+  ra.l = a_stack;
+  ra.M = M;
+  ra.K = K;
+  ra.r = R;
+  ra.R = p.R;
+  ra.ldx = K;
+  ra.ldl = K;
+  ra.scale = alpha / static_cast<float>(r);
+  ra.out_rows = p.xa_rows;
+  ra.ld_rows = p.R64;
+  ra.out_t = nullptr;
+  ra.ld_t = 0;
+  ra.partials = p.partials;
+  ra.counters = p.counters;
+  ra.splits = p.splits;
+  ra.elt = elt;
+  ra.row_group = ids;
+  ra.group_cols = r;
+  if ((rc = launch_rank(ra, s))) return rc;
+  GemmArgs ga;
+  ga.d = y;
+  ga.M = M;
+  ga.N = N;
+  ga.ldd = N;
+  ga.w_mn_major = false;
+  ga.elt = elt;
+  ga.out_dtype = dtype;
+  if (w0 != nullptr) {  // y = [x | xa] . [w0 | b_stack]^T
+    ga.x = x;
+    ga.w = w0;
+    ga.K = K;
+    ga.ldx = K;
+    ga.ldw = K;
+    ga.x2 = p.xa_rows;
+    ga.w2 = b_stack;
+    ga.R = p.R;
+    ga.w2_rows = R;
+    ga.ldx2 = p.R64;
+    ga.ldw2 = R;
+  } else {  // LoRA term only: y = xa . b_stack^T
+    ga.x = p.xa_rows;
+    ga.w = b_stack;
+    ga.K = R;
+    ga.ldx = p.R64;
+    ga.ldw = R;
+  }
+  return launch_gemm(ga, s);
+}
+
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {
   if (M <= 0 || K <= 0 || N <= 0) return 0;
   return linear_ws(M, K, N, dtype);

@@ -158,6 +158,10 @@ struct RankArgs {
   uint32_t* counters;  // [ceil(M/128)] zeroed
   int splits;
   Elt elt;
+  // stacked adapters: row m keeps only columns [g*group_cols, (g+1)*group_cols)
+  // of out_rows, g = row_group[m] (nullptr: all columns)
+  const int32_t* row_group = nullptr;
+  int64_t group_cols = 0;
 };
 int rank_splits(int64_t M, int64_t K);
 int launch_rank(const RankArgs& a, cudaStream_t stream);

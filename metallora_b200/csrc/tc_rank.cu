@@ -210,6 +210,8 @@ struct RankParams {
   float* partials;
   uint32_t* counters;
   uint32_t* status;
+  const int32_t* row_group;  // optional: keep only columns [g*group_cols, (g+1)*group_cols)
+  int group_cols;
 };
 
 template <int R, bool kBF16>
@@ -301,6 +303,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     } else if (final_cta && row < p.M) {
+      if (p.row_group != nullptr) {
+        // stacked adapters: the row keeps only its own adapter's columns (an
+        // id outside [0, R / group_cols) keeps none)
+        const int g = p.row_group[row];
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+          if (j / p.group_cols != g) acc[j] = 0.f;
+      }
       if (p.out_rows != nullptr) {
         T* dst = reinterpret_cast<T*>(p.out_rows) + row * p.ld_rows;
 #pragma unroll
@@ -463,6 +473,8 @@ int launch_rank_typed(const RankArgs& a, cudaStream_t stream) {
   p.partials = a.partials;
   p.counters = a.counters;
   p.status = device_status_ptr();
+  p.row_group = a.row_group;
+  p.group_cols = a.group_cols > 0 ? static_cast<int>(a.group_cols) : R;
   auto kern = rank_proj_kernel<R, kBF16>;
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
   dim3 grid(static_cast<unsigned>((a.M + 127) / 128), static_cast<unsigned>(a.splits));

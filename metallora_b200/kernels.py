@@ -368,3 +368,37 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
     if r != r_orig:
         da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
     return dx, da, db
+
+
+# ------------------------------------------------------ stacked adapters --
+
+MAX_STACKED_RANK = 256  # n_adapters * rank per launch
+
+
+def multi_lora_fwd(x2d: torch.Tensor, w0: torch.Tensor | None, a_stack: torch.Tensor,
+                   b_stack: torch.Tensor, ids: torch.Tensor, r: int, alpha: float) -> torch.Tensor:
+    """y = (x.w0^T if w0 is given) + (alpha/r) (x.A_g^T).B_g^T with g = ids[m] per
+    token, over n adapters stacked as a_stack [n*r, K] and b_stack [N, n*r]
+    (one launch of the rank kernel for all of them, then the tcgen05 GEMM);
+    ids is an int32 CUDA tensor [M]; an id outside [0, n) adds no LoRA term."""
+    _need_cuda(x2d, a_stack, b_stack, ids, w0)
+    M, K = x2d.shape
+    nr, K2 = a_stack.shape
+    N = b_stack.shape[0]
+    if K2 != K or b_stack.shape[1] != nr or nr % r:
+        raise ShapeError("a_stack [n*r, K] and b_stack [N, n*r] do not match x / r")
+    if w0 is not None:
+        _check_2d("W0", w0, (N, K), x2d.dtype)
+    if ids.dtype != torch.int32 or ids.numel() != M:
+        raise ShapeError("ids must be an int32 tensor with one entry per token")
+    n = nr // r
+    lib = _lib.load()
+    x2d, a_stack, b_stack = x2d.contiguous(), a_stack.contiguous(), b_stack.contiguous()
+    y = torch.empty((M, N), dtype=x2d.dtype, device=x2d.device)
+    code = _dtype_code(x2d)
+    ws = _workspace(lib.mlora_multi_lora_forward_workspace_bytes(M, K, N, r, n, code), x2d.device)
+    st = lib.mlora_multi_lora_forward(_ptr(x2d), _ptr(w0), _ptr(a_stack), _ptr(b_stack),
+                                      _ptr(ids.contiguous()), _ptr(y), M, K, N, r, n, float(alpha),
+                                      code, _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_multi_lora_forward")
+    return y

@@ -164,3 +164,48 @@ def unmerge_lora_weights(w_merged, W0, A, B, alpha: float = 16.0):  # noqa: N803
     a_rec = torch.diag(sqrt_s) @ vt[:rank, :]
     b_rec = u[:, :rank] @ torch.diag(sqrt_s)
     return a_rec.to(A.dtype), b_rec.to(B.dtype)
+
+
+def multi_adapter_forward(x, W0, adapters_A, adapters_B, adapter_ids, alpha: float = 16.0):  # noqa: N803
+    """Per-sample adapters over a shared base (the ``lora_multi_adapter`` kernel,
+    kernels/lora_kernels.metal:440-508): ``y[b] = x[b].W0^T + (alpha/r)
+    (x[b].A_id^T).B_id^T`` with ``id = adapter_ids[b]``.
+
+    x [B, S, K]; W0 [N, K] or None (LoRA term only); adapters_A [n, r, K];
+    adapters_B [n, N, r]; adapter_ids: ints, one per sample.  Only the
+    adapters the batch uses are stacked; more than fit one launch
+    (n * r <= 256) are applied in groups.
+    """
+    if x.dim() == 2:
+        x = x.unsqueeze(0)
+    Bsz, S, K = x.shape
+    n_all, r, _ = adapters_A.shape
+    N = adapters_B.shape[1]
+    # ids are small host data: grouping and per-token ids are built on the host
+    # (a CUDA tensor of ids is read back once)
+    ids = [int(i) for i in (adapter_ids.tolist() if torch.is_tensor(adapter_ids) else adapter_ids)]
+    if len(ids) != Bsz:
+        raise ShapeError(f"{len(ids)} adapter ids for {Bsz} samples")
+    if any(i < 0 or i >= n_all for i in ids):
+        raise ShapeError(f"adapter ids must be in [0, {n_all})")
+    x2d = x.reshape(-1, K)
+    used = sorted(set(ids))
+    r8 = (r + 7) // 8 * 8
+    per = max(1, _k.MAX_STACKED_RANK // r8)
+    y = None
+    for g0 in range(0, len(used), per):
+        group = used[g0:g0 + per]
+        sel = torch.tensor(group, dtype=torch.int64).to(x.device, non_blocking=True)
+        a, b = adapters_A.index_select(0, sel).to(x.dtype), adapters_B.index_select(0, sel).to(x.dtype)
+        if r8 != r:  # zero-padded rank, alpha/r unchanged
+            a = torch.nn.functional.pad(a, (0, 0, 0, r8 - r))
+            b = torch.nn.functional.pad(b, (0, r8 - r))
+        a_stack = a.reshape(len(group) * r8, K)
+        b_stack = b.permute(1, 0, 2).reshape(N, len(group) * r8)
+        slot = {g: j for j, g in enumerate(group)}
+        tok_host = torch.tensor([slot.get(i, -1) for i in ids], dtype=torch.int32)
+        tok = tok_host.repeat_interleave(S).to(x.device, non_blocking=True)
+        base = W0.to(x.dtype) if (W0 is not None and y is None) else None
+        part = _k.multi_lora_fwd(x2d, base, a_stack, b_stack, tok, r8, float(alpha) * r8 / r)
+        y = part if y is None else y + part
+    return y.reshape(Bsz, S, N)

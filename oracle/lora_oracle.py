@@ -146,3 +146,24 @@ def lora_flops(M, K, N, r, backward=False):
     if backward:
         return 2.0 * M * (N * K + 2 * N * r + 2 * r * K)
     return 2.0 * M * (K * N + K * r + r * N)
+
+
+def multi_adapter_forward(x, W0, A_all, B_all, ids, alpha, dtype=np.float64):  # noqa: N803
+    """Per-sample adapters over a shared base, as the reference's
+    ``lora_multi_adapter`` kernel computes it (kernels/lora_kernels.metal:
+    440-508): for sample b, ``out = x[b].W0^T + (alpha/rank).(x[b].A_id^T).B_id^T``
+    with ``id = ids[b]``; ``W0 = None`` gives the LoRA term alone and
+    ``alpha = rank`` gives ``MultiAdapterManager.forward_batched``
+    (python/metal_lora/optimizations.py:193-217, einsum bsk,brk->bsr then
+    bsr,bdr->bsd).  x [B, S, K]; A_all [n, r, K]; B_all [n, N, r]."""
+    x = np.asarray(x, dtype)
+    out = []
+    for b, g in enumerate(ids):
+        A = np.asarray(A_all[g], dtype)
+        B = np.asarray(B_all[g], dtype)
+        ax = x[b] @ A.T
+        y = (alpha / A.shape[0]) * (ax @ B.T)
+        if W0 is not None:
+            y = x[b] @ np.asarray(W0, dtype).T + y
+        out.append(y)
+    return np.stack(out)
