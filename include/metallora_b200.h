@@ -70,7 +70,9 @@ MLORA_API const char* mlora_last_error_message(void);
 MLORA_API int mlora_device_supported(int device);
 
 /* Reads (and with reset != 0 clears) the status word of the current device.
- * *out = 0 when no kernel has recorded a bounded-wait timeout.  Synchronous. */
+ * *out = 0 when no kernel has recorded a fault: 0x101-0x106 a bounded wait
+ * timed out (the kernel gave up instead of hanging); 0x107 a gathered row
+ * index was outside its table.  Synchronous. */
 MLORA_API int mlora_device_status(uint32_t* out, int reset);
 
 /* ---- measurement ------------------------------------------------------- */
@@ -283,6 +285,33 @@ MLORA_API int mlora_multi_lora_forward(const void* x, const void* w0, const void
                                        int64_t M, int64_t K, int64_t N, int64_t r, int64_t n,
                                        float alpha, int dtype, void* workspace,
                                        size_t workspace_bytes, void* stream);
+
+/* ---- LoRA embedding ----------------------------------------------------- */
+
+/* out[t, :] = table[idx[t], :] + (alpha/r) * b[idx[t], :] . a  (LoRAEmbedding.__call__,
+ * python/metal_lora/layers.py:220-225).  table [V, D], a [r, D], b [V, r],
+ * idx [T] int32 on the device; BF16/F16 run on the tensor cores (D, r
+ * multiples of 8), F32 on CUDA cores.  An index outside [0, V) gives a zero
+ * row and sets the device status word. */
+MLORA_API size_t mlora_lora_embedding_workspace_bytes(int64_t T, int64_t D, int64_t r, int dtype,
+                                                      int backward);
+MLORA_API int mlora_lora_embedding_forward(const int32_t* idx, const void* table, const void* a,
+                                           const void* b, void* out, int64_t T, int64_t V,
+                                           int64_t D, int64_t r, float alpha, int dtype,
+                                           void* workspace, size_t workspace_bytes, void* stream);
+/* Gradients of a and b (the table is frozen, layers.py:217-218), fp32:
+ *   da[j, :] = (alpha/r) sum_t b[idx[t], j] dy[t, :]
+ *   db[v, :] = (alpha/r) sum_{t: idx[t] = v} dy[t, :] . a^T
+ * sorted_idx / order: idx sorted stably and the token positions in that order
+ * (db rows are summed in that order: deterministic).  flags:
+ * MLORA_BWD_ACCUMULATE adds into da/db; otherwise db rows no token uses are
+ * zeroed. */
+MLORA_API int mlora_lora_embedding_backward(const void* dy, const int32_t* idx,
+                                            const int32_t* sorted_idx, const int32_t* order,
+                                            const void* a, const void* b, float* da, float* db,
+                                            int64_t T, int64_t V, int64_t D, int64_t r, float alpha,
+                                            int dtype, int flags, void* workspace,
+                                            size_t workspace_bytes, void* stream);
 
 /* ---- optimizer --------------------------------------------------------- */
 

@@ -1384,6 +1384,179 @@ int mlora_multi_lora_forward(const void* x, const void* w0, const void* a_stack,
   return launch_gemm(ga, s);
 }
 
+namespace {
+struct EmbedBwdPlan {
+  FwdPlan rank;       // U = s dy.A^T rows [T, R64] (16-bit)
+  void* gt;           // s B[idx]^T [R, pad8(T)]
+  float* wpart;       // weight-gradient partials
+  uint32_t* wcount;   // [ceil(D/128)]
+  int wsplits;
+  size_t bytes;
+};
+
+EmbedBwdPlan plan_embed_bwd(void* ws, int64_t T, int64_t D, int64_t r) {
+  EmbedBwdPlan p;
+  p.rank = plan_forward(ws, T, D, r, false);
+  Carve c(ws == nullptr ? nullptr : static_cast<uint8_t*>(ws) + p.rank.bytes);
+  p.gt = c.take(static_cast<size_t>(p.rank.R) * pad8(T) * 2);
+  p.wsplits = wgrad_splits(T, D, 1);
+  p.wcount = static_cast<uint32_t*>(c.take(static_cast<size_t>((D + 127) / 128) * 4));
+  p.wpart = p.wsplits > 1 ? static_cast<float*>(c.take(static_cast<size_t>(p.wsplits) * D * p.rank.R * 4))
+                          : nullptr;
+  p.bytes = p.rank.bytes + align_up(c.off, 256);
+  return p;
+}
+
+int check_embed(int64_t T, int64_t V, int64_t D, int64_t r, int dtype) {
+  if (T <= 0 || V <= 0 || D <= 0) return fail(MLORA_ERR_INVALID_ARG, "T, V, D must be positive");
+  if (r < 1 || r > 256) return fail(MLORA_ERR_INVALID_ARG, "rank must be in [1, 256]");
+  if (dtype != MLORA_DTYPE_BF16 && dtype != MLORA_DTYPE_F16 && dtype != MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_UNSUPPORTED, "dtype must be BF16, F16 or F32");
+  if (dtype != MLORA_DTYPE_F32 && (D % 8 || r % 8))
+    return fail(MLORA_ERR_UNSUPPORTED, "16-bit embedding: D and r must be multiples of 8");
+  if (T > (int64_t(1) << 31) - 1 || V > (int64_t(1) << 31) - 1)
+    return fail(MLORA_ERR_UNSUPPORTED, "too many tokens or rows");
+  return MLORA_OK;
+}
+}  // namespace
+
+size_t mlora_lora_embedding_workspace_bytes(int64_t T, int64_t D, int64_t r, int dtype,
+                                            int backward) {
+  if (T <= 0 || D <= 0 || r <= 0) return 0;
+  if (dtype == MLORA_DTYPE_F32) return backward ? align_up(static_cast<size_t>(T) * r * 4, 256) : 0;
+  if (!backward) return align_up(static_cast<size_t>(T) * r * 2, 256);
+  return plan_embed_bwd(nullptr, T, D, r).bytes;
+}
+
+int mlora_lora_embedding_forward(const int32_t* idx, const void* table, const void* a,
+                                 const void* b, void* out, int64_t T, int64_t V, int64_t D,
+                                 int64_t r, float alpha, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  int rc = check_embed(T, V, D, r, dtype);
+  if (rc) return rc;
+  if (!idx || !table || !a || !b || !out) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({table, a, b, out, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float scale = alpha / static_cast<float>(r);
+  if (dtype == MLORA_DTYPE_F32)
+    return launch_embedding_f32(idx, static_cast<const float*>(table), static_cast<const float*>(a),
+                                static_cast<const float*>(b), static_cast<float*>(out), T, V, D, r,
+                                scale, s);
+  const size_t need = align_up(static_cast<size_t>(T) * r * 2, 256);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MLORA_ERR_WORKSPACE, "embedding workspace needs " + std::to_string(need) + " bytes");
+  const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
+  // G = B[idx] [T, r], then out = s * G.A + E[idx] on the tensor cores
+  if ((rc = launch_gather_rows(idx, b, V, T, r, r, workspace, r, nullptr, 0, 1.f, elt, s))) return rc;
+  GemmArgs ga;
+  ga.x = workspace;
+  ga.w = a;            // A [r, D] read MN-major as W [K = r, N = D]
+  ga.d = out;
+  ga.c = table;        // addend rows gathered by idx
+  ga.ldc = D;
+  ga.c_index = idx;
+  ga.c_rows = V;
+  ga.acc_scale = scale;
+  ga.M = T;
+  ga.N = D;
+  ga.K = r;
+  ga.ldx = r;
+  ga.ldw = D;
+  ga.ldd = D;
+  ga.w_mn_major = true;
+  ga.elt = elt;
+  ga.out_dtype = dtype;
+  return launch_gemm(ga, s);
+}
+
+int mlora_lora_embedding_backward(const void* dy, const int32_t* idx, const int32_t* sorted_idx,
+                                  const int32_t* order, const void* a, const void* b, float* da,
+                                  float* db, int64_t T, int64_t V, int64_t D, int64_t r,
+                                  float alpha, int dtype, int flags, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  int rc = check_embed(T, V, D, r, dtype);
+  if (rc) return rc;
+  if (flags & ~MLORA_BWD_ACCUMULATE) return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
+  if (!dy || !idx || !sorted_idx || !order || !a || !b || !da || !db)
+    return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({dy, a, b, da, db, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  const bool accumulate = (flags & MLORA_BWD_ACCUMULATE) != 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float scale = alpha / static_cast<float>(r);
+  cudaError_t e;
+  if (!accumulate) {  // rows of db no token touches are zero
+    e = cudaMemsetAsync(db, 0, static_cast<size_t>(V) * r * 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "memset");
+  }
+  if (dtype == MLORA_DTYPE_F32) {
+    const size_t need = align_up(static_cast<size_t>(T) * r * 4, 256);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(MLORA_ERR_WORKSPACE, "embedding backward workspace needs " + std::to_string(need) + " bytes");
+    float* u = static_cast<float*>(workspace);
+    if ((rc = launch_rows_dot_f32(static_cast<const float*>(dy), static_cast<const float*>(a), u, T,
+                                  D, r, scale, s)))
+      return rc;
+    if ((rc = launch_segment_rows(sorted_idx, order, u, r, T, r, db, V, true, dtype, s))) return rc;
+    return launch_embed_da_f32(idx, static_cast<const float*>(b), static_cast<const float*>(dy), da,
+                               V, T, D, r, scale, accumulate, s);
+  }
+  const EmbedBwdPlan need = plan_embed_bwd(nullptr, T, D, r);
+  if (workspace == nullptr || workspace_bytes < need.bytes)
+    return fail(MLORA_ERR_WORKSPACE, "embedding backward workspace needs " + std::to_string(need.bytes) + " bytes");
+  const EmbedBwdPlan p = plan_embed_bwd(workspace, T, D, r);
+  const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
+  e = cudaMemsetAsync(p.rank.counters, 0, ((T + 127) / 128) * 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.wcount, 0, ((D + 127) / 128) * 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  // U = s dy.A^T, then dB rows as in-order sums of U over each index's tokens
+  RankArgs ra;
+  ra.x = dy;
+  ra.l = a;
+  ra.M = T;
+  ra.K = D;
+  ra.r = r;
+  ra.R = p.rank.R;
+  ra.ldx = D;
+  ra.ldl = D;
+  ra.scale = scale;
+  ra.out_rows = p.rank.xa_rows;
+  ra.ld_rows = p.rank.R64;
+  ra.out_t = nullptr;
+  ra.ld_t = 0;
+  ra.partials = p.rank.partials;
+  ra.counters = p.rank.counters;
+  ra.splits = p.rank.splits;
+  ra.elt = elt;
+  if ((rc = launch_rank(ra, s))) return rc;
+  if ((rc = launch_segment_rows(sorted_idx, order, p.rank.xa_rows, p.rank.R64, T, r, db, V, true,
+                                dtype, s)))
+    return rc;
+  // dA = (s B[idx])^T . dy on the tensor cores (weight-gradient kernel)
+  if ((rc = launch_gather_rows(idx, b, V, T, r, p.rank.R, nullptr, 0, p.gt, pad8(T), scale, elt, s)))
+    return rc;
+  WgradArgs w;
+  w.big = dy;
+  w.st = p.gt;
+  w.ld_st = pad8(T);
+  w.M = T;
+  w.P = D;
+  w.r = r;
+  w.R = p.rank.R;
+  w.ldb = D;
+  w.out = da;
+  w.ldo = D;
+  w.transposed = true;
+  w.accumulate = accumulate;
+  w.clip = 0.f;
+  w.partials = p.wpart;
+  w.counters = p.wcount;
+  w.splits = p.wsplits;
+  w.elt = elt;
+  return launch_wgrad(&w, 1, s);
+}
+
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {
   if (M <= 0 || K <= 0 || N <= 0) return 0;
   return linear_ws(M, K, N, dtype);

@@ -71,6 +71,8 @@ struct GemmArgs {
   void* d;         // [M, N] stride ldd
   const void* c = nullptr;  // optional addend [M, N] stride ldc, same type as d
   int64_t ldc = 0;
+  const int32_t* c_index = nullptr;  // optional: addend row for output row m = c_index[m]
+  int64_t c_rows = 0;                // rows of the addend table (bound for c_index)
   float acc_scale = 1.f;    // D = acc_scale * (X.W^T + X2.W2^T) + C
   int64_t M, N, K;
   int64_t R = 0;   // extra reduction width, multiple of 16 (0 = none)
@@ -186,6 +188,24 @@ struct WgradArgs {
 };
 int wgrad_splits(int64_t M, int64_t P, int nproblems);
 int launch_wgrad(const WgradArgs* probs, int nprobs, cudaStream_t stream);
+
+// ------------------------------------------------------------ embedding ------
+// g[t, :r] = B[idx[t]] ; gt[:R, t] = scale * B[idx[t]]^T (either may be null).
+int launch_gather_rows(const int32_t* idx, const void* b, int64_t V, int64_t n_tok, int64_t r,
+                       int64_t R, void* g, int64_t ldg, void* gt, int64_t ldgt, float scale,
+                       Elt elt, cudaStream_t s);
+// db[v] (+)= sum of u rows of the tokens with index v (sorted order; deterministic).
+int launch_segment_rows(const int32_t* sorted_idx, const int32_t* order, const void* u,
+                        int64_t ldu, int64_t n_tok, int64_t r, float* db, int64_t V,
+                        bool accumulate, int dtype, cudaStream_t s);
+int launch_embedding_f32(const int32_t* idx, const float* e, const float* a, const float* b,
+                         float* out, int64_t n_tok, int64_t V, int64_t D, int64_t r, float scale,
+                         cudaStream_t s);
+int launch_rows_dot_f32(const float* dy, const float* a, float* u, int64_t n_tok, int64_t D,
+                        int64_t r, float scale, cudaStream_t s);
+int launch_embed_da_f32(const int32_t* idx, const float* b, const float* dy, float* da, int64_t V,
+                        int64_t n_tok, int64_t D, int64_t r, float scale, bool accumulate,
+                        cudaStream_t s);
 
 // ---------------------------------------------------------- elementwise ------
 int launch_transpose_pad(const void* b, int64_t N, int64_t r, int64_t ldb, void* bt, int64_t R,

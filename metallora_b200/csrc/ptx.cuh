@@ -25,6 +25,7 @@ enum DevStatus : uint32_t {
   kDevTimeoutAccEmpty = 0x104,  // MMA waited too long for the epilogue to drain
   kDevTimeoutDrain = 0x105,     // exit path waited too long for in-flight work
   kDevTimeoutReduce = 0x106,    // split reduction waited too long
+  kDevBadIndex = 0x107,         // a gathered row index was outside its table
 };
 
 // Wall-clock budget of one barrier wait before it is declared lost.  Normal

@@ -48,6 +48,8 @@ struct GemmParams {
   long long ldd;
   const void* c;  // optional addend, same type/layout as d (ldc)
   long long ldc;
+  const int32_t* c_index;  // optional: addend row of output row m is c_index[m] (< c_rows)
+  long long c_rows;
   float acc_scale;
   int vec_ok;     // rows of d (and c) allow 16-byte vector access
   uint32_t* status;
@@ -203,6 +205,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_base = (tile % p.tiles_n) * kBN;
       OutT* out_row = reinterpret_cast<OutT*>(p.d) + static_cast<long long>(m) * p.ldd + n_base;
       const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * kBN;
+      // the addend's row: m, or a gathered row (an index outside the table
+      // contributes nothing and is reported in the status word)
+      const OutT* c_row = nullptr;
+      if (p.c != nullptr && m < p.M) {
+        long long cr = m;
+        if (p.c_index != nullptr) {
+          cr = p.c_index[m];
+          if (cr < 0 || cr >= p.c_rows) {
+            record_status(p.status, kDevBadIndex);
+            cr = -1;
+          }
+        }
+        if (cr >= 0) c_row = reinterpret_cast<const OutT*>(p.c) + cr * p.ldc + n_base;
+      }
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
@@ -215,9 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.acc_scale;
           if (!p.vec_ok) {
             // ragged or unaligned rows: element-wise, bounds-checked
-            const OutT* crow = p.c != nullptr ? reinterpret_cast<const OutT*>(p.c) +
-                                                    static_cast<long long>(m) * p.ldc + n0
-                                              : nullptr;
+            const OutT* crow = c_row != nullptr ? c_row + c * 32 : nullptr;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               if (n0 + i < p.N) {
@@ -228,9 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             continue;
           }
-          if (p.c != nullptr) {
-            const OutT* crow = reinterpret_cast<const OutT*>(p.c) +
-                               static_cast<long long>(m) * p.ldc + n0;
+          if (c_row != nullptr) {
+            const OutT* crow = c_row + c * 32;
             if constexpr (sizeof(OutT) == 2) {
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
@@ -321,6 +334,8 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.ldd = a.ldd;
   p.c = a.c;
   p.ldc = a.ldc;
+  p.c_index = a.c_index;
+  p.c_rows = a.c_rows;
   p.acc_scale = a.acc_scale;
   {
     const int64_t vec = 16 / static_cast<int64_t>(sizeof(OutT));

@@ -402,3 +402,62 @@ def multi_lora_fwd(x2d: torch.Tensor, w0: torch.Tensor | None, a_stack: torch.Te
                                       code, _ptr(ws), ws.numel(), _stream())
     _lib.check(st, "mlora_multi_lora_forward")
     return y
+
+
+# ------------------------------------------------------------ embedding --
+
+def _as_idx(indices: torch.Tensor) -> torch.Tensor:
+    return indices.reshape(-1).to(torch.int32).contiguous()
+
+
+def lora_embedding_fwd(indices: torch.Tensor, table: torch.Tensor, a: torch.Tensor,
+                       b: torch.Tensor, alpha: float) -> torch.Tensor:
+    """table[idx] + (alpha/r) b[idx].a for every index (LoRAEmbedding.__call__,
+    layers.py:220-225); returns [*indices.shape, D]."""
+    _need_cuda(indices, table, a, b)
+    V, D = table.shape
+    r = a.shape[0]
+    _check_2d("A", a, (r, D), table.dtype)
+    _check_2d("B", b, (V, r), table.dtype)
+    idx = _as_idx(indices)
+    T = idx.numel()
+    lib = _lib.load()
+    code = _dtype_code(table)
+    out = torch.empty((T, D), dtype=table.dtype, device=table.device)
+    ws = _workspace(lib.mlora_lora_embedding_workspace_bytes(T, D, r, code, 0), table.device)
+    st = lib.mlora_lora_embedding_forward(_ptr(idx), _ptr(table.contiguous()), _ptr(a.contiguous()),
+                                          _ptr(b.contiguous()), _ptr(out), T, V, D, r, float(alpha),
+                                          code, _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_lora_embedding_forward")
+    return out.reshape(*indices.shape, D)
+
+
+def lora_embedding_bwd(dy: torch.Tensor, indices: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                       alpha: float, da_out: torch.Tensor | None = None,
+                       db_out: torch.Tensor | None = None):
+    """fp32 (dA [r, D], dB [V, r]) of the LoRA embedding; dB rows are summed over
+    each index's tokens in token order (deterministic).  With da_out/db_out the
+    gradients are added into them."""
+    _need_cuda(dy, indices, a, b)
+    V, r = b.shape
+    D = a.shape[1]
+    idx = _as_idx(indices)
+    T = idx.numel()
+    dy2 = dy.reshape(T, D).contiguous()
+    sorted_idx, order = torch.sort(idx, stable=True)
+    order = order.to(torch.int32)
+    lib = _lib.load()
+    code = _dtype_code(dy2)
+    flags = 0
+    if da_out is not None and db_out is not None:
+        da, db, flags = da_out, db_out, _lib.BWD_ACCUMULATE
+    else:
+        da = torch.empty((r, D), dtype=torch.float32, device=dy.device)
+        db = torch.empty((V, r), dtype=torch.float32, device=dy.device)
+    ws = _workspace(lib.mlora_lora_embedding_workspace_bytes(T, D, r, code, 1), dy.device)
+    st = lib.mlora_lora_embedding_backward(_ptr(dy2), _ptr(idx), _ptr(sorted_idx), _ptr(order),
+                                           _ptr(a.contiguous()), _ptr(b.contiguous()), _ptr(da),
+                                           _ptr(db), T, V, D, r, float(alpha), code, flags,
+                                           _ptr(ws), ws.numel(), _stream())
+    _lib.check(st, "mlora_lora_embedding_backward")
+    return da, db

@@ -173,3 +173,58 @@ class LoRALinear(nn.Module):
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"rank={self.rank}, alpha={self.alpha}, merged={self.merged}")
+
+
+class _LoRAEmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, indices, table, a, b, alpha):
+        ctx.save_for_backward(indices, a, b)
+        ctx.alpha = alpha
+        return _k.lora_embedding_fwd(indices, table, a, b, alpha)
+
+    @staticmethod
+    def backward(ctx, dy):
+        indices, a, b = ctx.saved_tensors
+        da, db = _k.lora_embedding_bwd(dy, indices, a, b, ctx.alpha)
+        return None, None, da.to(a.dtype), db.to(b.dtype), None
+
+
+class LoRAEmbedding(nn.Module):
+    """Embedding with a LoRA delta (layers.py:194-230):
+    ``out = E[idx] + (alpha/rank) * B[idx] . A`` with E [num_embeddings, dim]
+    (frozen when ``freeze_base``), A [rank, dim] ~ U(+-1/sqrt(dim)), B
+    [num_embeddings, rank] = 0, E ~ N(0, 0.02^2) -- the reference's
+    initialisation (:207-213).  The forward gathers on the tensor cores
+    (16-bit) or CUDA cores (fp32); gradients flow to A and B only."""
+
+    def __init__(self, num_embeddings: int, embedding_dim: int, rank: int = 8,
+                 alpha: float = 16.0, freeze_base: bool = True, device=None, dtype=None):
+        super().__init__()
+        if num_embeddings <= 0 or embedding_dim <= 0:
+            raise ConfigurationError("num_embeddings and embedding_dim must be positive")
+        validate_rank(rank)
+        validate_alpha(alpha)
+        self.num_embeddings = num_embeddings
+        self.embedding_dim = embedding_dim
+        self.rank = rank
+        self.alpha = alpha
+        fk = {"device": device, "dtype": dtype}
+        self.embeddings = nn.Parameter(torch.randn((num_embeddings, embedding_dim), **fk) * 0.02,
+                                       requires_grad=not freeze_base)
+        bound = 1.0 / math.sqrt(embedding_dim)
+        self.A = nn.Parameter(torch.empty((rank, embedding_dim), **fk).uniform_(-bound, bound))
+        self.B = nn.Parameter(torch.zeros((num_embeddings, rank), **fk))
+
+    @property
+    def scale(self) -> float:
+        return self.alpha / self.rank
+
+    def forward(self, indices: torch.Tensor) -> torch.Tensor:
+        if self.embeddings.requires_grad:
+            raise ConfigurationError("LoRAEmbedding trains A and B only (freeze_base=True)")
+        return _LoRAEmbeddingFn.apply(indices, self.embeddings, self.A, self.B, float(self.alpha))
+
+    @torch.no_grad()
+    def merge_weights(self) -> torch.Tensor:
+        """layers.py:227-230: E + (alpha/rank) B.A."""
+        return _k.merge(self.embeddings, self.A, self.B, float(self.alpha))

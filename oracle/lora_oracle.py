@@ -167,3 +167,25 @@ def multi_adapter_forward(x, W0, A_all, B_all, ids, alpha, dtype=np.float64):  #
             y = x[b] @ np.asarray(W0, dtype).T + y
         out.append(y)
     return np.stack(out)
+
+
+def embedding_forward(idx, E, A, B, alpha, dtype=np.float64):  # noqa: N803
+    """LoRAEmbedding.__call__ (python/metal_lora/layers.py:220-225):
+    base_emb = E[idx]; lora_emb = B[idx] @ A; out = base_emb + (alpha/rank) lora_emb.
+    E [V, D], A [rank, D], B [V, rank]."""
+    E, A, B = (np.asarray(t, dtype) for t in (E, A, B))
+    idx = np.asarray(idx)
+    return E[idx] + (alpha / A.shape[0]) * (B[idx] @ A)
+
+
+def embedding_backward(dy, idx, A, B, alpha, dtype=np.float64):  # noqa: N803
+    """Gradients of embedding_forward with respect to A and B (the table is
+    frozen, layers.py:217-218): dA = s B[idx]^T dy, dB[v] = s sum_{t: idx=v} dy[t] A^T."""
+    A, B = np.asarray(A, dtype), np.asarray(B, dtype)
+    idx = np.asarray(idx).reshape(-1)
+    dy = np.asarray(dy, dtype).reshape(idx.size, -1)
+    s = alpha / A.shape[0]
+    dA = s * (B[idx].T @ dy)
+    dB = np.zeros_like(B)
+    np.add.at(dB, idx, s * (dy @ A.T))
+    return dA, dB
