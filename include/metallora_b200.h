@@ -286,6 +286,27 @@ MLORA_API int mlora_multi_lora_forward(const void* x, const void* w0, const void
                                        float alpha, int dtype, void* workspace,
                                        size_t workspace_bytes, void* stream);
 
+/* ---- KV-cache update (incremental decoding) ----------------------------- */
+
+/* One new token per sequence: for b < batch,
+ *   k_cache[b, cur_pos, :] = x[b] . wk^T + (alpha/r) (x[b] . ak^T) . bk^T
+ *   v_cache[b, cur_pos, :] = x[b] . wv^T + (alpha/r) (x[b] . av^T) . bv^T
+ * x [batch, D_in]; wk, wv [D_kv, D_in]; ak, av [r, D_in]; bk, bv [D_kv, r];
+ * caches [batch, max_seq, D_kv] (D_kv = heads * head_dim), BF16/F16.  Each
+ * projection writes its rows straight into the cache slot (decode kernel for
+ * up to 16 sequences, tcgen05 GEMM above).  Replaces lora_kv_cache_update
+ * (kernels/lora_kernels.metal:514-586; max_seq is a parameter here, not 8192)
+ * with LoRAKVCache.update (python/metal_lora/optimizations.py:327-336). */
+MLORA_API size_t mlora_lora_kv_cache_workspace_bytes(int64_t batch, int64_t D_in, int64_t D_kv,
+                                                     int64_t r, int dtype);
+MLORA_API int mlora_lora_kv_cache_update(const void* x, const void* wk, const void* wv,
+                                         const void* ak, const void* bk, const void* av,
+                                         const void* bv, void* k_cache, void* v_cache,
+                                         int64_t batch, int64_t cur_pos, int64_t max_seq,
+                                         int64_t D_in, int64_t D_kv, int64_t r, float alpha,
+                                         int dtype, void* workspace, size_t workspace_bytes,
+                                         void* stream);
+
 /* ---- LoRA embedding ----------------------------------------------------- */
 
 /* out[t, :] = table[idx[t], :] + (alpha/r) * b[idx[t], :] . a  (LoRAEmbedding.__call__,

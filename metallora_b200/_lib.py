@@ -73,6 +73,8 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_qlora_prepared_scales_bytes": (sz, [i32, i64, i64, i64]),
     "mlora_multi_lora_forward_workspace_bytes": (sz, [i64, i64, i64, i64, i64, i32]),
     "mlora_lora_embedding_workspace_bytes": (sz, [i64, i64, i64, i32, i32]),
+    "mlora_lora_kv_cache_workspace_bytes": (sz, [i64, i64, i64, i64, i32]),
+    "mlora_lora_kv_cache_update": (i32, [vp] * 9 + [i64] * 6 + [f32, i32, vp, sz, vp]),
     "mlora_lora_embedding_forward": (i32, [vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, i32, vp,
                                            sz, vp]),
     "mlora_lora_embedding_backward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64,

@@ -314,7 +314,7 @@ GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int sch
 int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
              int64_t group, const void* a, const void* b, void* y, int64_t M, int64_t K,
              int64_t N, int64_t r, float alpha, void* workspace, size_t workspace_bytes,
-             cudaStream_t s) {
+             cudaStream_t s, int64_t ldy = 0) {
   const GemvPlan need = plan_gemv(nullptr, M, K, N, r, scheme);
   if (workspace == nullptr || workspace_bytes < need.bytes)
     return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
@@ -346,6 +346,7 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
   g.r = r;
   g.group = group;
   g.splits = p.splits;
+  g.ldy = ldy;
   return launch_gemv(g, s);
 }
 
@@ -803,26 +804,16 @@ size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64
   return bytes;
 }
 
-int mlora_lora_forward(const void* x, const void* w0, const void* a, const void* b, void* y,
-                       void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
-                       int dtype, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_shapes(M, K, N, r, dtype, false);
-  if (rc) return rc;
-  if (!x || !w0 || !a || !b || !y) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
-  if (!aligned16(x) || !aligned16(w0) || !aligned16(a) || !aligned16(b) || !aligned16(y) ||
-      (saved_xa && !aligned16(saved_xa)))
-    return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
-  if ((rc = check_device())) return rc;
-  if (dtype == MLORA_DTYPE_F32) {
-    if (saved_xa) return fail(MLORA_ERR_UNSUPPORTED, "saved_xa is not produced for F32");
-    return lora_forward_f32(static_cast<const float*>(x), static_cast<const float*>(w0),
-                            static_cast<const float*>(a), static_cast<const float*>(b),
-                            static_cast<float*>(y), M, K, N, r, alpha, workspace, workspace_bytes,
-                            static_cast<cudaStream_t>(stream));
-  }
+namespace {
+// 16-bit LoRA forward (decode kernel for <= 16 tokens without saved_xa, else
+// rank kernel + tcgen05 GEMM) writing y rows with stride ldy.
+int lora_forward16(const void* x, const void* w0, const void* a, const void* b, void* y,
+                   int64_t ldy, void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r,
+                   float alpha, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
   if (saved_xa == nullptr && use_gemv(M, K, dtype))
     return run_gemv(0, x, w0, nullptr, 64, a, b, y, M, K, N, r, alpha, workspace,
-                    workspace_bytes, static_cast<cudaStream_t>(stream));
+                    workspace_bytes, static_cast<cudaStream_t>(stream), ldy);
   const FwdPlan need = plan_forward(nullptr, M, K, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
     return fail(MLORA_ERR_WORKSPACE, "forward workspace needs " + std::to_string(need.bytes) + " bytes");
@@ -868,11 +859,33 @@ int mlora_lora_forward(const void* x, const void* w0, const void* a, const void*
   ga.ldw = K;
   ga.ldx2 = p.R64;
   ga.ldw2 = r;
-  ga.ldd = N;
+  ga.ldd = ldy;
   ga.w_mn_major = false;
   ga.elt = elt;
   ga.out_dtype = dtype;
   return launch_gemm(ga, s);
+}
+}  // namespace
+
+int mlora_lora_forward(const void* x, const void* w0, const void* a, const void* b, void* y,
+                       void* saved_xa, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                       int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shapes(M, K, N, r, dtype, false);
+  if (rc) return rc;
+  if (!x || !w0 || !a || !b || !y) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(x) || !aligned16(w0) || !aligned16(a) || !aligned16(b) || !aligned16(y) ||
+      (saved_xa && !aligned16(saved_xa)))
+    return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  if ((rc = check_device())) return rc;
+  if (dtype == MLORA_DTYPE_F32) {
+    if (saved_xa) return fail(MLORA_ERR_UNSUPPORTED, "saved_xa is not produced for F32");
+    return lora_forward_f32(static_cast<const float*>(x), static_cast<const float*>(w0),
+                            static_cast<const float*>(a), static_cast<const float*>(b),
+                            static_cast<float*>(y), M, K, N, r, alpha, workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
+  }
+  return lora_forward16(x, w0, a, b, y, N, saved_xa, M, K, N, r, alpha, dtype, workspace,
+                        workspace_bytes, stream);
 }
 
 size_t mlora_lora_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype) {
@@ -1555,6 +1568,37 @@ int mlora_lora_embedding_backward(const void* dy, const int32_t* idx, const int3
   w.splits = p.wsplits;
   w.elt = elt;
   return launch_wgrad(&w, 1, s);
+}
+
+size_t mlora_lora_kv_cache_workspace_bytes(int64_t batch, int64_t D_in, int64_t D_kv, int64_t r,
+                                           int dtype) {
+  return mlora_lora_forward_workspace_bytes(batch, D_in, D_kv, r, dtype);
+}
+
+int mlora_lora_kv_cache_update(const void* x, const void* wk, const void* wv, const void* ak,
+                               const void* bk, const void* av, const void* bv, void* k_cache,
+                               void* v_cache, int64_t batch, int64_t cur_pos, int64_t max_seq,
+                               int64_t D_in, int64_t D_kv, int64_t r, float alpha, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != MLORA_DTYPE_BF16 && dtype != MLORA_DTYPE_F16)
+    return fail(MLORA_ERR_UNSUPPORTED, "KV-cache update takes BF16 or F16");
+  int rc = check_shapes(batch, D_in, D_kv, r, dtype, false);
+  if (rc) return rc;
+  if (D_kv % 8) return fail(MLORA_ERR_UNSUPPORTED, "KV width must be a multiple of 8");
+  if (max_seq <= 0 || cur_pos < 0 || cur_pos >= max_seq)
+    return fail(MLORA_ERR_INVALID_ARG, "cur_pos must be in [0, max_seq)");
+  if (!x || !wk || !wv || !ak || !bk || !av || !bv || !k_cache || !v_cache)
+    return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if ((rc = check_ptrs16({x, wk, wv, ak, bk, av, bv, k_cache, v_cache, workspace}))) return rc;
+  if ((rc = check_device())) return rc;
+  // row b of the new K (V) is cache[b, cur_pos, :]: row stride max_seq * D_kv
+  const int64_t ld = max_seq * D_kv;
+  const size_t off = static_cast<size_t>(cur_pos) * D_kv * 2;
+  if ((rc = lora_forward16(x, wk, ak, bk, static_cast<uint8_t*>(k_cache) + off, ld, nullptr, batch,
+                           D_in, D_kv, r, alpha, dtype, workspace, workspace_bytes, stream)))
+    return rc;
+  return lora_forward16(x, wv, av, bv, static_cast<uint8_t*>(v_cache) + off, ld, nullptr, batch,
+                        D_in, D_kv, r, alpha, dtype, workspace, workspace_bytes, stream);
 }
 
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {

@@ -80,6 +80,7 @@ struct DecParams {
   uint32_t* counters;      // [row blocks]
   int M, N, K, r, group, gps;  // gps: scale-table groups per stage box
   int splits, kspan, items, row_blocks;
+  long long ldy;  // row stride of y
   uint32_t* status;
 };
 
@@ -529,10 +530,10 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
             const int m0 = nt * 8 + 2 * q;
             if (m0 >= p.M) continue;
             const float r0 = have_rt ? rt[m0 * kDecRows + row] : 0.f;
-            p.y[static_cast<long long>(m0) * p.N + n] = __float2bfloat16_rn(acc[t][nt][2 * h] + r0);
+            p.y[static_cast<long long>(m0) * p.ldy + n] = __float2bfloat16_rn(acc[t][nt][2 * h] + r0);
             if (m0 + 1 < p.M) {
               const float r1 = have_rt ? rt[(m0 + 1) * kDecRows + row] : 0.f;
-              p.y[static_cast<long long>(m0 + 1) * p.N + n] =
+              p.y[static_cast<long long>(m0 + 1) * p.ldy + n] =
                   __float2bfloat16_rn(acc[t][nt][2 * h + 1] + r1);
             }
           }
@@ -598,7 +599,7 @@ __global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBloc
       if (p.b != nullptr) add_rank_term(p.b + static_cast<long long>(n) * p.r, sts, p.M, p.r, out);
 #pragma unroll
       for (int m = 0; m < kMaxTok; ++m)
-        if (m < p.M) p.y[static_cast<long long>(m) * p.N + n] = __float2bfloat16_rn(out[m]);
+        if (m < p.M) p.y[static_cast<long long>(m) * p.ldy + n] = __float2bfloat16_rn(out[m]);
     }
   }
 }
@@ -729,6 +730,7 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   p.kspan = cfg.kspan;
   p.row_blocks = static_cast<int>(gemv_row_blocks(a.N));
   p.items = p.row_blocks * cfg.splits;
+  p.ldy = a.ldy > 0 ? a.ldy : a.N;
   p.status = device_status_ptr();
   const size_t smem = static_cast<size_t>(cfg.smem);
   auto kern = lora_decode_kernel<kScheme, kNT>;

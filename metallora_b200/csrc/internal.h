@@ -118,6 +118,7 @@ struct GemvArgs {
   float* partials = nullptr;     // [splits, M, N]
   uint32_t* counters = nullptr;  // [gemv_row_blocks(N)] zeroed
   int64_t M = 0, N = 0, K = 0, r = 0, group = 64;
+  int64_t ldy = 0;  // row stride of y (0: N)
   int splits = 1;
 };
 constexpr int64_t kGemvMaxTokens = 16;

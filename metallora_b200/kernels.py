@@ -461,3 +461,39 @@ def lora_embedding_bwd(dy: torch.Tensor, indices: torch.Tensor, a: torch.Tensor,
                                            _ptr(ws), ws.numel(), _stream())
     _lib.check(st, "mlora_lora_embedding_backward")
     return da, db
+
+
+# ------------------------------------------------------- KV-cache update --
+
+def lora_kv_cache_update(x2d: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, ak: torch.Tensor,
+                         bk: torch.Tensor, av: torch.Tensor, bv: torch.Tensor,
+                         k_cache: torch.Tensor, v_cache: torch.Tensor, cur_pos: int,
+                         alpha: float) -> None:
+    """Projects one new token per sequence through the K and V LoRA linears and
+    writes the rows straight into k_cache/v_cache [batch, max_seq, ...] at
+    position cur_pos (lora_kv_cache_update, kernels/lora_kernels.metal:514-586)."""
+    _need_cuda(x2d, wk, wv, ak, bk, av, bv, k_cache, v_cache)
+    batch, D_in = x2d.shape
+    D_kv = wk.shape[0]
+    max_seq = k_cache.shape[1]
+    if k_cache.shape[0] != batch or k_cache[0, 0].numel() != D_kv or v_cache.shape != k_cache.shape:
+        raise ShapeError("caches must be [batch, max_seq, D_kv] (trailing dims may be heads, dim)")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ShapeError("caches must be contiguous")
+    r_orig = ak.shape[0]
+    ak, bk, alpha_k, r = _pad_rank(ak, bk, alpha)
+    av, bv, _, _ = _pad_rank(av, bv, alpha)
+    for name, t, shape in (("W_K", wk, (D_kv, D_in)), ("W_V", wv, (D_kv, D_in)),
+                           ("A_K", ak, (r, D_in)), ("A_V", av, (r, D_in)),
+                           ("B_K", bk, (D_kv, r)), ("B_V", bv, (D_kv, r))):
+        _check_2d(name, t, shape, x2d.dtype)
+    del r_orig
+    lib = _lib.load()
+    code = _dtype_code(x2d)
+    ws = _workspace(lib.mlora_lora_kv_cache_workspace_bytes(batch, D_in, D_kv, r, code), x2d.device)
+    st = lib.mlora_lora_kv_cache_update(
+        _ptr(x2d.contiguous()), _ptr(wk.contiguous()), _ptr(wv.contiguous()), _ptr(ak.contiguous()),
+        _ptr(bk.contiguous()), _ptr(av.contiguous()), _ptr(bv.contiguous()), _ptr(k_cache),
+        _ptr(v_cache), batch, int(cur_pos), max_seq, D_in, D_kv, r, float(alpha_k), code, _ptr(ws),
+        ws.numel(), _stream())
+    _lib.check(st, "mlora_lora_kv_cache_update")

@@ -1,7 +1,8 @@
-"""Batched inference with several LoRA adapters (python/metal_lora/optimizations.py:129-220).
+"""Batched inference with several LoRA adapters and a LoRA KV cache
+(python/metal_lora/optimizations.py:129-220, :307-340).
 
-Only ``MultiAdapterManager`` is on the LoRA-linear path; the reference
-module's compression, memory pool, speculative decoding, KV cache, lazy
+``MultiAdapterManager`` and ``LoRAKVCache`` are on the LoRA-linear path; the
+reference module's compression, memory pool, speculative decoding, lazy
 loading and mixed-precision trainer are not part of this package.
 """
 from __future__ import annotations
@@ -85,3 +86,52 @@ class MultiAdapterManager:
         y = multi_adapter_forward(x.to(self.dtype), None, self.batched_a, self.batched_b, slots,
                                   alpha=float(r))
         return y.to(x.dtype)
+
+
+class LoRAKVCache:
+    """KV cache for incremental LoRA decoding (optimizations.py:307-340): caches
+    [batch, max_seq_len, num_heads, head_dim]; ``update`` appends K/V rows,
+    ``project_and_update`` computes them from the new tokens with the K and V
+    LoRALinear layers in one fused call that writes into the cache slot
+    (kernels/lora_kernels.metal:514-586)."""
+
+    def __init__(self, batch_size: int, max_seq_len: int, num_heads: int, head_dim: int,
+                 dtype: torch.dtype = torch.float16, device=None):
+        self.batch_size = batch_size
+        self.max_seq_len = max_seq_len
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        shape = (batch_size, max_seq_len, num_heads, head_dim)
+        self.k_cache = torch.zeros(shape, dtype=dtype, device=device)
+        self.v_cache = torch.zeros(shape, dtype=dtype, device=device)
+        self.cur_pos = 0
+
+    def update(self, k_new: torch.Tensor, v_new: torch.Tensor):
+        """optimizations.py:327-336: write [batch, seq, heads, dim] at cur_pos."""
+        seq_len = k_new.shape[1]
+        end_pos = self.cur_pos + seq_len
+        if end_pos > self.max_seq_len:
+            raise ValueError(f"cache full: {end_pos} > {self.max_seq_len}")
+        self.k_cache[:, self.cur_pos:end_pos] = k_new
+        self.v_cache[:, self.cur_pos:end_pos] = v_new
+        self.cur_pos = end_pos
+        return self.k_cache[:, :end_pos], self.v_cache[:, :end_pos]
+
+    def project_and_update(self, x: torch.Tensor, k_proj, v_proj):
+        """x [batch, 1, D_in] (one new token per sequence); k_proj/v_proj are
+        unmerged LoRALinear layers with dense bases and equal rank and alpha."""
+        from .kernels import lora_kv_cache_update
+        if self.cur_pos >= self.max_seq_len:
+            raise ValueError("cache full")
+        if k_proj.rank != v_proj.rank or k_proj.alpha != v_proj.alpha:
+            raise ValueError("K and V projections must share rank and alpha")
+        dt = self.k_cache.dtype
+        x2d = x.reshape(self.batch_size, -1).to(dt)
+        lora_kv_cache_update(x2d, k_proj.W0.to(dt), v_proj.W0.to(dt), k_proj.A.to(dt),
+                             k_proj.B.to(dt), v_proj.A.to(dt), v_proj.B.to(dt), self.k_cache,
+                             self.v_cache, self.cur_pos, k_proj.alpha)
+        self.cur_pos += 1
+        return self.k_cache[:, :self.cur_pos], self.v_cache[:, :self.cur_pos]
+
+    def reset(self) -> None:
+        self.cur_pos = 0
