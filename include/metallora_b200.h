@@ -72,7 +72,7 @@ MLORA_API int mlora_device_supported(int device);
 /* Reads (and with reset != 0 clears) the status word of the current device.
  * *out = 0 when no kernel has recorded a fault: 0x101-0x106 a bounded wait
  * timed out (the kernel gave up instead of hanging); 0x107 a gathered row
- * index was outside its table.  Synchronous. */
+ * index was outside its table; 0x108 a peer GPU missed a barrier.  Synchronous. */
 MLORA_API int mlora_device_status(uint32_t* out, int reset);
 
 /* ---- measurement ------------------------------------------------------- */
@@ -306,6 +306,23 @@ MLORA_API int mlora_lora_kv_cache_update(const void* x, const void* wk, const vo
                                          int64_t D_in, int64_t D_kv, int64_t r, float alpha,
                                          int dtype, void* workspace, size_t workspace_bytes,
                                          void* stream);
+
+/* ---- data-parallel gradient exchange ----------------------------------- */
+
+/* out = scale * sum over ranks of their fp32 buffers [n], in rank order (the
+ * same bits on every rank), in one kernel over NVLink peer memory.  bufs and
+ * flags are DEVICE arrays of `world` pointers: each rank's buffer and its
+ * `world`-word flag array, both in memory every rank can address (e.g.
+ * symmetric memory); flags start at 0; seq counts calls from 1; counter is one
+ * zeroed device word owned by the caller.  Every rank calls it once per step
+ * on its own GPU; when it completes no peer reads this rank's buffer any more.
+ * A peer that does not arrive within 2 s sets status 0x108 (no hang).
+ * Replaces the NCCL all-reduce of the LoRA gradients for small buffers (the
+ * reference has no multi-device path: python/metal_lora/trainer.py:228-249 is
+ * single-device). */
+MLORA_API int mlora_peer_allreduce(const void* bufs, const void* flags, int rank, int world,
+                                   uint32_t seq, float* out, int64_t n, float scale,
+                                   uint32_t* counter, void* stream);
 
 /* ---- LoRA embedding ----------------------------------------------------- */
 

@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple] = {
     "mlora_multi_lora_forward_workspace_bytes": (sz, [i64, i64, i64, i64, i64, i32]),
     "mlora_lora_embedding_workspace_bytes": (sz, [i64, i64, i64, i32, i32]),
     "mlora_lora_kv_cache_workspace_bytes": (sz, [i64, i64, i64, i64, i32]),
+    "mlora_peer_allreduce": (i32, [vp, vp, i32, i32, C.c_uint32, vp, i64, f32, vp, vp]),
     "mlora_lora_kv_cache_update": (i32, [vp] * 9 + [i64] * 6 + [f32, i32, vp, sz, vp]),
     "mlora_lora_embedding_forward": (i32, [vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, i32, vp,
                                            sz, vp]),

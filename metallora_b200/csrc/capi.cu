@@ -541,11 +541,11 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
   const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
   const float scale = alpha / static_cast<float>(r);
 
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
-  if (e != cudaSuccess) return fail(MLORA_ERR_CUDA, std::string("memset: ") + cudaGetErrorString(e));
-
-  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection.
-  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s))) return rc;
+  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection;
+  // the same launch zeroes the split counters of the kernels below.
+  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s, p.counters,
+                                 static_cast<int64_t>(p.counter_bytes / 4))))
+    return rc;
 
   RankArgs ra;
   ra.x = dy;
@@ -1599,6 +1599,21 @@ int mlora_lora_kv_cache_update(const void* x, const void* wk, const void* wv, co
     return rc;
   return lora_forward16(x, wv, av, bv, static_cast<uint8_t*>(v_cache) + off, ld, nullptr, batch,
                         D_in, D_kv, r, alpha, dtype, workspace, workspace_bytes, stream);
+}
+
+int mlora_peer_allreduce(const void* bufs, const void* flags, int rank, int world,
+                         uint32_t seq, float* out, int64_t n, float scale, uint32_t* counter,
+                         void* stream) {
+  if (!bufs || !flags || !out || !counter) return fail(MLORA_ERR_INVALID_ARG, "NULL pointer");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(MLORA_ERR_INVALID_ARG, "rank must be in [0, world), world in [1, 64]");
+  if (seq == 0) return fail(MLORA_ERR_INVALID_ARG, "seq starts at 1");
+  if (n <= 0) return fail(MLORA_ERR_INVALID_ARG, "n must be positive");
+  int rc;
+  if ((rc = check_ptrs16({out}))) return rc;
+  if ((rc = check_device())) return rc;
+  return launch_peer_allreduce(bufs, flags, rank, world, seq, out, n, scale, counter,
+                               static_cast<cudaStream_t>(stream));
 }
 
 size_t mlora_linear_workspace_bytes(int64_t M, int64_t K, int64_t N, int dtype) {

@@ -190,6 +190,13 @@ struct WgradArgs {
 int wgrad_splits(int64_t M, int64_t P, int nproblems);
 int launch_wgrad(const WgradArgs* probs, int nprobs, cudaStream_t stream);
 
+// ---------------------------------------------------------------- peers ------
+// One-shot all-reduce over peer memory (see peer.cu); counter: one zeroed
+// device word per communicator, reset by the kernel.
+int launch_peer_allreduce(const void* bufs_dev, const void* flags_dev, int rank, int world,
+                          uint32_t seq, float* out, int64_t n, float scale, uint32_t* counter,
+                          cudaStream_t s);
+
 // ------------------------------------------------------------ embedding ------
 // g[t, :r] = B[idx[t]] ; gt[:R, t] = scale * B[idx[t]]^T (either may be null).
 int launch_gather_rows(const int32_t* idx, const void* b, int64_t V, int64_t n_tok, int64_t r,
@@ -209,8 +216,10 @@ int launch_embed_da_f32(const int32_t* idx, const float* b, const float* dy, flo
                         cudaStream_t s);
 
 // ---------------------------------------------------------- elementwise ------
+// Also zeroes zero[0, n_zero) (split counters of the kernels that follow).
 int launch_transpose_pad(const void* b, int64_t N, int64_t r, int64_t ldb, void* bt, int64_t R,
-                         Elt elt, cudaStream_t stream);
+                         Elt elt, cudaStream_t stream, uint32_t* zero = nullptr,
+                         int64_t n_zero = 0);
 
 // Split-precision (bf16 hi/lo) copies of fp32 tensors; pattern bit s = 1 puts
 // the lo part in segment s.  Patterns: kHHL = (hi, hi, lo), kHLH = (hi, lo, hi).

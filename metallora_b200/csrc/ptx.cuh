@@ -26,6 +26,7 @@ enum DevStatus : uint32_t {
   kDevTimeoutDrain = 0x105,     // exit path waited too long for in-flight work
   kDevTimeoutReduce = 0x106,    // split reduction waited too long
   kDevBadIndex = 0x107,         // a gathered row index was outside its table
+  kDevPeerTimeout = 0x108,      // a peer GPU did not reach a barrier in time
 };
 
 // Wall-clock budget of one barrier wait before it is declared lost.  Normal

@@ -422,14 +422,24 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (split_reduce<R>(acc, q.partials, q.counters, tile, w.split, q.splits, prow, q.P, flag) &&
         prow < q.P) {
       const bool clip = q.clip > 0.f;
+      const long long step_j = q.transposed ? q.ldo : 1;
+      float* const row = q.transposed ? q.out + prow : q.out + prow * q.ldo;
+      if (q.accumulate) {  // all old values loaded before any store: one round trip
+        float prev[R];
 #pragma unroll
-      for (int j = 0; j < R; ++j) {
-        if (j < q.r) {
+        for (int j = 0; j < R; ++j) prev[j] = j < q.r ? row[j * step_j] : 0.f;
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
           float v = acc[j];
           if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
-          float* dst = q.transposed ? q.out + static_cast<long long>(j) * q.ldo + prow
-                                    : q.out + prow * q.ldo + j;
-          *dst = q.accumulate ? *dst + v : v;
+          if (j < q.r) row[j * step_j] = prev[j] + v;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+          float v = acc[j];
+          if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
+          if (j < q.r) row[j * step_j] = v;
         }
       }
     }

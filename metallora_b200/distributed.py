@@ -51,3 +51,69 @@ def replicas_in_sync(t: torch.Tensor, group=None) -> bool:
     out = [torch.zeros_like(chk) for _ in range(dist.get_world_size(group))]
     dist.all_gather(out, chk, group=group)
     return all(torch.equal(o, out[0]) for o in out)
+
+
+class PeerAllReduce:
+    """Averages one small fp32 buffer over the ranks with a single kernel that
+    reads the peers' copies over NVLink (``mlora_peer_allreduce``): a flag
+    barrier, an in-rank-order sum (bitwise identical on every rank) and a
+    closing barrier, so ``buffer`` may be overwritten once the call's kernel has
+    run.  ``buffer`` (and the flags) live in symmetric memory; gradients are
+    accumulated straight into it.  One-shot reads (world - 1) x the buffer per
+    rank, so it is used for buffers up to ``MAX_BYTES``; larger ones, and
+    process groups without symmetric memory, keep NCCL (``create`` returns None).
+    """
+
+    MAX_BYTES = 8 << 20
+
+    def __init__(self, numel: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+        self._lib = _lib
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.numel = int(numel)
+        dev = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.buffer = symm_mem.empty(self.numel, dtype=torch.float32, device=dev)
+        self.flags = symm_mem.empty(max(self.world, 4), dtype=torch.int32, device=dev)
+        self.buffer.zero_()
+        self.flags.zero_()
+        # every rank's flags are zero before any rank can raise one
+        torch.cuda.synchronize(dev)
+        name = self.group.group_name
+        self._hb = symm_mem.rendezvous(self.buffer, name)
+        self._hf = symm_mem.rendezvous(self.flags, name)
+        dist.barrier(self.group)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.seq = 0
+
+    @classmethod
+    def create(cls, numel: int, group=None, device=None) -> "PeerAllReduce | None":
+        """A peer all-reduce for this group, or None where it does not apply."""
+        if not (dist.is_available() and dist.is_initialized()) or not torch.cuda.is_available():
+            return None
+        g = group if group is not None else dist.group.WORLD
+        if dist.get_world_size(g) < 2 or dist.get_backend(g) != "nccl":
+            return None
+        if numel * 4 > cls.MAX_BYTES:
+            return None
+        try:
+            return cls(numel, g, device)
+        except Exception:  # no peer access / symmetric memory on this system
+            return None
+
+    def allreduce(self, out: torch.Tensor, average: bool = True) -> torch.Tensor:
+        """out = mean (or sum) over ranks of ``buffer``; out is a separate
+        contiguous fp32 tensor of ``numel`` elements on this GPU."""
+        if out.dtype != torch.float32 or out.numel() != self.numel or not out.is_contiguous():
+            raise ValueError("out must be a contiguous fp32 tensor of the buffer's size")
+        self.seq += 1
+        st = self._lib.load().mlora_peer_allreduce(
+            self._hb.buffer_ptrs_dev, self._hf.buffer_ptrs_dev, self.rank, self.world, self.seq,
+            out.data_ptr(), self.numel, (1.0 / self.world) if average else 1.0,
+            self.counter.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        self._lib.check(st, "mlora_peer_allreduce")
+        return out

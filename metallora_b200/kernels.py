@@ -121,13 +121,14 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
                     a: torch.Tensor, b: torch.Tensor, alpha: float,
                     saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
                     need_dx: bool = True, da_out: torch.Tensor | None = None,
-                    db_out: torch.Tensor | None = None):
+                    db_out: torch.Tensor | None = None, accumulate: bool = True):
     """(dx, dA, dB) of the LoRA linear for 2-D dy [M, N], x [M, K].
 
     dA/dB are fp32 (master-gradient precision); clip_value > 0 clips them
     elementwise after the full reduction (ops.py:155).  With ``da_out`` and
     ``db_out`` (contiguous fp32 [r, K] / [N, r], rank a multiple of 8) the
-    gradients are ADDED into those buffers and returned."""
+    gradients are ADDED into those buffers (written over them when
+    ``accumulate`` is False) and returned."""
     _need_cuda(dy2d, x2d, a, b)
     dt = x2d.dtype
     code = _dtype_code(x2d)
@@ -149,7 +150,8 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
     lib = _lib.load()
     dx = torch.empty((M, K), dtype=dt, device=x2d.device) if need_dx else None
     flags = 0
-    if da_out is not None or db_out is not None:
+    into = da_out is not None or db_out is not None
+    if into:
         if r != r_orig:
             raise ShapeError("gradient accumulation buffers need a rank that is a multiple of 8")
         for name, t, shp in (("da_out", da_out, (r, K)), ("db_out", db_out, (N, r))):
@@ -157,7 +159,7 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
                     not t.is_contiguous():
                 raise ShapeError(f"{name} must be a contiguous fp32 tensor of shape {shp}")
         da, db = da_out, db_out
-        flags = _lib.BWD_ACCUMULATE
+        flags = _lib.BWD_ACCUMULATE if accumulate else 0
     else:
         da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
         db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
@@ -167,7 +169,7 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
                                     _ptr(db), M, K, N, r, float(alpha_p), float(clip_value), code,
                                     flags, _ptr(ws), ws.numel(), _stream())
     _lib.check(st, "mlora_lora_backward")
-    if flags:
+    if into:
         return dx, da, db
     if r != r_orig:
         da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
@@ -333,8 +335,9 @@ def qlora_linear_fwd(x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor, al
 def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor,
                      alpha: float, saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
                      need_dx: bool = True, da_out: torch.Tensor | None = None,
-                     db_out: torch.Tensor | None = None):
-    """(dx, dA, dB) through a frozen quantised base (staged or lean as the forward)."""
+                     db_out: torch.Tensor | None = None, accumulate: bool = True):
+    """(dx, dA, dB) through a frozen quantised base (staged or lean as the forward);
+    ``da_out``/``db_out``/``accumulate`` as in ``lora_linear_bwd``."""
     _need_cuda(dy2d, x2d, a, b)
     M, K = x2d.shape
     N = dy2d.shape[1]
@@ -347,10 +350,12 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
     lib = _lib.load()
     dx = torch.empty((M, K), dtype=torch.bfloat16, device=x2d.device) if need_dx else None
     flags = 0
-    if da_out is not None or db_out is not None:
+    into = da_out is not None or db_out is not None
+    if into:
         if r != r_orig:
             raise ShapeError("gradient accumulation buffers need a rank that is a multiple of 8")
-        da, db, flags = da_out, db_out, _lib.BWD_ACCUMULATE
+        da, db = da_out, db_out
+        flags = _lib.BWD_ACCUMULATE if accumulate else 0
     else:
         da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
         db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
@@ -363,7 +368,7 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
                                      _ptr(db), M, K, N, r, float(alpha_p), float(clip_value),
                                      _lib.DTYPE_BF16, flags, _ptr(ws), ws.numel(), _stream())
     _lib.check(st, "mlora_qlora_backward_ex")
-    if flags:
+    if into:
         return dx, da, db
     if r != r_orig:
         da, db = da[:r_orig].contiguous(), db[:, :r_orig].contiguous()

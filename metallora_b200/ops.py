@@ -14,6 +14,10 @@ from . import kernels as _k
 from .exceptions import ShapeError
 
 
+def _sink_accumulates(sink) -> bool:
+    return sink is None or len(sink) < 3 or bool(sink[2])
+
+
 class _LoRALinearFn(torch.autograd.Function):
     """y = x.W0^T + s.(x.A^T).B^T with the fused backward (dx, dA, dB in one
     launch sequence).  W0 gets a gradient only when it requires one (the
@@ -23,7 +27,8 @@ class _LoRALinearFn(torch.autograd.Function):
     compute): they are cast for the kernels and their gradients returned in
     their own dtype.  ``compute`` optionally supplies ready-made casts, and
     ``sink`` = (gA, gB) fp32 buffers receives the LoRA gradients by in-kernel
-    accumulation instead of autograd (the trainer's flat gradient buffer)."""
+    accumulation instead of autograd (the trainer's flat gradient buffer);
+    (gA, gB, False) writes them over the buffers' contents instead."""
 
     @staticmethod
     def forward(ctx, x2d, w0, a, b, alpha, compute, sink):
@@ -43,7 +48,8 @@ class _LoRALinearFn(torch.autograd.Function):
         dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a_c, b_c,
                                         ctx.alpha, saved, 0.0, need_dx=need_dx,
                                         da_out=sink[0] if sink else None,
-                                        db_out=sink[1] if sink else None)
+                                        db_out=sink[1] if sink else None,
+                                        accumulate=_sink_accumulates(sink))
         dw0 = None
         if ctx.needs_input_grad[1]:
             # trainable base weight (freeze_base=False): plain library GEMM
@@ -78,7 +84,8 @@ class _QLoRALinearFn(torch.autograd.Function):
         dx, da, db = _k.qlora_linear_bwd(dy.contiguous(), x2d, ctx.qw, a_c, b_c, ctx.alpha, saved,
                                          0.0, need_dx=need_dx,
                                          da_out=sink[0] if sink else None,
-                                         db_out=sink[1] if sink else None)
+                                         db_out=sink[1] if sink else None,
+                                         accumulate=_sink_accumulates(sink))
         if sink is not None:
             return dx, None, None, None, None, None, None
         da = da.to(ctx.ab_dtypes[0]) if ctx.needs_input_grad[1] else None
