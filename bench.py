@@ -69,11 +69,11 @@ def flops_per_token(K, N, r):
     return fwd + bwd
 
 
-# DRAM traffic of one lora_gemm_kernel launch of the headline workload (forward,
-# M 8192, K 4096, N 4096, rank block 16), from one ncu capture:
-# dram__bytes_read.sum 103.3 MB + dram__bytes_write.sum 45.3 MB.  Algorithmic
+# DRAM traffic of one lora_gemm_pair_kernel launch of the headline workload
+# (forward, M 8192, K 4096, N 4096, rank block 16), from one ncu capture:
+# dram__bytes_read.sum 111.2 MB + dram__bytes_write.sum 46.4 MB.  Algorithmic
 # bytes: x 64 MiB + W0 32 MiB + rank block 1.125 MiB read, y 64 MiB written.
-GEMM_TRAFFIC_BYTES = 148.6e6
+GEMM_TRAFFIC_BYTES = 157.5e6
 GEMM_ALGORITHMIC_BYTES = (64 + 32 + 1.125 + 64) * 2 ** 20
 
 
@@ -313,7 +313,7 @@ def run_ours(args, rank, world, local_rank):
                    "grad_exchange": exchange,
                    "l2": "inputs > L2 (~290 MB resident per GPU), no flush"},
         "tflops": round(total_tflops, 1),
-        "roofline": {"bound": "tensor", "kernel": "lora_gemm_kernel (tcgen05)",
+        "roofline": {"bound": "tensor", "kernel": "lora_gemm_pair_kernel (tcgen05 cta_group::2)",
                      "achieved": round(achieved, 1) if achieved else None,
                      "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4) if achieved else None,
