@@ -375,8 +375,6 @@ int lora_forward_f32(const float* x, const float* w0, const float* a, const floa
   ga.elt = Elt::kBF16;
   ga.out_dtype = MLORA_DTYPE_F32;
   if (lora) {
-    cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
-    if (e != cudaSuccess) return cuda_fail(e, "memset");
     if ((rc = launch_split3_cols(a, r, K, K, p.as, K, 3 * K, kHLH, s))) return rc;
     if ((rc = launch_split3_cols(b, N, r, r, p.bs, p.R, 3 * p.R, kHLH, s))) return rc;
     RankArgs ra;
@@ -422,8 +420,6 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
   const float scale = alpha / static_cast<float>(r);
   int rc;
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
-  if (e != cudaSuccess) return cuda_fail(e, "memset");
   if ((rc = launch_split3_cols(dy, M, N, N, p.dys_cols, N, 3 * N, kHHL, s))) return rc;
   if ((rc = launch_split3_cols(x, M, K, K, p.xs_cols, K, 3 * K, kHHL, s))) return rc;
   if ((rc = launch_split3_rows(dy, M, N, N, p.dy_rows, M, kHHL, s))) return rc;
@@ -541,11 +537,8 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
   const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
   const float scale = alpha / static_cast<float>(r);
 
-  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection;
-  // the same launch zeroes the split counters of the kernels below.
-  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s, p.counters,
-                                 static_cast<int64_t>(p.counter_bytes / 4))))
-    return rc;
+  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection.
+  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s))) return rc;
 
   RankArgs ra;
   ra.x = dy;
@@ -820,9 +813,6 @@ int lora_forward16(const void* x, const void* w0, const void* a, const void* b, 
   const FwdPlan p = plan_forward(workspace, M, K, r, saved_xa == nullptr);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
-
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
-  if (e != cudaSuccess) return fail(MLORA_ERR_CUDA, std::string("memset: ") + cudaGetErrorString(e));
 
   RankArgs ra;
   ra.x = x;
@@ -1195,8 +1185,6 @@ int mlora_qlora_forward_ex(const void* x, int scheme, const void* codes, const v
                                          " for the lean fused-dequant kernel)");
   const FwdPlan p = plan_forward(workspace, M, K, r, saved_xa == nullptr);
   const void* scales_t = prepared;
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
-  if (e != cudaSuccess) return cuda_fail(e, "memset");
   if (scales_t == nullptr) {
     void* tab = static_cast<uint8_t*>(workspace) + p.bytes;
     if ((rc = prep_scales(scheme, scales, zeros, N, K, group, tab, s))) return rc;
@@ -1343,8 +1331,6 @@ int mlora_multi_lora_forward(const void* x, const void* w0, const void* a_stack,
   const FwdPlan p = plan_forward(workspace, M, K, R, false);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, ((M + 127) / 128) * 4, s);
-  if (e != cudaSuccess) return cuda_fail(e, "memset");
   // one pass over x projects onto every stacked adapter; each row keeps its own
   RankArgs ra;
   ra.x = x;
@@ -1520,9 +1506,6 @@ int mlora_lora_embedding_backward(const void* dy, const int32_t* idx, const int3
     return fail(MLORA_ERR_WORKSPACE, "embedding backward workspace needs " + std::to_string(need.bytes) + " bytes");
   const EmbedBwdPlan p = plan_embed_bwd(workspace, T, D, r);
   const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
-  e = cudaMemsetAsync(p.rank.counters, 0, ((T + 127) / 128) * 4, s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(p.wcount, 0, ((D + 127) / 128) * 4, s);
-  if (e != cudaSuccess) return cuda_fail(e, "memset");
   // U = s dy.A^T, then dB rows as in-order sums of U over each index's tokens
   RankArgs ra;
   ra.x = dy;

@@ -1,7 +1,7 @@
 // Allocation-free variant of the LoRA weight-gradient entry point.
 //
-// mlora_lora_backward needs scratch (the transposed B, the rank intermediates
-// s.dy.B and s.x.A^T, split-reduction partial sums and counters) and takes it
+// mlora_lora_backward needs scratch (the transposed B and the rank
+// intermediates s.dy.B and s.x.A^T) and takes it
 // from a workspace the caller allocates.  Some callers cannot allocate device
 // memory when they run the backward: a process that hands all device memory to
 // its own pool at start-up and has none left to give, or a latency-critical
@@ -77,8 +77,7 @@ int mlora_lora_grads_static(const void* dy, const void* x, const void* a, const 
     mlora::set_error(std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
   }
-  // Same computation as mlora_lora_backward without dx; it clears the
-  // reduction counters it uses at the start of every call.
+  // Same computation as mlora_lora_backward without dx.
   return mlora_lora_backward(dy, x, nullptr, a, b, nullptr, nullptr, da, db, M, K, N, r, alpha,
                              clip_value, dtype, scratch, kStaticScratchBytes, stream);
 }

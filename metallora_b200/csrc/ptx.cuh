@@ -300,9 +300,17 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
   return r;
 }
 
+// Cluster-wide barrier (all threads of all CTAs of the cluster).  Not
+// `.aligned`: callers may reach it from warps that diverged (elected lanes).
 __device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Loads a float from the shared memory of any CTA of the cluster.
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
 }
 
 // Arrive on an mbarrier of any CTA of the cluster.

@@ -29,6 +29,7 @@ constexpr int kBK = 64;
 constexpr uint32_t kBigTileBytes = 128 * kBK * 2;  // 16 KB: [128 x 64] 16-bit
 constexpr uint32_t kMNBoxBytes = 64 * kBK * 2;     // 8 KB
 constexpr uint32_t kSmemBudget = 100 * 1024;       // two CTAs per SM
+constexpr int kMaxSplits = 8;                      // portable cluster size
 
 __host__ __device__ constexpr uint32_t small_tile_bytes(int R) { return R * 128u; }
 __host__ __device__ constexpr uint32_t stage_bytes(int R) {
@@ -143,58 +144,66 @@ __device__ __forceinline__ void load_acc_row(uint32_t taddr_row, float (&acc)[R]
   }
 }
 
-// Deterministic split reduction.  Every epilogue thread owns one row of the
-// [128 x R] tile.  Returns true in the CTA that must write the final result,
-// with `acc` holding the sum over splits in order 0..splits-1.
-template <int R>
-__device__ __forceinline__ bool split_reduce(float (&acc)[R], float* partials, uint32_t* counters,
-                                             int tile, int split, int splits, long long row,
-                                             long long rows_total, uint32_t* flag_smem) {
-  if (splits == 1) return true;
-  const bool valid = row < rows_total;
-  if (valid) {
-    float4* dst = reinterpret_cast<float4*>(partials + (static_cast<long long>(split) * rows_total + row) * R);
+// Cross-CTA split reduction through distributed shared memory.  The S CTAs of
+// a cluster computed the same [128 x R] tile over S disjoint ranges of the
+// reduction dimension (cluster rank = range index).  Each CTA parks its fp32
+// partial in its own shared memory (the TMA stage area, free once the MMAs
+// are done), column-major [j][row] so warps touch consecutive words; after a
+// cluster barrier CTA c sums its slice of columns [c W, (c+1) W) (W = CP / S)
+// of all 128 rows over s = 0..S-1 in that order -- fixed order, so results are
+// bitwise reproducible -- and hands pairs of columns to `emit(j, v_j, v_j+1)`.
+// A second barrier keeps every CTA resident until its peers have read it.
+// Columns go in passes of CP (R > 128: two passes), each read from TMEM at
+// `taddr` (this thread's lane) when `have` (zeros otherwise).  Every thread of
+// the CTA calls this; only epilogue threads (`epi`) move data.
+__host__ __device__ constexpr int reduce_cols(int R) { return R <= 128 ? R : 128; }
+
+template <int R, typename Emit>
+__device__ __forceinline__ void cluster_reduce(uint32_t taddr, bool have, float* buf, int S,
+                                               uint32_t crank, int row_local, bool epi,
+                                               Emit&& emit) {
+  constexpr int CP = reduce_cols(R);
+#pragma unroll 1
+  for (int pass = 0; pass < R / CP; ++pass) {
+    if (epi) {
+      float acc[CP];
+      if (have) {
+        load_acc_row<CP>(taddr + pass * CP, acc);
+      } else {
 #pragma unroll
-    for (int i = 0; i < R / 4; ++i)
-      __stcg(dst + i, make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]));
-  }
-  __threadfence();
-  named_bar_sync(1, 128);
-  if (threadIdx.x == 64) {
-    const uint32_t ticket = atomicAdd(&counters[tile], 1u);
-    const bool last = ticket == static_cast<uint32_t>(splits - 1);
-    if (last) counters[tile] = 0;  // ready for the next launch
-    *flag_smem = last ? 1u : 0u;
-  }
-  named_bar_sync(1, 128);
-  if (*flag_smem == 0) return false;
-  __threadfence();
-  if (valid) {
+        for (int j = 0; j < CP; ++j) acc[j] = 0.f;
+      }
 #pragma unroll
-    for (int i = 0; i < R; ++i) acc[i] = 0.f;
-    // splits in order, four splits' loads in flight together
-    for (int s0 = 0; s0 < splits; s0 += 4) {
+      for (int j = 0; j < CP; ++j) buf[j * 128 + row_local] = acc[j];
+    }
+    cluster_sync();
+    if (epi) {
+      const int W = CP / S;
+      const int j0 = static_cast<int>(crank) * W;
+      const uint32_t base = smem_u32(buf) + static_cast<uint32_t>(row_local) * 4u;
+      uint32_t peer[8];
 #pragma unroll
-      for (int i = 0; i < R / 4; ++i) {
-        float4 v[4];
+      for (int s = 0; s < 8; ++s) peer[s] = s < S ? mapa_shared(base, static_cast<uint32_t>(s)) : 0u;
+#pragma unroll 1
+      for (int jj = 0; jj < W; jj += 2) {
+        const uint32_t off0 = static_cast<uint32_t>(j0 + jj) * 512u;
+        float a[8], b[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          v[u] = s0 + u < splits
-                     ? __ldcg(reinterpret_cast<const float4*>(
-                                  partials + (static_cast<long long>(s0 + u) * rows_total + row) * R) +
-                              i)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          acc[4 * i] += v[u].x;
-          acc[4 * i + 1] += v[u].y;
-          acc[4 * i + 2] += v[u].z;
-          acc[4 * i + 3] += v[u].w;
+        for (int s = 0; s < 8; ++s) {
+          a[s] = s < S ? ld_shared_cluster_f32(peer[s] + off0) : 0.f;
+          b[s] = s < S ? ld_shared_cluster_f32(peer[s] + off0 + 512u) : 0.f;
         }
+        float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          v0 += a[s];
+          v1 += b[s];
+        }
+        emit(pass * CP + j0 + jj, v0, v1);
       }
     }
+    cluster_sync();
   }
-  return true;
 }
 
 struct RankParams {
@@ -207,13 +216,13 @@ struct RankParams {
   long long ld_t;
   int split_out;
   uint32_t split_pattern;
-  float* partials;
-  uint32_t* counters;
   uint32_t* status;
   const int32_t* row_group;  // optional: keep only columns [g*group_cols, (g+1)*group_cols)
   int group_cols;
 };
 
+// Grid (tiles, splits), cluster (1, splits, 1): the splits of one 128-row tile
+// are one cluster.
 template <int R, bool kBF16>
 __global__ void __launch_bounds__(kThreads, 2)
     rank_proj_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_l,
@@ -227,7 +236,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* empty_bar = full_bar + S;
   uint64_t* done_bar = empty_bar + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-  uint32_t* flag = tmem_slot + 1;
 
   const uint32_t warp = warp_id();
   if (threadIdx.x == 0) {
@@ -245,96 +253,74 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   const int tile = blockIdx.x;
-  const SplitWork w = split_work(tile, blockIdx.y, p.splits, p.num_kb);
+  const uint32_t crank = cluster_ctarank();
+  const SplitWork w = split_work(tile, static_cast<int>(crank), p.splits, p.num_kb);
   const bool has_work = w.kb_begin < w.kb_end;
   if (has_work) {
     run_pipeline<R, false, kBF16>(smem, full_bar, empty_bar, done_bar, tmem, &tm_x, &tm_l,
                                   tile * 128, w.kb_begin, w.kb_end, p.status);
   }
-  if (warp >= 2) {
-    const uint32_t quarter = warp & 3u;
-    const long long row = static_cast<long long>(tile) * 128 + quarter * 32 + lane_id();
-    float acc[R];
-    bool ok = true;
-    if (has_work) {
-      ok = mbar_wait(done_bar, 0, p.status, kDevTimeoutAccFull);
-      tc_fence_after();
-      if (ok) load_acc_row<R>(tmem + ((quarter * 32u) << 16), acc);
-    } else {
-#pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] = 0.f;
-    }
-    if (!ok) {
-#pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] = 0.f;
-    }
-    const bool final_cta =
-        split_reduce<R>(acc, p.partials, p.counters, tile, w.split, p.splits, row, p.M, flag);
-    if (final_cta && row < p.M && p.split_out) {
+  const bool epi = warp >= 2;
+  const int row_local = static_cast<int>((warp & 3u) * 32 + lane_id());
+  const long long row = static_cast<long long>(tile) * 128 + row_local;
+  bool have = false;
+  if (epi && has_work) {
+    have = mbar_wait(done_bar, 0, p.status, kDevTimeoutAccFull);
+    tc_fence_after();
+  }
+  int group = -1;
+  if (epi && p.row_group != nullptr && row < p.M) group = p.row_group[row];
+  const bool live = epi && row < p.M;
+  auto emit = [&](int j, float v0, float v1) {
+    if (!live) return;
+    v0 *= p.scale;
+    v1 *= p.scale;
+    if (p.split_out) {
       // fp32 path: bf16 hi/lo parts of the scaled value (bf16 instantiation only)
-#pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] *= p.scale;
-      if (p.out_rows != nullptr) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out_rows) + row * p.ld_rows;
-        for (int s = 0; s < 3; ++s) {
-          const bool lo = (p.split_pattern >> s) & 1u;
-#pragma unroll
-          for (int i = 0; i < R / 2; ++i) {
-            const float a0 = acc[2 * i], a1 = acc[2 * i + 1];
-            const float h0 = __bfloat162float(__float2bfloat16_rn(a0));
-            const float h1 = __bfloat162float(__float2bfloat16_rn(a1));
-            *reinterpret_cast<uint32_t*>(dst + s * R + 2 * i) =
-                lo ? pack2<__nv_bfloat16>(a0 - h0, a1 - h1) : pack2<__nv_bfloat16>(a0, a1);
-          }
-        }
-        for (long long j = 3 * R; j < p.ld_rows; j += 8)
-          *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
-      }
-      if (p.out_t != nullptr) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out_t);
-        for (int s = 0; s < 3; ++s) {
-          const bool lo = (p.split_pattern >> s) & 1u;
-#pragma unroll
-          for (int j = 0; j < R; ++j) {
-            const __nv_bfloat16 h = __float2bfloat16_rn(acc[j]);
-            dst[static_cast<long long>(j) * p.ld_t + s * p.M + row] =
-                lo ? __float2bfloat16_rn(acc[j] - __bfloat162float(h)) : h;
-          }
+      const float h0 = __bfloat162float(__float2bfloat16_rn(v0));
+      const float h1 = __bfloat162float(__float2bfloat16_rn(v1));
+      for (int s = 0; s < 3; ++s) {
+        const bool lo = (p.split_pattern >> s) & 1u;
+        const float o0 = lo ? v0 - h0 : v0, o1 = lo ? v1 - h1 : v1;
+        if (p.out_rows != nullptr)
+          *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.out_rows) +
+                                       row * p.ld_rows + s * R + j) = pack2<__nv_bfloat16>(o0, o1);
+        if (p.out_t != nullptr) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out_t) + s * p.M + row;
+          dst[static_cast<long long>(j) * p.ld_t] = __float2bfloat16_rn(o0);
+          dst[static_cast<long long>(j + 1) * p.ld_t] = __float2bfloat16_rn(o1);
         }
       }
-    } else if (final_cta && row < p.M) {
-      if (p.row_group != nullptr) {
-        // stacked adapters: the row keeps only its own adapter's columns (an
-        // id outside [0, R / group_cols) keeps none)
-        const int g = p.row_group[row];
-#pragma unroll
-        for (int j = 0; j < R; ++j)
-          if (j / p.group_cols != g) acc[j] = 0.f;
-      }
-      if (p.out_rows != nullptr) {
-        T* dst = reinterpret_cast<T*>(p.out_rows) + row * p.ld_rows;
-#pragma unroll
-        for (int i = 0; i < R / 8; ++i) {
-          uint4 v;
-          v.x = pack2<T>(acc[8 * i] * p.scale, acc[8 * i + 1] * p.scale);
-          v.y = pack2<T>(acc[8 * i + 2] * p.scale, acc[8 * i + 3] * p.scale);
-          v.z = pack2<T>(acc[8 * i + 4] * p.scale, acc[8 * i + 5] * p.scale);
-          v.w = pack2<T>(acc[8 * i + 6] * p.scale, acc[8 * i + 7] * p.scale);
-          reinterpret_cast<uint4*>(dst)[i] = v;
-        }
-        for (long long j = R; j < p.ld_rows; j += 8)
-          *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
-      }
-      if (p.out_t != nullptr) {
-        T* dst = reinterpret_cast<T*>(p.out_t);
-#pragma unroll
-        for (int j = 0; j < R; ++j) {
-          if constexpr (kBF16)
-            dst[static_cast<long long>(j) * p.ld_t + row] = __float2bfloat16_rn(acc[j] * p.scale);
-          else
-            dst[static_cast<long long>(j) * p.ld_t + row] = __float2half_rn(acc[j] * p.scale);
-        }
-      }
+      return;
+    }
+    if (p.row_group != nullptr) {
+      // stacked adapters: the row keeps only its own adapter's columns (an
+      // id outside [0, R / group_cols) keeps none)
+      if (j / p.group_cols != group) v0 = 0.f;
+      if ((j + 1) / p.group_cols != group) v1 = 0.f;
+    }
+    if (p.out_rows != nullptr)
+      *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.out_rows) + row * p.ld_rows + j) =
+          pack2<T>(v0, v1);
+    if (p.out_t != nullptr) {
+      T* dst = reinterpret_cast<T*>(p.out_t) + row;
+      dst[static_cast<long long>(j) * p.ld_t] = static_cast<T>(v0);
+      dst[static_cast<long long>(j + 1) * p.ld_t] = static_cast<T>(v1);
+    }
+  };
+  cluster_reduce<R>(tmem + ((static_cast<uint32_t>(row_local & ~31)) << 16), have,
+                    reinterpret_cast<float*>(smem), p.splits, crank, row_local, epi, emit);
+  // zero padding of the row buffer past the computed columns (cluster rank 0)
+  if (live && crank == 0 && p.out_rows != nullptr) {
+    const long long from = p.split_out ? 3 * R : R;
+    if (p.split_out) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out_rows) + row * p.ld_rows;
+      for (long long j = from; j < p.ld_rows; j += 8)
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
+    } else {
+      T* dst = reinterpret_cast<T*>(p.out_rows) + row * p.ld_rows;
+      for (long long j = from; j < p.ld_rows; j += 8)
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
     }
   }
   tc_fence_before();
@@ -347,23 +333,24 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 struct WgradProblem {
   long long M, P;
-  int r, num_kb, splits, tiles;
+  int r, num_kb, tiles;
   float* out;
   long long ldo;
   int transposed;
   int accumulate;
   float clip;
-  float* partials;
-  uint32_t* counters;
 };
 
 struct WgradParams {
   WgradProblem prob[2];
   int nprobs;
-  int ctas0;  // CTAs of problem 0 (= tiles * splits)
+  int splits;  // cluster size: the splits of one tile are one cluster
+  int ctas0;   // CTAs of problem 0 (= tiles * splits)
   uint32_t* status;
 };
 
+// 1-D grid, cluster (splits, 1, 1): CTA b of problem q works on tile
+// b / splits over token range b % splits (= its cluster rank).
 template <int R, bool kBF16>
 __global__ void __launch_bounds__(kThreads, 2)
     wgrad_kernel(const __grid_constant__ CUtensorMap tm_big0, const __grid_constant__ CUtensorMap tm_st0,
@@ -377,7 +364,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* empty_bar = full_bar + S;
   uint64_t* done_bar = empty_bar + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-  uint32_t* flag = tmem_slot + 1;
 
   const uint32_t warp = warp_id();
   if (threadIdx.x == 0) {
@@ -397,53 +383,47 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int which = (static_cast<int>(blockIdx.x) < p.ctas0) ? 0 : 1;
   const WgradProblem& q = p.prob[which];
   const int local = static_cast<int>(blockIdx.x) - (which ? p.ctas0 : 0);
-  const int tile = local % q.tiles;
-  const SplitWork w = split_work(tile, local / q.tiles, q.splits, q.num_kb);
+  const uint32_t crank = cluster_ctarank();
+  const int tile = local / p.splits;
+  const SplitWork w = split_work(tile, static_cast<int>(crank), p.splits, q.num_kb);
   const bool has_work = w.kb_begin < w.kb_end;
   if (has_work) {
     run_pipeline<R, true, kBF16>(smem, full_bar, empty_bar, done_bar, tmem,
                                  which ? &tm_big1 : &tm_big0, which ? &tm_st1 : &tm_st0,
                                  tile * 128, w.kb_begin, w.kb_end, p.status);
   }
-  if (warp >= 2) {
-    const uint32_t quarter = warp & 3u;
-    const long long prow = static_cast<long long>(tile) * 128 + quarter * 32 + lane_id();
-    float acc[R];
-    bool ok = true;
-    if (has_work) {
-      ok = mbar_wait(done_bar, 0, p.status, kDevTimeoutAccFull);
-      tc_fence_after();
-      if (ok) load_acc_row<R>(tmem + ((quarter * 32u) << 16), acc);
-    }
-    if (!has_work || !ok) {
-#pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] = 0.f;
-    }
-    if (split_reduce<R>(acc, q.partials, q.counters, tile, w.split, q.splits, prow, q.P, flag) &&
-        prow < q.P) {
-      const bool clip = q.clip > 0.f;
-      const long long step_j = q.transposed ? q.ldo : 1;
-      float* const row = q.transposed ? q.out + prow : q.out + prow * q.ldo;
-      if (q.accumulate) {  // all old values loaded before any store: one round trip
-        float prev[R];
-#pragma unroll
-        for (int j = 0; j < R; ++j) prev[j] = j < q.r ? row[j * step_j] : 0.f;
-#pragma unroll
-        for (int j = 0; j < R; ++j) {
-          float v = acc[j];
-          if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
-          if (j < q.r) row[j * step_j] = prev[j] + v;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < R; ++j) {
-          float v = acc[j];
-          if (clip) v = fminf(fmaxf(v, -q.clip), q.clip);
-          if (j < q.r) row[j * step_j] = v;
-        }
-      }
-    }
+  const bool epi = warp >= 2;
+  const int row_local = static_cast<int>((warp & 3u) * 32 + lane_id());
+  const long long prow = static_cast<long long>(tile) * 128 + row_local;
+  bool have = false;
+  if (epi && has_work) {
+    have = mbar_wait(done_bar, 0, p.status, kDevTimeoutAccFull);
+    tc_fence_after();
   }
+  const bool live = epi && prow < q.P;
+  const bool clip = q.clip > 0.f;
+  const long long step_j = q.transposed ? q.ldo : 1;
+  float* const out_row = q.transposed ? q.out + prow : q.out + prow * q.ldo;
+  auto emit = [&](int j, float v0, float v1) {
+    if (!live) return;
+    if (clip) {
+      v0 = fminf(fmaxf(v0, -q.clip), q.clip);
+      v1 = fminf(fmaxf(v1, -q.clip), q.clip);
+    }
+    float* d0 = out_row + j * step_j;
+    float* d1 = d0 + step_j;
+    const bool w0 = j < q.r, w1 = j + 1 < q.r;
+    if (q.accumulate) {  // both old values loaded before either store
+      const float o0 = w0 ? *d0 : 0.f, o1 = w1 ? *d1 : 0.f;
+      if (w0) *d0 = o0 + v0;
+      if (w1) *d1 = o1 + v1;
+    } else {
+      if (w0) *d0 = v0;
+      if (w1) *d1 = v1;
+    }
+  };
+  cluster_reduce<R>(tmem + ((static_cast<uint32_t>(row_local & ~31)) << 16), have,
+                    reinterpret_cast<float*>(smem), p.splits, crank, row_local, epi, emit);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -463,11 +443,34 @@ bool set_smem_attr(K kern, size_t bytes) {
   return true;
 }
 
+// Launches `kern` with a (cx, cy, 1) cluster.
+template <typename Kern, typename... Args>
+cudaError_t launch_clustered(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, unsigned cx,
+                             unsigned cy, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cx;
+  attr[0].val.clusterDim.y = cy;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <int R, bool kBF16>
 int launch_rank_typed(const RankArgs& a, cudaStream_t stream) {
   CUtensorMap tx, tl;
   if (!make_tmap_2d_16b(&tx, a.x, a.K, a.M, a.ldx, kBK, 128)) return MLORA_ERR_INVALID_ARG;
   if (!make_tmap_2d_16b(&tl, a.l, a.K, a.r, a.ldl, kBK, R)) return MLORA_ERR_INVALID_ARG;
+  if (a.splits < 1 || a.splits > kMaxSplits || (a.splits & (a.splits - 1)) != 0) {
+    set_error("rank: splits must be 1, 2, 4 or 8");
+    return MLORA_ERR_INVALID_ARG;
+  }
   RankParams p;
   p.M = a.M;
   p.r = static_cast<int>(a.r);
@@ -480,8 +483,6 @@ int launch_rank_typed(const RankArgs& a, cudaStream_t stream) {
   p.ld_t = a.ld_t;
   p.split_out = a.split_out ? 1 : 0;
   p.split_pattern = a.split_pattern;
-  p.partials = a.partials;
-  p.counters = a.counters;
   p.status = device_status_ptr();
   p.row_group = a.row_group;
   p.group_cols = a.group_cols > 0 ? static_cast<int>(a.group_cols) : R;
@@ -489,8 +490,9 @@ int launch_rank_typed(const RankArgs& a, cudaStream_t stream) {
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
   dim3 grid(static_cast<unsigned>((a.M + 127) / 128), static_cast<unsigned>(a.splits));
   LaunchScope scope(kKindRank, stream);
-  kern<<<grid, kThreads, smem_bytes(R), stream>>>(tx, tl, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_clustered(kern, grid, smem_bytes(R), stream, 1u,
+                                   static_cast<unsigned>(a.splits), tx, tl, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("rank launch: ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
@@ -503,6 +505,12 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
   CUtensorMap tb[2], ts[2];
   WgradParams p;
   p.nprobs = n;
+  p.splits = probs[0].splits;
+  if (p.splits < 1 || p.splits > kMaxSplits || (p.splits & (p.splits - 1)) != 0 ||
+      (n == 2 && probs[1].splits != p.splits)) {
+    set_error("wgrad: splits must be 1, 2, 4 or 8 and equal for both problems");
+    return MLORA_ERR_INVALID_ARG;
+  }
   int total = 0;
   for (int i = 0; i < 2; ++i) {
     const WgradArgs& a = probs[i < n ? i : 0];
@@ -513,24 +521,23 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
     q.P = a.P;
     q.r = static_cast<int>(a.r);
     q.num_kb = static_cast<int>((a.M + kBK - 1) / kBK);
-    q.splits = a.splits;
     q.tiles = static_cast<int>((a.P + 127) / 128);
     q.out = a.out;
     q.ldo = a.ldo;
     q.transposed = a.transposed ? 1 : 0;
     q.accumulate = a.accumulate ? 1 : 0;
     q.clip = a.clip;
-    q.partials = a.partials;
-    q.counters = a.counters;
-    if (i < n) total += q.tiles * q.splits;
-    if (i == 0) p.ctas0 = q.tiles * q.splits;
+    if (i < n) total += q.tiles * p.splits;
+    if (i == 0) p.ctas0 = q.tiles * p.splits;
   }
   p.status = device_status_ptr();
   auto kern = wgrad_kernel<R, kBF16>;
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
   LaunchScope scope(kKindWgrad, stream);
-  kern<<<total, kThreads, smem_bytes(R), stream>>>(tb[0], ts[0], tb[1], ts[1], p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_clustered(kern, dim3(static_cast<unsigned>(total)), smem_bytes(R), stream,
+                                   static_cast<unsigned>(p.splits), 1u, tb[0], ts[0], tb[1], ts[1],
+                                   p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("wgrad launch: ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
@@ -558,28 +565,26 @@ int wgrad_dispatch(const WgradArgs* probs, int n, cudaStream_t s) {
   MLORA_DISPATCH_R(probs[0].R, launch_wgrad_typed, probs, n, s)
 }
 
+int pow2_splits(int64_t tiles, int64_t num_kb) {
+  int64_t cap = (2 * num_sms()) / tiles;
+  const int64_t max_splits = num_kb / 4 > 0 ? num_kb / 4 : 1;  // >= 4 k-blocks per split
+  if (cap > max_splits) cap = max_splits;
+  int splits = 1;
+  while (splits * 2 <= cap && splits * 2 <= kMaxSplits) splits *= 2;
+  return splits;
+}
+
 }  // namespace
 
-// Split counts keep tiles x splits within one wave of resident CTAs (2 per SM):
-// a second, nearly empty wave would double the kernel's time.
+// Split counts (the cluster size of the split reduction: 1, 2, 4 or 8) keep
+// tiles x splits within one wave of resident CTAs (2 per SM): a second, nearly
+// empty wave would double the kernel's time.
 int rank_splits(int64_t M, int64_t K) {
-  const int64_t tiles = (M + 127) / 128;
-  const int64_t num_kb = (K + kBK - 1) / kBK;
-  int64_t splits = (2 * num_sms()) / tiles;
-  const int64_t max_splits = num_kb / 4 > 0 ? num_kb / 4 : 1;  // >= 4 k-blocks per split
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
-  return static_cast<int>(splits);
+  return pow2_splits((M + 127) / 128, (K + kBK - 1) / kBK);
 }
 
 int wgrad_splits(int64_t M, int64_t P, int nproblems) {
-  const int64_t tiles = (P + 127) / 128 * nproblems;
-  const int64_t num_kb = (M + kBK - 1) / kBK;
-  int64_t splits = (2 * num_sms()) / tiles;
-  const int64_t max_splits = num_kb / 4 > 0 ? num_kb / 4 : 1;
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
-  return static_cast<int>(splits);
+  return pow2_splits((P + 127) / 128 * nproblems, (M + kBK - 1) / kBK);
 }
 
 int launch_rank(const RankArgs& a, cudaStream_t stream) {
