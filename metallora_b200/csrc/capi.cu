@@ -127,10 +127,8 @@ int check_shapes(int64_t M, int64_t K, int64_t N, int64_t r, int dtype, bool nee
 struct FwdPlan {
   int64_t R, R64;
   int splits;
-  uint32_t* counters;
   void* xa_rows;
   void* xa_t;
-  float* partials;
   size_t bytes;
 };
 
@@ -140,10 +138,8 @@ FwdPlan plan_forward(void* ws, int64_t M, int64_t K, int64_t r, bool need_xa_t) 
   p.R64 = pad64(p.R);
   p.splits = rank_splits(M, K);
   Carve c(ws);
-  p.counters = static_cast<uint32_t*>(c.take(((M + 127) / 128) * 4));
   p.xa_rows = c.take(static_cast<size_t>(M) * p.R64 * 2);
   p.xa_t = need_xa_t ? c.take(static_cast<size_t>(p.R) * pad8(M) * 2) : nullptr;
-  p.partials = p.splits > 1 ? static_cast<float*>(c.take(size_t(p.splits) * M * p.R * 4)) : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
@@ -152,15 +148,10 @@ FwdPlan plan_forward(void* ws, int64_t M, int64_t K, int64_t r, bool need_xa_t) 
 struct BwdPlan {
   int64_t R, R64;
   int rsplits, wsplits;
-  uint32_t* counters;  // [tiles_m] rank(U) | [tiles_m] rank(T) | [N/128] dB | [K/128] dA
-  size_t counter_bytes;
   void* bt;
   void* u_rows;
   void* u_t;
   void* xa_t;
-  float* rpartials;
-  float* wpart_db;
-  float* wpart_da;
   size_t bytes;
 };
 
@@ -170,17 +161,11 @@ BwdPlan plan_backward(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, bool
   p.R64 = pad64(p.R);
   p.rsplits = rank_splits(M, N > K ? N : K);
   p.wsplits = wgrad_splits(M, N > K ? N : K, 2);
-  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128, tk = (K + 127) / 128;
   Carve c(ws);
-  p.counter_bytes = static_cast<size_t>(2 * tm + tn + tk) * 4;
-  p.counters = static_cast<uint32_t*>(c.take(p.counter_bytes));
   p.bt = c.take(static_cast<size_t>(p.R) * N * 2);
   p.u_rows = c.take(static_cast<size_t>(M) * p.R64 * 2);
   p.u_t = c.take(static_cast<size_t>(p.R) * pad8(M) * 2);
   p.xa_t = need_xa_t ? c.take(static_cast<size_t>(p.R) * pad8(M) * 2) : nullptr;
-  p.rpartials = p.rsplits > 1 ? static_cast<float*>(c.take(size_t(p.rsplits) * M * p.R * 4)) : nullptr;
-  p.wpart_db = p.wsplits > 1 ? static_cast<float*>(c.take(size_t(p.wsplits) * N * p.R * 4)) : nullptr;
-  p.wpart_da = p.wsplits > 1 ? static_cast<float*>(c.take(size_t(p.wsplits) * K * p.R * 4)) : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
@@ -192,13 +177,11 @@ BwdPlan plan_backward(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, bool
 struct F32FwdPlan {
   int64_t R, R3_64;
   int splits;
-  uint32_t* counters;
   void* xs;     // [M, 3K]  (hi, hi, lo)
   void* ws;     // [N, 3K]  (hi, lo, hi)
   void* as;     // [r, 3K]  (hi, lo, hi)
   void* bs;     // [N, 3R]  (hi, lo, hi)
   void* t_rows; // [M, pad64(3R)] (hi, hi, lo) of s.x.A^T
-  float* partials;
   size_t bytes;
 };
 
@@ -208,15 +191,11 @@ F32FwdPlan plan_forward_f32(void* ws, int64_t M, int64_t K, int64_t N, int64_t r
   p.R3_64 = pad64(3 * p.R);
   p.splits = rank_splits(M, 3 * K);
   Carve c(ws);
-  p.counters = static_cast<uint32_t*>(c.take(((M + 127) / 128) * 4));
   p.xs = c.take(static_cast<size_t>(M) * 3 * K * 2);
   p.ws = c.take(static_cast<size_t>(N) * 3 * K * 2);
   p.as = lora ? c.take(static_cast<size_t>(r) * 3 * K * 2) : nullptr;
   p.bs = lora ? c.take(static_cast<size_t>(N) * 3 * p.R * 2) : nullptr;
   p.t_rows = lora ? c.take(static_cast<size_t>(M) * p.R3_64 * 2) : nullptr;
-  p.partials = (lora && p.splits > 1)
-                   ? static_cast<float*>(c.take(size_t(p.splits) * M * p.R * 4))
-                   : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
@@ -224,8 +203,6 @@ F32FwdPlan plan_forward_f32(void* ws, int64_t M, int64_t K, int64_t N, int64_t r
 struct F32BwdPlan {
   int64_t R, R3_64, ld3;
   int rsplits, wsplits;
-  uint32_t* counters;  // [tm] U | [tm] T | [tn] dB | [tk] dA
-  size_t counter_bytes;
   void* dys_cols;  // [M, 3N] HHL
   void* xs_cols;   // [M, 3K] HHL
   void* dy_rows;   // [3M, N] HHL
@@ -237,9 +214,6 @@ struct F32BwdPlan {
   void* u_rows;    // [M, pad64(3R)] HLH (dx only)
   void* u_t;       // [R, ld3] HLH
   void* t_t;       // [R, ld3] HLH
-  float* rpartials;
-  float* wpart_db;
-  float* wpart_da;
   size_t bytes;
 };
 
@@ -251,10 +225,7 @@ F32BwdPlan plan_backward_f32(void* ws, int64_t M, int64_t K, int64_t N, int64_t 
   const int64_t big = 3 * (N > K ? N : K);
   p.rsplits = rank_splits(M, big);
   p.wsplits = wgrad_splits(3 * M, N > K ? N : K, 2);
-  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128, tk = (K + 127) / 128;
   Carve c(ws);
-  p.counter_bytes = static_cast<size_t>(2 * tm + tn + tk) * 4;
-  p.counters = static_cast<uint32_t*>(c.take(p.counter_bytes));
   p.dys_cols = c.take(static_cast<size_t>(M) * 3 * N * 2);
   p.xs_cols = c.take(static_cast<size_t>(M) * 3 * K * 2);
   p.dy_rows = c.take(static_cast<size_t>(3 * M) * N * 2);
@@ -266,9 +237,6 @@ F32BwdPlan plan_backward_f32(void* ws, int64_t M, int64_t K, int64_t N, int64_t 
   p.u_rows = dx ? c.take(static_cast<size_t>(M) * p.R3_64 * 2) : nullptr;
   p.u_t = c.take(static_cast<size_t>(p.R) * p.ld3 * 2);
   p.t_t = c.take(static_cast<size_t>(p.R) * p.ld3 * 2);
-  p.rpartials = p.rsplits > 1 ? static_cast<float*>(c.take(size_t(p.rsplits) * M * p.R * 4)) : nullptr;
-  p.wpart_db = p.wsplits > 1 ? static_cast<float*>(c.take(size_t(p.wsplits) * N * p.R * 4)) : nullptr;
-  p.wpart_da = p.wsplits > 1 ? static_cast<float*>(c.take(size_t(p.wsplits) * K * p.R * 4)) : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
@@ -393,8 +361,6 @@ int lora_forward_f32(const float* x, const float* w0, const float* a, const floa
     ra.ld_t = 0;
     ra.split_out = true;
     ra.split_pattern = kHHL;
-    ra.partials = p.partials;
-    ra.counters = p.counters;
     ra.splits = p.splits;
     ra.elt = Elt::kBF16;
     if ((rc = launch_rank(ra, s))) return rc;
@@ -444,8 +410,6 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   ru.ld_t = p.ld3;
   ru.split_out = true;
   ru.split_pattern = kHLH;
-  ru.partials = p.rpartials;
-  ru.counters = p.counters;
   ru.splits = rank_splits(M, 3 * N);
   if (ru.splits > p.rsplits) ru.splits = p.rsplits;
   ru.elt = Elt::kBF16;
@@ -460,7 +424,6 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   rt.ldl = 3 * K;
   rt.out_rows = nullptr;
   rt.out_t = p.t_t;
-  rt.counters = p.counters + tm;
   rt.splits = rank_splits(M, 3 * K);
   if (rt.splits > p.rsplits) rt.splits = p.rsplits;
   if ((rc = launch_rank(rt, s))) return rc;
@@ -504,8 +467,6 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   w[0].transposed = false;
   w[0].accumulate = accumulate;
   w[0].clip = clip;
-  w[0].partials = p.wpart_db;
-  w[0].counters = p.counters + 2 * tm;
   w[0].splits = p.wsplits;
   w[0].elt = Elt::kBF16;
   w[1] = w[0];
@@ -516,8 +477,6 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   w[1].out = da;
   w[1].ldo = K;
   w[1].transposed = true;
-  w[1].partials = p.wpart_da;
-  w[1].counters = p.counters + 2 * tm + tn;
   return launch_wgrad(w, 2, s);
 }
 
@@ -554,8 +513,6 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
   ra.ld_rows = p.R64;
   ra.out_t = p.u_t;
   ra.ld_t = pad8(M);
-  ra.partials = p.rpartials;
-  ra.counters = p.counters;
   ra.splits = rank_splits(M, N);
   ra.elt = elt;
   if (ra.splits > p.rsplits) ra.splits = p.rsplits;
@@ -572,7 +529,6 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     rt.ldl = K;
     rt.out_rows = nullptr;
     rt.out_t = p.xa_t;
-    rt.counters = p.counters + tm;
     rt.splits = rank_splits(M, K);
     if (rt.splits > p.rsplits) rt.splits = p.rsplits;
     if ((rc = launch_rank(rt, s))) return rc;
@@ -635,8 +591,6 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
   w[0].transposed = false;
   w[0].accumulate = accumulate;
   w[0].clip = clip_value;
-  w[0].partials = p.wpart_db;
-  w[0].counters = p.counters + 2 * tm;
   w[0].splits = p.wsplits;
   w[0].elt = elt;
   // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
@@ -648,8 +602,6 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
   w[1].out = da;
   w[1].ldo = K;
   w[1].transposed = true;
-  w[1].partials = p.wpart_da;
-  w[1].counters = p.counters + 2 * tm + tn;
   return launch_wgrad(w, 2, s);
 }
 
@@ -828,8 +780,6 @@ int lora_forward16(const void* x, const void* w0, const void* a, const void* b, 
   ra.ld_rows = p.R64;
   ra.out_t = saved_xa ? saved_xa : p.xa_t;
   ra.ld_t = pad8(M);
-  ra.partials = p.partials;
-  ra.counters = p.counters;
   ra.splits = p.splits;
   ra.elt = elt;
   if ((rc = launch_rank(ra, s))) return rc;
@@ -1204,8 +1154,6 @@ int mlora_qlora_forward_ex(const void* x, int scheme, const void* codes, const v
   ra.ld_rows = p.R64;
   ra.out_t = saved_xa ? saved_xa : p.xa_t;
   ra.ld_t = pad8(M);
-  ra.partials = p.partials;
-  ra.counters = p.counters;
   ra.splits = p.splits;
   ra.elt = Elt::kBF16;
   if ((rc = launch_rank(ra, s))) return rc;
@@ -1346,8 +1294,6 @@ int mlora_multi_lora_forward(const void* x, const void* w0, const void* a_stack,
   ra.ld_rows = p.R64;
   ra.out_t = nullptr;
   ra.ld_t = 0;
-  ra.partials = p.partials;
-  ra.counters = p.counters;
   ra.splits = p.splits;
   ra.elt = elt;
   ra.row_group = ids;
@@ -1387,8 +1333,6 @@ namespace {
 struct EmbedBwdPlan {
   FwdPlan rank;       // U = s dy.A^T rows [T, R64] (16-bit)
   void* gt;           // s B[idx]^T [R, pad8(T)]
-  float* wpart;       // weight-gradient partials
-  uint32_t* wcount;   // [ceil(D/128)]
   int wsplits;
   size_t bytes;
 };
@@ -1399,9 +1343,6 @@ EmbedBwdPlan plan_embed_bwd(void* ws, int64_t T, int64_t D, int64_t r) {
   Carve c(ws == nullptr ? nullptr : static_cast<uint8_t*>(ws) + p.rank.bytes);
   p.gt = c.take(static_cast<size_t>(p.rank.R) * pad8(T) * 2);
   p.wsplits = wgrad_splits(T, D, 1);
-  p.wcount = static_cast<uint32_t*>(c.take(static_cast<size_t>((D + 127) / 128) * 4));
-  p.wpart = p.wsplits > 1 ? static_cast<float*>(c.take(static_cast<size_t>(p.wsplits) * D * p.rank.R * 4))
-                          : nullptr;
   p.bytes = p.rank.bytes + align_up(c.off, 256);
   return p;
 }
@@ -1521,8 +1462,6 @@ int mlora_lora_embedding_backward(const void* dy, const int32_t* idx, const int3
   ra.ld_rows = p.rank.R64;
   ra.out_t = nullptr;
   ra.ld_t = 0;
-  ra.partials = p.rank.partials;
-  ra.counters = p.rank.counters;
   ra.splits = p.rank.splits;
   ra.elt = elt;
   if ((rc = launch_rank(ra, s))) return rc;
@@ -1546,8 +1485,6 @@ int mlora_lora_embedding_backward(const void* dy, const int32_t* idx, const int3
   w.transposed = true;
   w.accumulate = accumulate;
   w.clip = 0.f;
-  w.partials = p.wpart;
-  w.counters = p.wcount;
   w.splits = p.wsplits;
   w.elt = elt;
   return launch_wgrad(&w, 1, s);

@@ -7,20 +7,10 @@ namespace mlora {
 namespace {
 
 // bt[j, n] = b[n, j] for j < r, 0 for r <= j < R.  b is [N, r] with row stride ldb.
-// zero[0, n_zero) is cleared on the way (saves a memset launch before the
-// kernels that use those counters).
 template <typename T>
 __global__ void transpose_pad_kernel(const T* __restrict__ b, int64_t N, int64_t r, int64_t ldb,
-                                     T* __restrict__ bt, int64_t R, uint32_t* __restrict__ zero,
-                                     int64_t n_zero) {
+                                     T* __restrict__ bt, int64_t R) {
   __shared__ T tile[32][33];
-  {
-    const int64_t threads = static_cast<int64_t>(blockDim.x) * blockDim.y;
-    const int64_t nblocks = static_cast<int64_t>(gridDim.x) * gridDim.y;
-    const int64_t tid = (static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x) * threads +
-                        threadIdx.y * blockDim.x + threadIdx.x;
-    for (int64_t i = tid; i < n_zero; i += nblocks * threads) zero[i] = 0u;
-  }
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32;
   const int64_t j0 = static_cast<int64_t>(blockIdx.y) * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -133,18 +123,16 @@ int launch_split3_cols_t(const float* src, int64_t N, int64_t r, int64_t ld_src,
 }
 
 int launch_transpose_pad(const void* b, int64_t N, int64_t r, int64_t ldb, void* bt, int64_t R,
-                         Elt elt, cudaStream_t stream, uint32_t* zero, int64_t n_zero) {
+                         Elt elt, cudaStream_t stream) {
   dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((R + 31) / 32));
   dim3 block(32, 8);
   LaunchScope scope(kKindElementwise, stream);
   if (elt == Elt::kBF16)
     transpose_pad_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(b), N, r, ldb, static_cast<__nv_bfloat16*>(bt), R, zero,
-        n_zero);
+        static_cast<const __nv_bfloat16*>(b), N, r, ldb, static_cast<__nv_bfloat16*>(bt), R);
   else
     transpose_pad_kernel<__half><<<grid, block, 0, stream>>>(static_cast<const __half*>(b), N, r,
-                                                             ldb, static_cast<__half*>(bt), R,
-                                                             zero, n_zero);
+                                                             ldb, static_cast<__half*>(bt), R);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("transpose launch: ") + cudaGetErrorString(e));

@@ -157,9 +157,7 @@ struct RankArgs {
   // hi or lo part of the value as bit s of split_pattern says (0 = hi).
   bool split_out = false;
   uint32_t split_pattern = 0;
-  float* partials; // [splits, M, R] fp32 workspace
-  uint32_t* counters;  // [ceil(M/128)] zeroed
-  int splits;
+  int splits;      // 1, 2, 4 or 8 (cluster size of the split reduction)
   Elt elt;
   // stacked adapters: row m keeps only columns [g*group_cols, (g+1)*group_cols)
   // of out_rows, g = row_group[m] (nullptr: all columns)
@@ -182,9 +180,7 @@ struct WgradArgs {
   bool transposed;
   bool accumulate = false;  // out += result (after the clip) instead of out = result
   float clip;       // <= 0: no clip
-  float* partials;  // [splits, P, R]
-  uint32_t* counters;  // [ceil(P/128)] zeroed
-  int splits;
+  int splits;       // 1, 2, 4 or 8 (cluster size of the split reduction)
   Elt elt;
 };
 int wgrad_splits(int64_t M, int64_t P, int nproblems);
@@ -216,10 +212,8 @@ int launch_embed_da_f32(const int32_t* idx, const float* b, const float* dy, flo
                         cudaStream_t s);
 
 // ---------------------------------------------------------- elementwise ------
-// Also zeroes zero[0, n_zero) (split counters of the kernels that follow).
 int launch_transpose_pad(const void* b, int64_t N, int64_t r, int64_t ldb, void* bt, int64_t R,
-                         Elt elt, cudaStream_t stream, uint32_t* zero = nullptr,
-                         int64_t n_zero = 0);
+                         Elt elt, cudaStream_t stream);
 
 // Split-precision (bf16 hi/lo) copies of fp32 tensors; pattern bit s = 1 puts
 // the lo part in segment s.  Patterns: kHHL = (hi, hi, lo), kHLH = (hi, lo, hi).
