@@ -196,12 +196,16 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from metallora_b200 import _lib, kernels
+    from metallora_b200.distributed import bind_to_device
     from metallora_b200.layers import LoRALinear
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     if not kernels.is_metal_available():
         raise SystemExit("metallora_b200 CUDA extension unavailable on this device")
+    # this rank's host cores (and so its pinned buffers) on the GPU's NUMA node
+    affinity_before = bind_to_device(dev)
+    host_cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None
     M = WORKLOAD["tokens_per_gpu"]
     K, N, r, alpha = (WORKLOAD[k] for k in ("in_features", "out_features", "rank", "alpha"))
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -331,8 +335,11 @@ def run_ours(args, rank, world, local_rank):
         "clocks": sampler.summary(t_wall0, t_wall2),
         "e2e": e2e,
     }
+    line["config"]["host_cores_per_rank"] = host_cores
     if rank == 0:
-        if world == 1:  # the host baseline is taken at N=1 only
+        if world == 1:  # the host baseline is taken at N=1 only, on every host core
+            if affinity_before:
+                os.sched_setaffinity(0, affinity_before)
             line["cpu_baseline"] = cpu_baseline(args.cpu_tokens, args.cpu_reps)
         print(json.dumps(line), flush=True)
 
@@ -345,7 +352,7 @@ def run_e2e(args, layer, M, K, N, dev, world):
     import torch
     import torch.distributed as dist
 
-    steps = max(3, min(args.steps, 20))
+    steps = max(3, min(args.steps, 50))
     g = torch.Generator().manual_seed(99)
     xh = [torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory() for _ in range(2)]
     dyh = [torch.randn(M, N, generator=g).to(torch.bfloat16).pin_memory() for _ in range(2)]

@@ -5,6 +5,8 @@ all-reduce over the flat gradient buffer.  The reference is single-device; this
 is the multi-GPU layer of this implementation."""
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -23,6 +25,42 @@ def shard_tokens(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     flat = x.reshape(-1, *x.shape[2:]) if x.dim() > 2 else x
     b, e = shard_bounds(flat.shape[0], rank, world)
     return flat[b:e]
+
+
+def device_cpus(device) -> list[int] | None:
+    """The host cores NVML reports as closest to a CUDA device (its NUMA
+    node), or None when NVML or the device is unavailable.  Read-only: no
+    setting of the device changes."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            props = torch.cuda.get_device_properties(device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            n = os.cpu_count() or 1
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, (n + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # no NVML, no GPU, or a device NVML does not list
+        return None
+    cpus = [w * 64 + b for w, m in enumerate(words) for b in range(64)
+            if (int(m) >> b) & 1 and w * 64 + b < n]
+    return cpus or None
+
+
+def bind_to_device(device) -> list[int] | None:
+    """Restricts this process to the host cores of ``device``'s NUMA node, so
+    pinned host buffers it allocates afterwards sit next to the GPU's PCIe root
+    (one process per GPU: each rank's host<->device copies then use its own
+    socket's memory).  Returns the previous affinity (to restore), or None if
+    the cores are unknown."""
+    cpus = device_cpus(device)
+    if not cpus or not hasattr(os, "sched_setaffinity"):
+        return None
+    before = sorted(os.sched_getaffinity(0))
+    os.sched_setaffinity(0, cpus)
+    return before
 
 
 def average_gradients(flat_grad: torch.Tensor, group=None) -> None:

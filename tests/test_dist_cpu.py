@@ -62,3 +62,15 @@ def test_gloo_average_and_sync():
     for r in res:
         assert r[2] == [1.5] * 10                    # mean of 1 and 2
         assert r[3] is True and r[4] is False
+
+
+def test_device_cpus_without_gpu_is_none():
+    """NUMA binding degrades to a no-op where NVML or the device is missing."""
+    import torch
+
+    from metallora_b200.distributed import bind_to_device, device_cpus
+    if torch.cuda.is_available():
+        import pytest
+        pytest.skip("CPU-only check")
+    assert device_cpus(0) is None
+    assert bind_to_device(0) is None

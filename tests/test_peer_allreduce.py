@@ -32,3 +32,13 @@ def test_peer_allreduce_rejects_bad_arguments():
     assert lib.mlora_peer_allreduce(None, None, 0, 1, 1, None, 4, 1.0, None, None) == -1
     assert lib.mlora_peer_allreduce(8, 8, 2, 2, 1, 16, 4, 1.0, 8, None) == -1  # rank >= world
     assert lib.mlora_peer_allreduce(8, 8, 0, 1, 0, 16, 4, 1.0, 8, None) == -1  # seq 0
+
+
+@pytest.mark.gpu
+def test_device_cpus_reports_numa_cores(cuda):
+    """NVML names the host cores of the GPU's NUMA node (read-only query)."""
+    import os
+
+    from metallora_b200.distributed import device_cpus
+    cpus = device_cpus(cuda)
+    assert cpus and all(0 <= c < (os.cpu_count() or 1) for c in cpus)
