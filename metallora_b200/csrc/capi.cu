@@ -535,6 +535,36 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     xa_t = p.xa_t;
   }
 
+  // Weight gradients first: they read dy right after the rank pass over it
+  // (much of dy still in L2); the compute-bound dx GEMM follows.
+  WgradArgs w[2];
+  // db[n, j] = sum_m dy[m, n] * (s x A^T)[m, j]
+  w[0].big = dy;
+  w[0].st = xa_t;
+  w[0].ld_st = pad8(M);
+  w[0].M = M;
+  w[0].P = N;
+  w[0].r = r;
+  w[0].R = p.R;
+  w[0].ldb = N;
+  w[0].out = db;
+  w[0].ldo = r;
+  w[0].transposed = false;
+  w[0].accumulate = accumulate;
+  w[0].clip = clip_value;
+  w[0].splits = p.wsplits;
+  w[0].elt = elt;
+  // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
+  w[1] = w[0];
+  w[1].big = x;
+  w[1].st = p.u_t;
+  w[1].P = K;
+  w[1].ldb = K;
+  w[1].out = da;
+  w[1].ldo = K;
+  w[1].transposed = true;
+  if ((rc = launch_wgrad(w, 2, s))) return rc;
+
   if (dx != nullptr && qdx != nullptr) {
     QGemmArgs q = *qdx;
     q.w_mn_major = true;
@@ -576,33 +606,7 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     if ((rc = launch_gemm(ga, s))) return rc;
   }
 
-  WgradArgs w[2];
-  // db[n, j] = sum_m dy[m, n] * (s x A^T)[m, j]
-  w[0].big = dy;
-  w[0].st = xa_t;
-  w[0].ld_st = pad8(M);
-  w[0].M = M;
-  w[0].P = N;
-  w[0].r = r;
-  w[0].R = p.R;
-  w[0].ldb = N;
-  w[0].out = db;
-  w[0].ldo = r;
-  w[0].transposed = false;
-  w[0].accumulate = accumulate;
-  w[0].clip = clip_value;
-  w[0].splits = p.wsplits;
-  w[0].elt = elt;
-  // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
-  w[1] = w[0];
-  w[1].big = x;
-  w[1].st = p.u_t;
-  w[1].P = K;
-  w[1].ldb = K;
-  w[1].out = da;
-  w[1].ldo = K;
-  w[1].transposed = true;
-  return launch_wgrad(w, 2, s);
+  return MLORA_OK;
 }
 
 // ---- plain linear and merge plans ----------------------------------------
