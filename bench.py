@@ -223,12 +223,23 @@ def run_ours(args, rank, world, local_rank):
     from metallora_b200.distributed import PeerAllReduce
     n_a, n_b = layer.A.numel(), layer.B.numel()
     peer = PeerAllReduce.create(n_a + n_b, device=dev) if world > 1 else None
+    side = exchanged = None
     if peer is not None:
+        flat_grads = torch.empty(n_a + n_b, dtype=torch.float32, device=dev)
+        side, exchanged = torch.cuda.Stream(device=dev), torch.cuda.Event()
+
+        def exchange():
+            # started as soon as dA/dB are enqueued: runs beside the dx GEMM
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                peer.allreduce(flat_grads)
+            exchanged.record(side)
+
         # written over (not added to) every step: no zeroing between steps
         layer._grad_sink = (peer.buffer[:n_a].view(layer.A.shape),
-                            peer.buffer[n_a:].view(layer.B.shape), False)
-        flat_grads = torch.empty(n_a + n_b, dtype=torch.float32, device=dev)
-    exchange = "peer" if peer is not None else ("nccl" if world > 1 else "none")
+                            peer.buffer[n_a:].view(layer.B.shape), False, exchange)
+    exchange_kind = ("peer, overlapped with the dx GEMM" if peer is not None
+                     else ("nccl" if world > 1 else "none"))
 
     def step(xin, dyin):
         nonlocal flat_grads
@@ -238,7 +249,8 @@ def run_ours(args, rank, world, local_rank):
         y = layer(xin)
         y.backward(dyin)
         if peer is not None:
-            peer.allreduce(flat_grads)
+            # the next step's backward rewrites the exchanged buffer
+            torch.cuda.current_stream().wait_event(exchanged)
         elif world > 1:
             flat = torch.cat([layer.A.grad.reshape(-1), layer.B.grad.reshape(-1)]).float()
             dist.all_reduce(flat)
@@ -314,7 +326,7 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded N(0,1) activations/grads, N(0,1/4096) base, U(+-1/64) A, "
                 "N(0,0.02) B)",
         "config": {**WORKLOAD, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)",
-                   "grad_exchange": exchange,
+                   "grad_exchange": exchange_kind,
                    "l2": "inputs > L2 (~290 MB resident per GPU), no flush"},
         "tflops": round(total_tflops, 1),
         "roofline": {"bound": "tensor", "kernel": "lora_gemm_pair_kernel (tcgen05 cta_group::2)",

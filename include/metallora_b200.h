@@ -134,10 +134,16 @@ MLORA_API int mlora_lora_backward(const void* dy, const void* x, const void* w0,
 
 /* Flags of mlora_lora_backward_ex. */
 #define MLORA_BWD_ACCUMULATE 1 /* da += result, db += result (after the clip) */
+#define MLORA_BWD_DEFER_DX 2   /* everything but the dx GEMM; s.dy.B stays in the workspace */
+#define MLORA_BWD_DX_ONLY 4    /* only the dx GEMM, from a MLORA_BWD_DEFER_DX call's workspace */
 
 /* mlora_lora_backward with flags; with MLORA_BWD_ACCUMULATE the weight
  * gradients are added into da/db (gradient accumulation across micro-batches,
- * the reference trainer's gradient_accumulation_steps, trainer.py:82). */
+ * the reference trainer's gradient_accumulation_steps, trainer.py:82).
+ * MLORA_BWD_DEFER_DX then MLORA_BWD_DX_ONLY split one backward in two calls
+ * (same arguments, same workspace, same stream; 16-bit dtypes, dx set): the
+ * caller can start work that needs only da/db -- a data-parallel gradient
+ * exchange on another stream -- while the dx GEMM runs. */
 MLORA_API int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const void* a,
                                      const void* b, const void* saved_xa, void* dx, float* da,
                                      float* db, int64_t M, int64_t K, int64_t N, int64_t r,

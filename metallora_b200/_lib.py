@@ -22,6 +22,8 @@ MLORA_ERR_WORKSPACE = -4
 MLORA_ERR_DEVICE = -5
 
 BWD_ACCUMULATE = 1
+BWD_DEFER_DX = 2
+BWD_DX_ONLY = 4
 
 QUANT_NF4 = 1
 QUANT_INT4 = 2

@@ -480,90 +480,97 @@ int lora_backward_f32(const float* dy, const float* x, const float* w0, const fl
   return launch_wgrad(w, 2, s);
 }
 
+// Phases of the 16-bit backward (flags MLORA_BWD_DEFER_DX / MLORA_BWD_DX_ONLY).
+constexpr int kPhaseAll = 0, kPhaseDeferDx = 1, kPhaseDx = 2;
+
 // Backward of the 16-bit LoRA linear (dense W0, or a quantised W0 described
-// by qdx): rank projections, dx GEMM, dA/dB weight gradients.
+// by qdx): rank projections, dA/dB weight gradients, dx GEMM.
 int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* qdx,
                const void* a, const void* b, const void* saved_xa, void* dx, float* da,
                float* db, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                float clip_value, bool accumulate, int dtype, void* workspace,
-               size_t workspace_bytes, cudaStream_t s) {
+               size_t workspace_bytes, cudaStream_t s, int phase = kPhaseAll) {
   int rc;
   const BwdPlan need = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
     return fail(MLORA_ERR_WORKSPACE, "backward workspace needs " + std::to_string(need.bytes) + " bytes");
   const BwdPlan p = plan_backward(workspace, M, K, N, r, saved_xa == nullptr);
   const Elt elt = dtype == MLORA_DTYPE_BF16 ? Elt::kBF16 : Elt::kF16;
-  const int64_t tm = (M + 127) / 128, tn = (N + 127) / 128;
   const float scale = alpha / static_cast<float>(r);
 
-  // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection.
-  if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s))) return rc;
+  // kPhaseDeferDx stops before the dx GEMM (s.dy.B stays in the workspace);
+  // kPhaseDx runs only that GEMM, from the workspace of a deferred call.
+  if (phase != kPhaseDx) {
+    // B^T, zero-padded to R rows: the K-major operand of the U = s.dy.B projection.
+    if ((rc = launch_transpose_pad(b, N, r, r, p.bt, p.R, elt, s))) return rc;
 
-  RankArgs ra;
-  ra.x = dy;
-  ra.l = p.bt;
-  ra.M = M;
-  ra.K = N;
-  ra.r = p.R;
-  ra.R = p.R;
-  ra.ldx = N;
-  ra.ldl = N;
-  ra.scale = scale;
-  ra.out_rows = dx ? p.u_rows : nullptr;
-  ra.ld_rows = p.R64;
-  ra.out_t = p.u_t;
-  ra.ld_t = pad8(M);
-  ra.splits = rank_splits(M, N);
-  ra.elt = elt;
-  if (ra.splits > p.rsplits) ra.splits = p.rsplits;
-  if ((rc = launch_rank(ra, s))) return rc;
+    RankArgs ra;
+    ra.x = dy;
+    ra.l = p.bt;
+    ra.M = M;
+    ra.K = N;
+    ra.r = p.R;
+    ra.R = p.R;
+    ra.ldx = N;
+    ra.ldl = N;
+    ra.scale = scale;
+    ra.out_rows = dx ? p.u_rows : nullptr;
+    ra.ld_rows = p.R64;
+    ra.out_t = p.u_t;
+    ra.ld_t = pad8(M);
+    ra.splits = rank_splits(M, N);
+    ra.elt = elt;
+    if (ra.splits > p.rsplits) ra.splits = p.rsplits;
+    if ((rc = launch_rank(ra, s))) return rc;
 
-  const void* xa_t = saved_xa;
-  if (xa_t == nullptr) {
-    RankArgs rt = ra;
-    rt.x = x;
-    rt.l = a;
-    rt.K = K;
-    rt.r = r;
-    rt.ldx = K;
-    rt.ldl = K;
-    rt.out_rows = nullptr;
-    rt.out_t = p.xa_t;
-    rt.splits = rank_splits(M, K);
-    if (rt.splits > p.rsplits) rt.splits = p.rsplits;
-    if ((rc = launch_rank(rt, s))) return rc;
-    xa_t = p.xa_t;
+    const void* xa_t = saved_xa;
+    if (xa_t == nullptr) {
+      RankArgs rt = ra;
+      rt.x = x;
+      rt.l = a;
+      rt.K = K;
+      rt.r = r;
+      rt.ldx = K;
+      rt.ldl = K;
+      rt.out_rows = nullptr;
+      rt.out_t = p.xa_t;
+      rt.splits = rank_splits(M, K);
+      if (rt.splits > p.rsplits) rt.splits = p.rsplits;
+      if ((rc = launch_rank(rt, s))) return rc;
+      xa_t = p.xa_t;
+    }
+
+    // Weight gradients first: they read dy right after the rank pass over it
+    // (much of dy still in L2); the compute-bound dx GEMM follows.
+    WgradArgs w[2];
+    // db[n, j] = sum_m dy[m, n] * (s x A^T)[m, j]
+    w[0].big = dy;
+    w[0].st = xa_t;
+    w[0].ld_st = pad8(M);
+    w[0].M = M;
+    w[0].P = N;
+    w[0].r = r;
+    w[0].R = p.R;
+    w[0].ldb = N;
+    w[0].out = db;
+    w[0].ldo = r;
+    w[0].transposed = false;
+    w[0].accumulate = accumulate;
+    w[0].clip = clip_value;
+    w[0].splits = p.wsplits;
+    w[0].elt = elt;
+    // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
+    w[1] = w[0];
+    w[1].big = x;
+    w[1].st = p.u_t;
+    w[1].P = K;
+    w[1].ldb = K;
+    w[1].out = da;
+    w[1].ldo = K;
+    w[1].transposed = true;
+    if ((rc = launch_wgrad(w, 2, s))) return rc;
   }
-
-  // Weight gradients first: they read dy right after the rank pass over it
-  // (much of dy still in L2); the compute-bound dx GEMM follows.
-  WgradArgs w[2];
-  // db[n, j] = sum_m dy[m, n] * (s x A^T)[m, j]
-  w[0].big = dy;
-  w[0].st = xa_t;
-  w[0].ld_st = pad8(M);
-  w[0].M = M;
-  w[0].P = N;
-  w[0].r = r;
-  w[0].R = p.R;
-  w[0].ldb = N;
-  w[0].out = db;
-  w[0].ldo = r;
-  w[0].transposed = false;
-  w[0].accumulate = accumulate;
-  w[0].clip = clip_value;
-  w[0].splits = p.wsplits;
-  w[0].elt = elt;
-  // da[j, k] = sum_m (s dy B)[m, j] * x[m, k]
-  w[1] = w[0];
-  w[1].big = x;
-  w[1].st = p.u_t;
-  w[1].P = K;
-  w[1].ldb = K;
-  w[1].out = da;
-  w[1].ldo = K;
-  w[1].transposed = true;
-  if ((rc = launch_wgrad(w, 2, s))) return rc;
+  if (phase == kPhaseDeferDx) return MLORA_OK;
 
   if (dx != nullptr && qdx != nullptr) {
     QGemmArgs q = *qdx;
@@ -853,12 +860,19 @@ int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const 
                            float clip_value, int dtype, int flags, void* workspace,
                            size_t workspace_bytes, void* stream) {
   const bool accumulate = (flags & MLORA_BWD_ACCUMULATE) != 0;
-  if (flags & ~MLORA_BWD_ACCUMULATE) return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
+  if (flags & ~(MLORA_BWD_ACCUMULATE | MLORA_BWD_DEFER_DX | MLORA_BWD_DX_ONLY))
+    return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
+  if ((flags & MLORA_BWD_DEFER_DX) && (flags & MLORA_BWD_DX_ONLY))
+    return fail(MLORA_ERR_INVALID_ARG, "MLORA_BWD_DEFER_DX and MLORA_BWD_DX_ONLY exclude each other");
+  const int phase = (flags & MLORA_BWD_DEFER_DX) ? kPhaseDeferDx
+                    : (flags & MLORA_BWD_DX_ONLY) ? kPhaseDx : kPhaseAll;
   int rc = check_shapes(M, K, N, r, dtype);
   if (rc) return rc;
   if (!dy || !x || !a || !b || !da || !db) return fail(MLORA_ERR_INVALID_ARG, "NULL tensor pointer");
   if ((dx == nullptr) != (w0 == nullptr))
     return fail(MLORA_ERR_INVALID_ARG, "w0 and dx must be both set or both NULL");
+  if (phase != kPhaseAll && (dx == nullptr || dtype == MLORA_DTYPE_F32))
+    return fail(MLORA_ERR_INVALID_ARG, "a split backward needs dx and a 16-bit dtype");
   const void* ptrs[] = {dy, x, w0, a, b, saved_xa, dx, da, db};
   for (const void* q : ptrs)
     if (q && !aligned16(q)) return fail(MLORA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
@@ -870,7 +884,8 @@ int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const 
                              N, r, alpha, clip_value, accumulate, workspace, workspace_bytes,
                              static_cast<cudaStream_t>(stream));
   return backward16(dy, x, w0, nullptr, a, b, saved_xa, dx, da, db, M, K, N, r, alpha, clip_value,
-                    accumulate, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                    accumulate, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                    phase);
 }
 
 long long mlora_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }

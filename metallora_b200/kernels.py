@@ -176,6 +176,54 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
     return dx, da, db
 
 
+def lora_linear_bwd_split(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor,
+                          a: torch.Tensor, b: torch.Tensor, alpha: float,
+                          saved_xa: torch.Tensor | None, da_out: torch.Tensor,
+                          db_out: torch.Tensor, accumulate: bool = True):
+    """The 16-bit backward in two launches (MLORA_BWD_DEFER_DX, then
+    MLORA_BWD_DX_ONLY): enqueues everything but the dx GEMM -- dA/dB land in
+    ``da_out``/``db_out`` (fp32, added or written as ``accumulate`` says) --
+    and returns ``finish``, which enqueues the dx GEMM and returns dx.  Work
+    that needs only dA/dB (a gradient exchange on another stream) can be
+    started between the two and overlaps the GEMM."""
+    _need_cuda(dy2d, x2d, a, b)
+    dt = x2d.dtype
+    if dt == torch.float32:
+        raise ShapeError("the split backward takes bf16/fp16 tensors")
+    code = _dtype_code(x2d)
+    M, K = x2d.shape
+    N = dy2d.shape[1]
+    r = a.shape[0]
+    if r % 8:
+        raise ShapeError("gradient buffers need a rank that is a multiple of 8")
+    _check_2d("grad_output", dy2d, (M, N), dt)
+    _check_2d("W0", w0, (N, K), dt)
+    _check_2d("A", a, (r, K), dt)
+    _check_2d("B", b, (N, r), dt)
+    for name, t, shp in (("da_out", da_out, (r, K)), ("db_out", db_out, (N, r))):
+        if t.dtype != torch.float32 or tuple(t.shape) != shp or not t.is_contiguous():
+            raise ShapeError(f"{name} must be a contiguous fp32 tensor of shape {shp}")
+    dy2d, x2d, w0, a, b = (t.contiguous() for t in (dy2d, x2d, w0, a, b))
+    lib = _lib.load()
+    dx = torch.empty((M, K), dtype=dt, device=x2d.device)
+    ws = _workspace(lib.mlora_lora_backward_workspace_bytes(M, K, N, r, code), x2d.device)
+    flags = _lib.BWD_ACCUMULATE if accumulate else 0
+
+    def call(phase):
+        st = lib.mlora_lora_backward_ex(_ptr(dy2d), _ptr(x2d), _ptr(w0), _ptr(a), _ptr(b),
+                                        _ptr(saved_xa), _ptr(dx), _ptr(da_out), _ptr(db_out), M, K,
+                                        N, r, float(alpha), 0.0, code, flags | phase, _ptr(ws),
+                                        ws.numel(), _stream())
+        _lib.check(st, "mlora_lora_backward_ex")
+
+    call(_lib.BWD_DEFER_DX)
+
+    def finish() -> torch.Tensor:
+        call(_lib.BWD_DX_ONLY)
+        return dx
+    return finish
+
+
 def linear(x2d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """y = x.W^T (merged-weight forward, ops.py:106-114)."""
     _need_cuda(x2d, w)

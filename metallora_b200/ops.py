@@ -28,7 +28,10 @@ class _LoRALinearFn(torch.autograd.Function):
     their own dtype.  ``compute`` optionally supplies ready-made casts, and
     ``sink`` = (gA, gB) fp32 buffers receives the LoRA gradients by in-kernel
     accumulation instead of autograd (the trainer's flat gradient buffer);
-    (gA, gB, False) writes them over the buffers' contents instead."""
+    (gA, gB, False) writes them over the buffers' contents instead.  A fourth
+    element ``on_grads`` (a callable) is called once dA/dB are enqueued and
+    before the dx GEMM is: work it starts on another stream (a gradient
+    exchange) overlaps that GEMM."""
 
     @staticmethod
     def forward(ctx, x2d, w0, a, b, alpha, compute, sink):
@@ -45,11 +48,21 @@ class _LoRALinearFn(torch.autograd.Function):
         x2d, w0, a_c, b_c, saved = ctx.saved_tensors
         need_dx = ctx.needs_input_grad[0]
         sink = ctx.sink
-        dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a_c, b_c,
-                                        ctx.alpha, saved, 0.0, need_dx=need_dx,
-                                        da_out=sink[0] if sink else None,
-                                        db_out=sink[1] if sink else None,
-                                        accumulate=_sink_accumulates(sink))
+        on_grads = sink[3] if sink is not None and len(sink) > 3 else None
+        if on_grads is not None and need_dx and x2d.dtype != torch.float32:
+            finish = _k.lora_linear_bwd_split(dy.contiguous(), x2d, w0, a_c, b_c, ctx.alpha,
+                                              saved, sink[0], sink[1],
+                                              accumulate=_sink_accumulates(sink))
+            on_grads()
+            dx, da, db = finish(), sink[0], sink[1]
+        else:
+            dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a_c,
+                                            b_c, ctx.alpha, saved, 0.0, need_dx=need_dx,
+                                            da_out=sink[0] if sink else None,
+                                            db_out=sink[1] if sink else None,
+                                            accumulate=_sink_accumulates(sink))
+            if on_grads is not None:
+                on_grads()
         dw0 = None
         if ctx.needs_input_grad[1]:
             # trainable base weight (freeze_base=False): plain library GEMM
@@ -86,6 +99,8 @@ class _QLoRALinearFn(torch.autograd.Function):
                                          da_out=sink[0] if sink else None,
                                          db_out=sink[1] if sink else None,
                                          accumulate=_sink_accumulates(sink))
+        if sink is not None and len(sink) > 3 and sink[3] is not None:
+            sink[3]()
         if sink is not None:
             return dx, None, None, None, None, None, None
         da = da.to(ctx.ab_dtypes[0]) if ctx.needs_input_grad[1] else None
