@@ -9,9 +9,10 @@
 //
 // Both stream one large operand once from HBM, so they are bandwidth-bound:
 // each CTA keeps a deep TMA ring and several CTAs share an SM.  Work is split
-// along the reduction dimension across CTAs; partial sums (fp32) go to a
-// workspace and the last CTA of each output tile -- found with a counter --
-// adds them in fixed split order, so results are bitwise reproducible.
+// along the reduction dimension across the CTAs of one thread-block cluster;
+// their fp32 partial tiles are summed through distributed shared memory in
+// fixed split order (cluster_reduce below), so results are bitwise
+// reproducible and no global scratch or counter is needed.
 //
 // Warp roles: warp 0 TMA producer, warp 1 TMEM owner + UMMA issuer (M = 128,
 // N = R, K = 16), warps 2-5 epilogue (one accumulator row per thread).
