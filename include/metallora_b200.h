@@ -136,6 +136,7 @@ MLORA_API int mlora_lora_backward(const void* dy, const void* x, const void* w0,
 #define MLORA_BWD_ACCUMULATE 1 /* da += result, db += result (after the clip) */
 #define MLORA_BWD_DEFER_DX 2   /* everything but the dx GEMM; s.dy.B stays in the workspace */
 #define MLORA_BWD_DX_ONLY 4    /* only the dx GEMM, from a MLORA_BWD_DEFER_DX call's workspace */
+#define MLORA_BWD_GRADS_16BIT 8 /* da, db point to `dtype` (bf16/f16) buffers, not fp32 */
 
 /* mlora_lora_backward with flags; with MLORA_BWD_ACCUMULATE the weight
  * gradients are added into da/db (gradient accumulation across micro-batches,
@@ -143,7 +144,10 @@ MLORA_API int mlora_lora_backward(const void* dy, const void* x, const void* w0,
  * MLORA_BWD_DEFER_DX then MLORA_BWD_DX_ONLY split one backward in two calls
  * (same arguments, same workspace, same stream; 16-bit dtypes, dx set): the
  * caller can start work that needs only da/db -- a data-parallel gradient
- * exchange on another stream -- while the dx GEMM runs. */
+ * exchange on another stream -- while the dx GEMM runs.  MLORA_BWD_GRADS_16BIT
+ * stores da/db rounded to `dtype` (sums still accumulate in fp32), for
+ * callers whose A/B parameters are 16-bit (the reference keeps gradients in the
+ * parameters' dtype, ops.py:144-155). */
 MLORA_API int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const void* a,
                                      const void* b, const void* saved_xa, void* dx, float* da,
                                      float* db, int64_t M, int64_t K, int64_t N, int64_t r,

@@ -24,6 +24,7 @@ MLORA_ERR_DEVICE = -5
 BWD_ACCUMULATE = 1
 BWD_DEFER_DX = 2
 BWD_DX_ONLY = 4
+BWD_GRADS_16BIT = 8
 
 QUANT_NF4 = 1
 QUANT_INT4 = 2

@@ -489,7 +489,8 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
                const void* a, const void* b, const void* saved_xa, void* dx, float* da,
                float* db, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                float clip_value, bool accumulate, int dtype, void* workspace,
-               size_t workspace_bytes, cudaStream_t s, int phase = kPhaseAll) {
+               size_t workspace_bytes, cudaStream_t s, int phase = kPhaseAll,
+               bool grads16 = false) {
   int rc;
   const BwdPlan need = plan_backward(nullptr, M, K, N, r, saved_xa == nullptr);
   if (workspace == nullptr || workspace_bytes < need.bytes || !aligned16(workspace))
@@ -556,6 +557,7 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     w[0].ldo = r;
     w[0].transposed = false;
     w[0].accumulate = accumulate;
+    w[0].out16 = grads16;
     w[0].clip = clip_value;
     w[0].splits = p.wsplits;
     w[0].elt = elt;
@@ -860,8 +862,12 @@ int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const 
                            float clip_value, int dtype, int flags, void* workspace,
                            size_t workspace_bytes, void* stream) {
   const bool accumulate = (flags & MLORA_BWD_ACCUMULATE) != 0;
-  if (flags & ~(MLORA_BWD_ACCUMULATE | MLORA_BWD_DEFER_DX | MLORA_BWD_DX_ONLY))
+  if (flags & ~(MLORA_BWD_ACCUMULATE | MLORA_BWD_DEFER_DX | MLORA_BWD_DX_ONLY |
+                MLORA_BWD_GRADS_16BIT))
     return fail(MLORA_ERR_INVALID_ARG, "unknown flags");
+  const bool grads16 = (flags & MLORA_BWD_GRADS_16BIT) != 0;
+  if (grads16 && dtype == MLORA_DTYPE_F32)
+    return fail(MLORA_ERR_INVALID_ARG, "MLORA_BWD_GRADS_16BIT needs a 16-bit dtype");
   if ((flags & MLORA_BWD_DEFER_DX) && (flags & MLORA_BWD_DX_ONLY))
     return fail(MLORA_ERR_INVALID_ARG, "MLORA_BWD_DEFER_DX and MLORA_BWD_DX_ONLY exclude each other");
   const int phase = (flags & MLORA_BWD_DEFER_DX) ? kPhaseDeferDx
@@ -885,7 +891,7 @@ int mlora_lora_backward_ex(const void* dy, const void* x, const void* w0, const 
                              static_cast<cudaStream_t>(stream));
   return backward16(dy, x, w0, nullptr, a, b, saved_xa, dx, da, db, M, K, N, r, alpha, clip_value,
                     accumulate, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
-                    phase);
+                    phase, grads16);
 }
 
 long long mlora_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -335,10 +335,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 struct WgradProblem {
   long long M, P;
   int r, num_kb, tiles;
-  float* out;
+  float* out;     // fp32, or 16-bit (the operands' type) when out16
   long long ldo;
   int transposed;
   int accumulate;
+  int out16;
   float clip;
 };
 
@@ -404,16 +405,31 @@ __global__ void __launch_bounds__(kThreads, 2)
   const bool live = epi && prow < q.P;
   const bool clip = q.clip > 0.f;
   const long long step_j = q.transposed ? q.ldo : 1;
-  float* const out_row = q.transposed ? q.out + prow : q.out + prow * q.ldo;
+  const long long row_off = q.transposed ? prow : prow * q.ldo;
+  float* const out_row = q.out + row_off;
+  using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
   auto emit = [&](int j, float v0, float v1) {
     if (!live) return;
     if (clip) {
       v0 = fminf(fmaxf(v0, -q.clip), q.clip);
       v1 = fminf(fmaxf(v1, -q.clip), q.clip);
     }
+    const bool w0 = j < q.r, w1 = j + 1 < q.r;
+    if (q.out16) {  // gradients in the operands' 16-bit type (sum kept in fp32)
+      T* h0 = reinterpret_cast<T*>(q.out) + row_off + j * step_j;
+      T* h1 = h0 + step_j;
+      if (q.accumulate) {
+        const float o0 = w0 ? static_cast<float>(*h0) : 0.f;
+        const float o1 = w1 ? static_cast<float>(*h1) : 0.f;
+        v0 += o0;
+        v1 += o1;
+      }
+      if (w0) *h0 = static_cast<T>(v0);
+      if (w1) *h1 = static_cast<T>(v1);
+      return;
+    }
     float* d0 = out_row + j * step_j;
     float* d1 = d0 + step_j;
-    const bool w0 = j < q.r, w1 = j + 1 < q.r;
     if (q.accumulate) {  // both old values loaded before either store
       const float o0 = w0 ? *d0 : 0.f, o1 = w1 ? *d1 : 0.f;
       if (w0) *d0 = o0 + v0;
@@ -527,6 +543,7 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
     q.ldo = a.ldo;
     q.transposed = a.transposed ? 1 : 0;
     q.accumulate = a.accumulate ? 1 : 0;
+    q.out16 = a.out16 ? 1 : 0;
     q.clip = a.clip;
     if (i < n) total += q.tiles * p.splits;
     if (i == 0) p.ctas0 = q.tiles * p.splits;

@@ -121,11 +121,13 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
                     a: torch.Tensor, b: torch.Tensor, alpha: float,
                     saved_xa: torch.Tensor | None = None, clip_value: float = 0.0,
                     need_dx: bool = True, da_out: torch.Tensor | None = None,
-                    db_out: torch.Tensor | None = None, accumulate: bool = True):
+                    db_out: torch.Tensor | None = None, accumulate: bool = True,
+                    grad_dtype: torch.dtype | None = None):
     """(dx, dA, dB) of the LoRA linear for 2-D dy [M, N], x [M, K].
 
-    dA/dB are fp32 (master-gradient precision); clip_value > 0 clips them
-    elementwise after the full reduction (ops.py:155).  With ``da_out`` and
+    dA/dB are fp32 (master-gradient precision), or x's 16-bit dtype when
+    ``grad_dtype`` names it (written by the kernel, no cast launch); clip_value
+    > 0 clips them elementwise after the full reduction (ops.py:155).  With ``da_out`` and
     ``db_out`` (contiguous fp32 [r, K] / [N, r], rank a multiple of 8) the
     gradients are ADDED into those buffers (written over them when
     ``accumulate`` is False) and returned."""
@@ -161,8 +163,11 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
         da, db = da_out, db_out
         flags = _lib.BWD_ACCUMULATE if accumulate else 0
     else:
-        da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
-        db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
+        gdt = torch.float32
+        if grad_dtype is not None and grad_dtype == dt and dt != torch.float32:
+            gdt, flags = dt, _lib.BWD_GRADS_16BIT
+        da = torch.empty((r, K), dtype=gdt, device=x2d.device)
+        db = torch.empty((N, r), dtype=gdt, device=x2d.device)
     ws = _workspace(lib.mlora_lora_backward_workspace_bytes(M, K, N, r, code), x2d.device)
     st = lib.mlora_lora_backward_ex(_ptr(dy2d), _ptr(x2d), _ptr(w0) if need_dx else None,
                                     _ptr(a_p), _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da),

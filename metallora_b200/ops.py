@@ -56,11 +56,13 @@ class _LoRALinearFn(torch.autograd.Function):
             on_grads()
             dx, da, db = finish(), sink[0], sink[1]
         else:
+            same = ctx.ab_dtypes[0] == ctx.ab_dtypes[1] == x2d.dtype  # 16-bit grads direct
             dx, da, db = _k.lora_linear_bwd(dy.contiguous(), x2d, w0 if need_dx else None, a_c,
                                             b_c, ctx.alpha, saved, 0.0, need_dx=need_dx,
                                             da_out=sink[0] if sink else None,
                                             db_out=sink[1] if sink else None,
-                                            accumulate=_sink_accumulates(sink))
+                                            accumulate=_sink_accumulates(sink),
+                                            grad_dtype=x2d.dtype if same else None)
             if on_grads is not None:
                 on_grads()
         dw0 = None

@@ -61,3 +61,22 @@ def test_split_flags_rejected_for_fp32_and_conflicts():
     assert lib.mlora_lora_backward_ex(*head, _lib.DTYPE_BF16, _lib.BWD_DEFER_DX | _lib.BWD_DX_ONLY,
                                       None, 0, None) == -1
     assert b"exclude each other" in lib.mlora_last_error_message()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_16bit_grads_equal_rounded_fp32(cuda, dtype):
+    """MLORA_BWD_GRADS_16BIT writes dA/dB in the operands' dtype: the same
+    values as the fp32 gradients rounded once (what a cast would give)."""
+    M, K, N, r = 384, 256, 512, 16
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(M, K, device=cuda, generator=g).to(dtype)
+    w = (torch.randn(N, K, device=cuda, generator=g) / K ** 0.5).to(dtype)
+    a = (torch.randn(r, K, device=cuda, generator=g) / K ** 0.5).to(dtype)
+    b = (torch.randn(N, r, device=cuda, generator=g) * 0.1).to(dtype)
+    dy = torch.randn(M, N, device=cuda, generator=g).to(dtype)
+    dx1, da1, db1 = kernels.lora_linear_bwd(dy, x, w, a, b, 32.0)
+    dx2, da2, db2 = kernels.lora_linear_bwd(dy, x, w, a, b, 32.0, grad_dtype=dtype)
+    assert da2.dtype == dtype and db2.dtype == dtype
+    assert torch.equal(dx1, dx2)
+    assert torch.equal(da1.to(dtype), da2) and torch.equal(db1.to(dtype), db2)
