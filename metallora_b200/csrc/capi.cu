@@ -521,8 +521,10 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     ra.ld_t = pad8(M);
     ra.splits = rank_splits(M, N);
     ra.elt = elt;
+    ra.overlap_prev = true;  // set-up overlaps the transpose just launched
     if (ra.splits > p.rsplits) ra.splits = p.rsplits;
     if ((rc = launch_rank(ra, s))) return rc;
+    ra.overlap_prev = false;
 
     const void* xa_t = saved_xa;
     if (xa_t == nullptr) {

@@ -10,6 +10,8 @@ namespace {
 template <typename T>
 __global__ void transpose_pad_kernel(const T* __restrict__ b, int64_t N, int64_t r, int64_t ldb,
                                      T* __restrict__ bt, int64_t R) {
+  // the rank projection that follows may start its set-up now
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ T tile[32][33];
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32;
   const int64_t j0 = static_cast<int64_t>(blockIdx.y) * 32;

@@ -156,6 +156,9 @@ struct RankArgs {
   // (R columns each) and out_t[j, s*M + m] = part_s, where part_s is the bf16
   // hi or lo part of the value as bit s of split_pattern says (0 = hi).
   bool split_out = false;
+  // launched as a programmatic dependent of the kernel before it on the
+  // stream: set-up overlaps that kernel, loads wait for it to finish
+  bool overlap_prev = false;
   uint32_t split_pattern = 0;
   int splits;      // 1, 2, 4 or 8 (cluster size of the split reduction)
   Elt elt;

@@ -252,6 +252,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // A programmatic dependent launch gets here while the previous kernel may
+  // still run: nothing is read before it has completed (a no-op otherwise).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int tile = blockIdx.x;
   const uint32_t crank = cluster_ctarank();
@@ -460,22 +463,25 @@ bool set_smem_attr(K kern, size_t bytes) {
   return true;
 }
 
-// Launches `kern` with a (cx, cy, 1) cluster.
+// Launches `kern` with a (cx, cy, 1) cluster; `overlap_prev` also makes it a
+// programmatic dependent of the previous kernel on the stream.
 template <typename Kern, typename... Args>
 cudaError_t launch_clustered(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, unsigned cx,
-                             unsigned cy, Args... args) {
+                             unsigned cy, bool overlap_prev, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cx;
   attr[0].val.clusterDim.y = cy;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = overlap_prev ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
@@ -508,7 +514,7 @@ int launch_rank_typed(const RankArgs& a, cudaStream_t stream) {
   dim3 grid(static_cast<unsigned>((a.M + 127) / 128), static_cast<unsigned>(a.splits));
   LaunchScope scope(kKindRank, stream);
   cudaError_t e = launch_clustered(kern, grid, smem_bytes(R), stream, 1u,
-                                   static_cast<unsigned>(a.splits), tx, tl, p);
+                                   static_cast<unsigned>(a.splits), a.overlap_prev, tx, tl, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("rank launch: ") + cudaGetErrorString(e));
@@ -553,8 +559,8 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
   LaunchScope scope(kKindWgrad, stream);
   cudaError_t e = launch_clustered(kern, dim3(static_cast<unsigned>(total)), smem_bytes(R), stream,
-                                   static_cast<unsigned>(p.splits), 1u, tb[0], ts[0], tb[1], ts[1],
-                                   p);
+                                   static_cast<unsigned>(p.splits), 1u, false, tb[0], ts[0], tb[1],
+                                   ts[1], p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("wgrad launch: ") + cudaGetErrorString(e));
