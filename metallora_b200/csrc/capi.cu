@@ -560,6 +560,7 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     w[0].transposed = false;
     w[0].accumulate = accumulate;
     w[0].out16 = grads16;
+    w[0].overlap_prev = true;  // set-up overlaps the rank projection before it
     w[0].clip = clip_value;
     w[0].splits = p.wsplits;
     w[0].elt = elt;

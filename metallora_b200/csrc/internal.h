@@ -183,6 +183,7 @@ struct WgradArgs {
   bool transposed;
   bool accumulate = false;  // out += result (after the clip) instead of out = result
   bool out16 = false;       // out holds the operands' 16-bit type instead of fp32
+  bool overlap_prev = false;  // programmatic dependent of the previous kernel
   float clip;       // <= 0: no clip
   int splits;       // 1, 2, 4 or 8 (cluster size of the split reduction)
   Elt elt;

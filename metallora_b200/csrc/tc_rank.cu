@@ -264,6 +264,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     run_pipeline<R, false, kBF16>(smem, full_bar, empty_bar, done_bar, tmem, &tm_x, &tm_l,
                                   tile * 128, w.kb_begin, w.kb_end, p.status);
   }
+  // a programmatic dependent (the weight-gradient kernel) may start its set-up
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const bool epi = warp >= 2;
   const int row_local = static_cast<int>((warp & 3u) * 32 + lane_id());
   const long long row = static_cast<long long>(tile) * 128 + row_local;
@@ -384,6 +386,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // nothing is read before a programmatic predecessor has completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int which = (static_cast<int>(blockIdx.x) < p.ctas0) ? 0 : 1;
   const WgradProblem& q = p.prob[which];
@@ -559,8 +563,8 @@ int launch_wgrad_typed(const WgradArgs* probs, int n, cudaStream_t stream) {
   if (!set_smem_attr(kern, smem_bytes(R))) return MLORA_ERR_CUDA;
   LaunchScope scope(kKindWgrad, stream);
   cudaError_t e = launch_clustered(kern, dim3(static_cast<unsigned>(total)), smem_bytes(R), stream,
-                                   static_cast<unsigned>(p.splits), 1u, false, tb[0], ts[0], tb[1],
-                                   ts[1], p);
+                                   static_cast<unsigned>(p.splits), 1u, probs[0].overlap_prev,
+                                   tb[0], ts[0], tb[1], ts[1], p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("wgrad launch: ") + cudaGetErrorString(e));
