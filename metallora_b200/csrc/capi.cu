@@ -819,6 +819,7 @@ int lora_forward16(const void* x, const void* w0, const void* a, const void* b, 
   ga.w_mn_major = false;
   ga.elt = elt;
   ga.out_dtype = dtype;
+  ga.overlap_prev = true;  // only X2 (s.x.A^T) comes from the rank kernel just launched
   return launch_gemm(ga, s);
 }
 }  // namespace

@@ -74,6 +74,9 @@ struct GemmArgs {
   const int32_t* c_index = nullptr;  // optional: addend row for output row m = c_index[m]
   int64_t c_rows = 0;                // rows of the addend table (bound for c_index)
   float acc_scale = 1.f;    // D = acc_scale * (X.W^T + X2.W2^T) + C
+  // launched as a programmatic dependent of the previous kernel, which must
+  // have written nothing this GEMM reads except X2 (waited for before X2 loads)
+  bool overlap_prev = false;
   int64_t M, N, K;
   int64_t R = 0;   // extra reduction width, multiple of 16 (0 = none)
   int64_t w2_rows = 0;  // K-major: r (columns of w2); MN-major: r (rows of w2)

@@ -48,6 +48,7 @@ struct GemmParams {
   int num_kb_main, num_kb_extra, R;
   int tiles_m, tiles_n, num_tiles;
   int group_m;  // tile rows per raster group
+  int wait_prev;  // programmatic dependent: wait for the previous grid before X2 loads
   void* d;
   long long ldd;
   const void* c;  // optional addend, same type/layout as d (ldc)
@@ -219,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool armed[kStages];
       for (int s = 0; s < kStages; ++s) armed[s] = false, armed_parity[s] = 0;
       bool ok = true;
+      bool prev_done = false;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         int tm, tn;
         tile_coords(p, tile, tm, tn);
@@ -235,6 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           armed[stage] = true;
           armed_parity[stage] = phase;
           const bool extra = kb >= p.num_kb_main;
+          if (extra && p.wait_prev && !prev_done) {  // X2 comes from the previous grid
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            prev_done = true;
+          }
           const CUtensorMap* mx = extra ? &tm_x2 : &tm_x;
           const CUtensorMap* mw = extra ? &tm_w2 : &tm_w;
           const int k0 = (extra ? kb - p.num_kb_main : kb) * kBK;
@@ -413,6 +419,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool armed[kPairStages];
       for (int s = 0; s < kPairStages; ++s) armed[s] = false, armed_parity[s] = 0;
       bool ok = true;
+      bool prev_done = false;
       for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
         int tm, tn;
         tile_coords(p, tile, tm, tn);
@@ -432,6 +439,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           const uint32_t bar = lead_full + stage * 8u;
           const bool extra = kb >= p.num_kb_main;
+          if (extra && p.wait_prev && !prev_done) {  // X2 comes from the previous grid
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            prev_done = true;
+          }
           const CUtensorMap* mx = extra ? &tm_x2 : &tm_x;
           const CUtensorMap* mw = extra ? &tm_w2 : &tm_w;
           const int k0 = (extra ? kb - p.num_kb_main : kb) * kBK;
@@ -552,6 +563,30 @@ bool pair_enabled() {
   return on;
 }
 
+// Plain launch, or a programmatic dependent launch of the previous kernel on
+// the stream (`dependent`).
+template <typename Kern>
+cudaError_t launch_maybe_dependent(Kern kern, int grid, size_t smem, cudaStream_t stream, bool dependent,
+                            const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tx2,
+                            const CUtensorMap& tw2, const GemmParams& p) {
+  if (!dependent) {
+    kern<<<grid, kThreads, smem, stream>>>(tx, tw, tx2, tw2, p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tx2, tw2, p);
+  return e == cudaSuccess ? cudaGetLastError() : e;
+}
+
 template <typename Kern>
 int set_smem_attr(Kern kern, size_t bytes, bool* done) {
   int dev = 0;
@@ -617,6 +652,7 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.c_index = a.c_index;
   p.c_rows = a.c_rows;
   p.acc_scale = a.acc_scale;
+  p.wait_prev = (a.overlap_prev && a.R > 0) ? 1 : 0;
   {
     const int64_t vec = 16 / static_cast<int64_t>(sizeof(OutT));
     const bool d_ok = a.N % vec == 0 && a.ldd % vec == 0 &&
@@ -628,6 +664,7 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
   p.status = device_status_ptr();
 
   int rc;
+  cudaError_t err = cudaSuccess;
   if (pair) {
     auto kern = lora_gemm_pair_kernel<kWMN, kBF16, OutT>;
     static bool attr_set[64] = {};
@@ -654,18 +691,19 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
     }
     const int grid_pairs = p.num_tiles < pairs ? p.num_tiles : pairs;
     LaunchScope scope(kKindGemm, stream);
-    kern<<<2 * grid_pairs, kThreads, kPairSmemBytes, stream>>>(tx, tw, tx2, tw2, p);
+    err = launch_maybe_dependent(kern, 2 * grid_pairs, kPairSmemBytes, stream, p.wait_prev != 0, tx,
+                                 tw, tx2, tw2, p);
   } else {
     auto kern = lora_gemm_kernel<kWMN, kBF16, OutT>;
     static bool attr_set[64] = {};
     if ((rc = set_smem_attr(kern, kSmemBytes, attr_set))) return rc;
     const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
     LaunchScope scope(kKindGemm, stream);
-    kern<<<grid, kThreads, kSmemBytes, stream>>>(tx, tw, tx2, tw2, p);
+    err = launch_maybe_dependent(kern, grid, kSmemBytes, stream, p.wait_prev != 0, tx, tw, tx2, tw2,
+                                 p);
   }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_error(std::string("gemm launch: ") + cudaGetErrorString(e));
+  if (err != cudaSuccess) {
+    set_error(std::string("gemm launch: ") + cudaGetErrorString(err));
     return MLORA_ERR_CUDA;
   }
   return MLORA_OK;
