@@ -20,6 +20,12 @@ launch sequence instead of a Python function they cannot look into:
   (ops.py:162-172).
 * ``metal_lora::linear(x, w) -> y`` -- the merged-weight forward ``x.W^T``
   (ops.py:106-114).
+* ``metal_lora::qlora_fwd(x, codes, scales, zeros, prepared, scheme, group,
+  lean, a, b, alpha) -> (y, saved)`` and ``qlora_bwd(...) -> (dx, dA, dB)`` --
+  the same over a frozen NF4 / INT4 / INT8 base in the reference's packed
+  layout (kernels/lora_quantized.metal:29-164); autograd registered on
+  ``qlora_fwd``.  ``prepared`` is the weight's TMA-ready scale table
+  (``QuantizedWeight.prepared_scales()``), or None to build it in the call.
 
 Each operator has a fake (shape) implementation, so it traces without a GPU.
 The real implementations are the calls of :mod:`metallora_b200.kernels`; CPU
@@ -38,6 +44,7 @@ from torch.library import custom_op
 
 from . import kernels as _k
 from .exceptions import ShapeError
+from .quant import SCHEMES, QuantizedWeight
 
 _NS = "metal_lora"
 
@@ -172,6 +179,109 @@ def _linear_fake(x, w):
     if w.dim() != 2 or w.shape[1] != x.shape[-1]:
         raise ShapeError(f"W must be [out, {x.shape[-1]}], got {tuple(w.shape)}")
     return x.new_empty((*x.shape[:-1], w.shape[0]))
+
+
+# ------------------------------------------------------ quantised bases --
+
+def _qweight(x, codes, scales, zeros, prepared, scheme, group, lean) -> QuantizedWeight:
+    if scheme not in SCHEMES:
+        raise ShapeError(f"unknown scheme {scheme!r}; use one of {sorted(SCHEMES)}")
+    qw = QuantizedWeight(scheme, codes, scales, zeros, int(group), (codes.shape[0], x.shape[-1]),
+                         bool(lean))
+    if prepared is not None:
+        object.__setattr__(qw, "_prepared", prepared)
+    return qw
+
+
+def _check_q(x, codes, a, b, scheme):
+    K, N, r = x.shape[-1], codes.shape[0], a.shape[0]
+    per_byte = 1 if scheme == "int8" else 2
+    if codes.dim() != 2 or codes.shape[1] * per_byte != K:
+        raise ShapeError(f"codes must be [out, {K // per_byte}] for {scheme} with {K} inputs, "
+                         f"got {tuple(codes.shape)}")
+    if a.dim() != 2 or a.shape[1] != K:
+        raise ShapeError(f"A must be [rank, {K}], got {tuple(a.shape)}")
+    if b.dim() != 2 or tuple(b.shape) != (N, r):
+        raise ShapeError(f"B must be [{N}, {r}], got {tuple(b.shape)}")
+
+
+@custom_op(f"{_NS}::qlora_fwd", mutates_args=())
+def qlora_fwd(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+              zeros: torch.Tensor | None, prepared: torch.Tensor | None, scheme: str, group: int,
+              lean: bool, a: torch.Tensor, b: torch.Tensor,
+              alpha: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """LoRA forward over a quantised base: ``x.deq(W)^T + (alpha/r).(x.A^T).B^T``
+    (lora_quantized.metal:29-164 with the adapter of ops.py:91-94); bf16 x."""
+    _check_q(x, codes, a, b, scheme)
+    qw = _qweight(x, codes, scales, zeros, prepared, scheme, group, lean)
+    y, saved = _k.qlora_linear_fwd(x.reshape(-1, x.shape[-1]), qw, a.to(x.dtype), b.to(x.dtype),
+                                   alpha, save_xa=True)
+    return y.reshape(*x.shape[:-1], codes.shape[0]), saved
+
+
+@qlora_fwd.register_fake
+def _qlora_fwd_fake(x, codes, scales, zeros, prepared, scheme, group, lean, a, b, alpha):
+    _check_q(x, codes, a, b, scheme)
+    return (x.new_empty((*x.shape[:-1], codes.shape[0])),
+            x.new_empty(_saved_shape(x, a.shape[0])))
+
+
+def _qlora_fwd_setup(ctx, inputs, output):
+    x, codes, scales, zeros, prepared, scheme, group, lean, a, b, alpha = inputs
+    ctx.mark_non_differentiable(output[1])
+    ctx.save_for_backward(x, codes, scales, zeros, prepared, a, b, output[1])
+    ctx.meta = (scheme, group, lean, alpha)
+
+
+def _qlora_fwd_backward(ctx, dy, _dsaved):
+    x, codes, scales, zeros, prepared, a, b, saved = ctx.saved_tensors
+    scheme, group, lean, alpha = ctx.meta
+    need_dx = ctx.needs_input_grad[0]
+    dx, da, db = torch.ops.metal_lora.qlora_bwd(dy, x, codes, scales, zeros, prepared, scheme,
+                                                group, lean, a, b, saved, alpha, 0.0, need_dx)
+    return (dx if need_dx else None, None, None, None, None, None, None, None,
+            da.to(a.dtype) if ctx.needs_input_grad[8] else None,
+            db.to(b.dtype) if ctx.needs_input_grad[9] else None, None)
+
+
+qlora_fwd.register_autograd(_qlora_fwd_backward, setup_context=_qlora_fwd_setup)
+
+
+@custom_op(f"{_NS}::qlora_bwd", mutates_args=())
+def qlora_bwd(dy: torch.Tensor, x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+              zeros: torch.Tensor | None, prepared: torch.Tensor | None, scheme: str, group: int,
+              lean: bool, a: torch.Tensor, b: torch.Tensor, saved: torch.Tensor, alpha: float,
+              clip_value: float, need_dx: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dx, dA, dB) through a frozen quantised base; dA/dB fp32."""
+    _check_q(x, codes, a, b, scheme)
+    qw = _qweight(x, codes, scales, zeros, prepared, scheme, group, lean)
+    K, N = x.shape[-1], codes.shape[0]
+    sv = saved if saved.numel() > 0 else None
+    dx, da, db = _k.qlora_linear_bwd(dy.reshape(-1, N), x.reshape(-1, K), qw, a.to(x.dtype),
+                                     b.to(x.dtype), alpha, sv, clip_value, need_dx=need_dx)
+    dx = dx.reshape(x.shape) if need_dx else x.new_empty((0,))
+    return dx, da, db
+
+
+@qlora_bwd.register_fake
+def _qlora_bwd_fake(dy, x, codes, scales, zeros, prepared, scheme, group, lean, a, b, saved,
+                    alpha, clip_value, need_dx):
+    _check_q(x, codes, a, b, scheme)
+    dx = x.new_empty(x.shape) if need_dx else x.new_empty((0,))
+    return (dx, a.new_empty(a.shape, dtype=torch.float32),
+            b.new_empty(b.shape, dtype=torch.float32))
+
+
+def qlora_linear(x: torch.Tensor, qweight: QuantizedWeight, a: torch.Tensor, b: torch.Tensor,
+                 alpha: float = 16.0) -> torch.Tensor:
+    """``y`` of ``torch.ops.metal_lora.qlora_fwd`` for a ``QuantizedWeight``:
+    the traceable form of ``ops.qlora_forward``."""
+    qw = qweight
+    prepared = getattr(qw, "_prepared", None)
+    if prepared is None and qw.codes.is_cuda:
+        prepared = qw.prepared_scales()
+    return torch.ops.metal_lora.qlora_fwd(x, qw.codes, qw.scales, qw.zeros, prepared, qw.scheme,
+                                          qw.group, qw.lean, a, b, float(alpha))[0]
 
 
 def lora_linear(x: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: torch.Tensor,

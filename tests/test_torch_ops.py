@@ -172,3 +172,83 @@ def test_merge_and_linear_ops_match_kernels(cuda):
     assert torch.equal(y, kernels.linear(x, wm))
     # merged forward == unmerged forward (examples/basic_usage.py:114-140)
     assert _rel(y, torch_ops.lora_linear(x, w0, a, b, 32.0)) < 2e-2
+
+
+def _q_inputs(device, scheme, M=64, K=128, N=136, r=16):
+    g = torch.Generator(device=device).manual_seed(21)
+    per_byte = 1 if scheme == "int8" else 2
+    group = 64 if scheme == "nf4" else 128
+    x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+    codes = torch.randint(0, 256, (N, K // per_byte), device=device, generator=g,
+                          dtype=torch.int32).to(torch.uint8)
+    if scheme == "nf4":
+        scales = torch.rand(N, K // group, device=device, generator=g)
+        zeros = None
+    else:
+        scales = (torch.rand(N, K // group, device=device, generator=g) * 0.01).half()
+        zeros = torch.full((N, K // group), 8.0, device=device).half()
+    a = (torch.randn(r, K, device=device, generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = (torch.randn(N, r, device=device, generator=g) * 0.1).to(torch.bfloat16)
+    return x, codes, scales, zeros, group, a, b
+
+
+@pytest.mark.parametrize("scheme", ["nf4", "int4", "int8"])
+def test_qlora_fake_trace(scheme):
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    x, codes, scales, zeros, group, a, b = _q_inputs("cpu", scheme)
+    a = a.float().requires_grad_(True)
+    b = b.float().requires_grad_(True)
+    x.requires_grad_(True)
+
+    def step(x, codes, scales, zeros, a, b):
+        y = torch.ops.metal_lora.qlora_fwd(x, codes, scales, zeros, None, scheme, group, False,
+                                           a, b, 32.0)[0]
+        return (y,) + torch.autograd.grad(y.float().sum(), (x, a, b))
+
+    gm = make_fx(step, tracing_mode="fake")(x, codes, scales, zeros, a, b)
+    targets = [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+    assert "metal_lora.qlora_fwd.default" in targets
+    assert "metal_lora.qlora_bwd.default" in targets
+    outs = [o.meta["val"] for o in [n for n in gm.graph.nodes if n.op == "output"][0].args[0]]
+    assert [tuple(t.shape) for t in outs] == [(64, 136), (64, 128), (16, 128), (136, 16)]
+    with pytest.raises(ShapeError):
+        torch.ops.metal_lora.qlora_fwd(x.detach()[:, :64], codes, scales, zeros, None, scheme,
+                                       group, False, a.detach(), b.detach(), 32.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("scheme,lean", [("nf4", False), ("nf4", True), ("int4", False),
+                                         ("int8", False)])
+def test_qlora_custom_op_matches_module_path(cuda, scheme, lean):
+    """Quantised base: the operators equal the ops.qlora_forward autograd path
+    bit for bit (forward, dx, dA, dB)."""
+    from metallora_b200 import quant
+
+    g = torch.Generator(device=cuda).manual_seed(13)
+    M, K, N, r = 300, 256, 264, 16
+    w = torch.randn(N, K, device=cuda, generator=g) / K ** 0.5
+    qw = quant.quantize(w, scheme, lean=lean)
+    x = torch.randn(3, M // 3, K, device=cuda, generator=g).to(torch.bfloat16)
+    a = (torch.randn(r, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = (torch.randn(N, r, device=cuda, generator=g) * 0.1).to(torch.bfloat16)
+    dy = torch.randn(3, M // 3, N, device=cuda, generator=g).to(torch.bfloat16)
+    res = []
+    for fn in (lambda *t: ops.qlora_forward(t[0], qw, t[1], t[2], 32.0),
+               lambda *t: torch_ops.qlora_linear(t[0], qw, t[1], t[2], 32.0)):
+        xs, as_, bs = (t.detach().clone().requires_grad_(True) for t in (x, a, b))
+        y = fn(xs, as_, bs)
+        y.backward(dy)
+        res.append((y.detach(), xs.grad, as_.grad, bs.grad))
+    for t1, t2 in zip(*res):
+        assert t1.dtype == t2.dtype and t1.shape == t2.shape
+        assert torch.equal(t1, t2)
+    # against torch fp32 on the dequantised weight
+    wd = qw.dequantize(torch.float32)
+    xf = x.float().reshape(-1, K)
+    y_ref = xf @ wd.t() + (32.0 / r) * (xf @ a.float().t()) @ b.float().t()
+    assert _rel(res[1][0].reshape(-1, N), y_ref) < 2e-2
+    # the prepared scale table passed in or built in the call: same result
+    y2 = torch.ops.metal_lora.qlora_fwd(x, qw.codes, qw.scales, qw.zeros, None, scheme, qw.group,
+                                        lean, a, b, 32.0)[0]
+    assert torch.equal(y2, res[1][0])
