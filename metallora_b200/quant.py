@@ -122,3 +122,88 @@ def from_reference_layout(scheme: str, codes, scales, zeros, shape, group,
     return QuantizedWeight(scheme, codes.contiguous(), scales.contiguous(),
                            None if zeros is None else zeros.contiguous(), int(group),
                            (int(shape[0]), int(shape[1])), lean)
+
+
+# ------------------------------------------------------------ pack format --
+# The reference has no on-disk form for a quantised base.  This one keeps the
+# kernels' layout unchanged: one safetensors file holding, per weight,
+# ``{name}.codes`` (uint8), ``{name}.scales`` (fp32 absmax for NF4, fp16 for
+# INT4/INT8) and, for INT4/INT8, ``{name}.zeros`` (fp16); the safetensors
+# header metadata carries ``format`` = PACK_FORMAT and ``weights`` = a JSON map
+# name -> {scheme, group, out_features, in_features}.  Files written here load
+# without any conversion and are validated shape by shape on load.
+
+PACK_FORMAT = "metallora-qbase-1"
+
+
+def _expected_shapes(scheme: str, N: int, K: int, group: int):
+    per_byte = 1 if scheme == "int8" else 2
+    groups = -(-K // group)
+    codes = (N, -(-K // per_byte))
+    scale_dt = torch.float32 if scheme == "nf4" else torch.float16
+    return codes, (N, groups), scale_dt
+
+
+def pack_quantized(weights: dict[str, QuantizedWeight]) -> tuple[dict, dict]:
+    """(tensors, metadata) of the pack format for ``{name: QuantizedWeight}``;
+    tensors are copied to host memory."""
+    tensors: dict[str, torch.Tensor] = {}
+    meta = {}
+    for name, qw in weights.items():
+        tensors[f"{name}.codes"] = qw.codes.detach().contiguous().cpu()
+        tensors[f"{name}.scales"] = qw.scales.detach().contiguous().cpu()
+        if qw.zeros is not None:
+            tensors[f"{name}.zeros"] = qw.zeros.detach().contiguous().cpu()
+        meta[name] = {"scheme": qw.scheme, "group": int(qw.group),
+                      "out_features": int(qw.shape[0]), "in_features": int(qw.shape[1])}
+    import json
+    return tensors, {"format": PACK_FORMAT, "weights": json.dumps(meta, sort_keys=True)}
+
+
+def unpack_quantized(tensors: dict, metadata: dict, device=None,
+                     lean: bool = False) -> dict[str, QuantizedWeight]:
+    """Inverse of ``pack_quantized``; every tensor is checked against the
+    shape and dtype its scheme, group and weight shape imply."""
+    import json
+    if (metadata or {}).get("format") != PACK_FORMAT:
+        raise QuantizationError(f"not a {PACK_FORMAT} pack (metadata {metadata!r})")
+    out = {}
+    for name, m in json.loads(metadata["weights"]).items():
+        scheme, group = m["scheme"], int(m["group"])
+        N, K = int(m["out_features"]), int(m["in_features"])
+        if scheme not in SCHEMES:
+            raise QuantizationError(f"{name}: unknown scheme {scheme!r}")
+        codes_shape, scales_shape, scale_dt = _expected_shapes(scheme, N, K, group)
+        want = {"codes": (codes_shape, torch.uint8), "scales": (scales_shape, scale_dt)}
+        if scheme != "nf4":
+            want["zeros"] = (scales_shape, torch.float16)
+        got = {}
+        for part, (shape, dt) in want.items():
+            t = tensors.get(f"{name}.{part}")
+            if t is None:
+                raise QuantizationError(f"{name}: missing {part}")
+            if tuple(t.shape) != shape or t.dtype != dt:
+                raise QuantizationError(f"{name}.{part}: expected {shape} {dt}, got "
+                                        f"{tuple(t.shape)} {t.dtype}")
+            got[part] = t.to(device) if device is not None else t
+        out[name] = from_reference_layout(scheme, got["codes"], got["scales"], got.get("zeros"),
+                                          (N, K), group, lean=lean)
+    return out
+
+
+def save_quantized(weights: dict[str, QuantizedWeight], path) -> None:
+    """Writes ``{name: QuantizedWeight}`` to one safetensors file in the pack format."""
+    from safetensors.torch import save_file
+    tensors, meta = pack_quantized(weights)
+    save_file(tensors, str(path), metadata=meta)
+
+
+def load_quantized(path, device=None, lean: bool = False) -> dict[str, QuantizedWeight]:
+    """Reads a pack written by ``save_quantized`` (onto ``device`` if given)."""
+    from safetensors import safe_open
+    tensors = {}
+    with safe_open(str(path), framework="pt") as f:
+        meta = f.metadata()
+        for k in f.keys():
+            tensors[k] = f.get_tensor(k)
+    return unpack_quantized(tensors, meta, device=device, lean=lean)

@@ -67,6 +67,47 @@ def load_adapter(model: nn.Module, path: str | Path, adapter_name: str = "defaul
     return model
 
 
+def save_quantized_bases(model: nn.Module, path: str | Path, name: str = "base") -> None:
+    """Writes the quantised bases of every LoRA module of ``model`` (those made
+    by ``LoRALinear.quantize_base``) to ``{path}/{name}.safetensors`` in the
+    pack format of ``quant.save_quantized``, keyed by module name."""
+    from .quant import save_quantized
+
+    weights = {mname: m.qweight for mname, m in _lora_modules(model)
+               if getattr(m, "qweight", None) is not None}
+    if not weights:
+        raise AdapterError("the model has no quantised base to save")
+    save_path = Path(path)
+    save_path.mkdir(parents=True, exist_ok=True)
+    save_quantized(weights, save_path / f"{name}.safetensors")
+
+
+def load_quantized_bases(model: nn.Module, path: str | Path, name: str = "base",
+                         lean: bool = False) -> nn.Module:
+    """Installs the quantised bases saved by ``save_quantized_bases`` into the
+    matching LoRA modules (their dense W0 is released, as ``quantize_base``
+    does); each weight must match the module's [out, in] shape."""
+    from .quant import load_quantized
+
+    load_path = Path(path) / f"{name}.safetensors"
+    if not load_path.is_file():
+        raise AdapterError(f"quantised base file not found: {load_path}")
+    modules = dict(_lora_modules(model))
+    for mname, qw in load_quantized(load_path, lean=lean).items():
+        m = modules.get(mname)
+        if m is None:
+            raise AdapterError(f"no LoRA module named {mname!r} in the model")
+        if tuple(qw.shape) != (m.out_features, m.in_features):
+            raise AdapterError(f"{mname}: quantised base {tuple(qw.shape)} does not match "
+                               f"({m.out_features}, {m.in_features})")
+        dev = m.A.device
+        m.qweight = type(qw)(qw.scheme, qw.codes.to(dev), qw.scales.to(dev),
+                             None if qw.zeros is None else qw.zeros.to(dev), qw.group, qw.shape,
+                             qw.lean)
+        m.W0 = nn.Parameter(torch.empty(0, device=dev, dtype=m.W0.dtype), requires_grad=False)
+    return model
+
+
 def apply_lora_to_model(model: nn.Module, rank: int = 8, alpha: float = 16.0,
                         target_modules: list[str] | None = None, dropout: float = 0.0) -> nn.Module:
     """utils.py:54-80: replaces every ``nn.Linear`` whose dotted name contains a
