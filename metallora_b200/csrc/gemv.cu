@@ -28,6 +28,7 @@
 // last CTA of each row block sums them in split order, adds the rank-r term
 // and writes y.
 #include <algorithm>
+#include <atomic>
 #include <string>
 
 #include "internal.h"
@@ -836,11 +837,18 @@ int rank_small_splits(int64_t K) {
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
                       float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s) {
   // same shared-memory carveout as the decode kernel that follows, so SMs
-  // need no reconfiguration between the two
-  static const cudaError_t carve = cudaFuncSetAttribute(
-      lora_rank_small_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-      static_cast<int>(cudaSharedmemCarveoutMaxShared));
-  (void)carve;
+  // need no reconfiguration between the two (a hint, set once per device)
+  static std::atomic<bool> carve_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !carve_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(lora_rank_small_kernel,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+      cudaGetLastError();  // a hint only: clear the error, launch without it
+    else if (dev < 64)
+      carve_set[dev].store(true, std::memory_order_release);
+  }
   LaunchScope scope(kKindGemv, s);
   const int splits = rank_small_splits(K);
   const int64_t kslice = ((K + splits - 1) / splits + 7) / 8 * 8;

@@ -20,6 +20,7 @@
 //              global stores; each thread owns one output row.
 // Tiles are visited n-fastest so the CTAs resident at one time share W and X
 // tiles in L2.
+#include <atomic>
 #include <cstdlib>
 #include <string>
 
@@ -587,18 +588,20 @@ cudaError_t launch_maybe_dependent(Kern kern, int grid, size_t smem, cudaStream_
   return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
+// `done`: per-device flags (atomic: host threads may launch concurrently; a
+// repeated cudaFuncSetAttribute with the same value is harmless)
 template <typename Kern>
-int set_smem_attr(Kern kern, size_t bytes, bool* done) {
+int set_smem_attr(Kern kern, size_t bytes, std::atomic<bool>* done) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !done[dev]) {
+  if (dev >= 64 || !done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(bytes));
     if (e != cudaSuccess) {
       set_error(std::string("cudaFuncSetAttribute(gemm): ") + cudaGetErrorString(e));
       return MLORA_ERR_CUDA;
     }
-    done[dev] = true;
+    if (dev < 64) done[dev].store(true, std::memory_order_release);
   }
   return MLORA_OK;
 }
@@ -667,14 +670,15 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
   if (pair) {
     auto kern = lora_gemm_pair_kernel<kWMN, kBF16, OutT>;
-    static bool attr_set[64] = {};
-    static int max_pairs[64] = {};
+    static std::atomic<bool> attr_set[64];
+    static std::atomic<int> max_pairs[64];
     if ((rc = set_smem_attr(kern, kPairSmemBytes, attr_set))) return rc;
     int dev = 0;
     cudaGetDevice(&dev);
     int pairs = num_sms() / 2;
     if (dev < 64) {
-      if (max_pairs[dev] == 0) {
+      int known = max_pairs[dev].load(std::memory_order_acquire);
+      if (known == 0) {
         // clusters that can be resident at once (GPCs may leave an SM unpaired)
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
@@ -685,9 +689,10 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
           cudaGetLastError();
           n = pairs;
         }
-        max_pairs[dev] = n;
+        max_pairs[dev].store(n, std::memory_order_release);
+        known = n;
       }
-      pairs = max_pairs[dev];
+      pairs = known;
     }
     const int grid_pairs = p.num_tiles < pairs ? p.num_tiles : pairs;
     LaunchScope scope(kKindGemm, stream);
@@ -695,7 +700,7 @@ int launch_typed(const GemmArgs& a, cudaStream_t stream) {
                                  tw, tx2, tw2, p);
   } else {
     auto kern = lora_gemm_kernel<kWMN, kBF16, OutT>;
-    static bool attr_set[64] = {};
+    static std::atomic<bool> attr_set[64];
     if ((rc = set_smem_attr(kern, kSmemBytes, attr_set))) return rc;
     const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
     LaunchScope scope(kKindGemm, stream);
