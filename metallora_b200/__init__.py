@@ -6,6 +6,7 @@ from .exceptions import (  # noqa: F401
     AdapterError,
     ConfigurationError,
     DeviceError,
+    DistributedError,
     MetalLoRAError,
     QuantizationError,
     ShapeError,

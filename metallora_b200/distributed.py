@@ -10,6 +10,36 @@ import os
 import torch
 import torch.distributed as dist
 
+from .exceptions import DistributedError
+
+FAULT_ENV = "MLORA_FAULT_INJECT"
+
+
+class InjectedFault(RuntimeError):
+    """Raised by ``maybe_inject_fault`` on the rank and at the point that
+    MLORA_FAULT_INJECT names."""
+
+
+def maybe_inject_fault(point: str, rank: int | None = None) -> None:
+    """Host-side fault injection for failure-detection tests.
+
+    With MLORA_FAULT_INJECT = "<point>@<rank>" (several comma-separated), the
+    rank ``rank`` (default: this process's rank in the default group) raises
+    InjectedFault when it reaches ``point``.  Points: "before_allreduce" (the
+    flat-gradient all-reduce) and "before_peer_allreduce" (the NVLink
+    exchange).  The failure is made on the host, before anything is enqueued:
+    no kernel or collective of the failing rank is in flight, and no GPU is
+    faulted.  Unset, this is one environment lookup."""
+    spec = os.environ.get(FAULT_ENV)
+    if not spec:
+        return
+    if rank is None:
+        rank = dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+    for item in spec.split(","):
+        name, _, who = item.strip().partition("@")
+        if name == point and who.strip() != "" and int(who) == rank:
+            raise InjectedFault(f"injected fault at {point} on rank {rank}")
+
 
 def shard_bounds(n_tokens: int, rank: int, world: int) -> tuple[int, int]:
     """[begin, end) of this rank's contiguous token shard (sizes differ by at most 1)."""
@@ -65,17 +95,28 @@ def bind_to_device(device) -> list[int] | None:
 
 def average_gradients(flat_grad: torch.Tensor, group=None) -> None:
     """In-place mean of a flat gradient buffer over the process group (AVG on
-    NCCL; SUM then scale elsewhere)."""
+    NCCL; SUM then scale elsewhere).
+
+    A peer that raised, left or did not arrive ends the collective with the
+    process group's timeout; the error surfaces here as DistributedError
+    (gloo, and NCCL errors reported at the call).  On NCCL a timeout found
+    later by torch's watchdog aborts the communicator instead."""
     if not (dist.is_available() and dist.is_initialized()):
         return
     world = dist.get_world_size(group)
     if world == 1:
         return
-    if dist.get_backend(group) == "nccl":
-        dist.all_reduce(flat_grad, op=dist.ReduceOp.AVG, group=group)
-    else:
-        dist.all_reduce(flat_grad, group=group)
-        flat_grad.mul_(1.0 / world)
+    rank = dist.get_rank(group)
+    maybe_inject_fault("before_allreduce", rank)
+    try:
+        if dist.get_backend(group) == "nccl":
+            dist.all_reduce(flat_grad, op=dist.ReduceOp.AVG, group=group)
+        else:
+            dist.all_reduce(flat_grad, group=group)
+            flat_grad.mul_(1.0 / world)
+    except RuntimeError as e:
+        raise DistributedError(f"gradient all-reduce failed on rank {rank} of {world}: "
+                               f"{str(e).splitlines()[0] if str(e) else type(e).__name__}") from e
 
 
 def replicas_in_sync(t: torch.Tensor, group=None) -> bool:
@@ -148,6 +189,7 @@ class PeerAllReduce:
         contiguous fp32 tensor of ``numel`` elements on this GPU."""
         if out.dtype != torch.float32 or out.numel() != self.numel or not out.is_contiguous():
             raise ValueError("out must be a contiguous fp32 tensor of the buffer's size")
+        maybe_inject_fault("before_peer_allreduce", self.rank)
         self.seq += 1
         st = self._lib.load().mlora_peer_allreduce(
             self._hb.buffer_ptrs_dev, self._hf.buffer_ptrs_dev, self.rank, self.world, self.seq,

@@ -29,6 +29,12 @@ class QuantizationError(MetalLoRAError):
     """Quantization error (exceptions.py:29)."""
 
 
+class DistributedError(MetalLoRAError):
+    """A data-parallel collective failed: a peer rank raised, left or did not
+    arrive within the process group's timeout.  The reference is
+    single-device and has no counterpart."""
+
+
 def validate_rank(rank: int, min_rank: int = 1, max_rank: int = 256) -> None:
     """exceptions.py:34-39."""
     if not isinstance(rank, int):

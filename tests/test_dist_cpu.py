@@ -74,3 +74,70 @@ def test_device_cpus_without_gpu_is_none():
         pytest.skip("CPU-only check")
     assert device_cpus(0) is None
     assert bind_to_device(0) is None
+
+
+def test_fault_injection_spec(monkeypatch):
+    from metallora_b200.distributed import FAULT_ENV, InjectedFault, maybe_inject_fault
+    monkeypatch.delenv(FAULT_ENV, raising=False)
+    maybe_inject_fault("before_allreduce", 1)
+    monkeypatch.setenv(FAULT_ENV, "before_peer_allreduce@0, before_allreduce@1")
+    maybe_inject_fault("before_allreduce", 0)
+    maybe_inject_fault("before_peer_allreduce", 1)
+    with pytest.raises(InjectedFault):
+        maybe_inject_fault("before_allreduce", 1)
+    with pytest.raises(InjectedFault):
+        maybe_inject_fault("before_peer_allreduce", 0)
+
+
+def _fault_worker(rank, world, port, q, mode):
+    import datetime
+    import time
+
+    from metallora_b200.distributed import FAULT_ENV, InjectedFault
+    from metallora_b200.exceptions import DistributedError
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ[FAULT_ENV] = "before_allreduce@1"
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    t0 = time.monotonic()
+    try:
+        g = torch.ones(8)
+        average_gradients(g)
+        q.put((rank, "ok", time.monotonic() - t0))
+    except InjectedFault:
+        q.put((rank, "injected", time.monotonic() - t0))
+        if mode == "linger":
+            time.sleep(8)  # alive, but never joins the collective
+    except DistributedError:
+        q.put((rank, "distributed_error", time.monotonic() - t0))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+@pytest.mark.parametrize("mode", ["exit", "linger"])
+def test_peer_failure_surfaces_as_error(mode):
+    """A rank that fails on the host before the gradient all-reduce (injected
+    through MLORA_FAULT_INJECT) -- and then exits, or stays alive without
+    joining -- makes its peer's all-reduce end with DistributedError within
+    the process group's timeout instead of hanging."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_fault_worker, args=(r, world, port, q, mode))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict((r, (kind, dt)) for r, kind, dt in (q.get(timeout=90) for _ in range(world)))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    assert res[1][0] == "injected"
+    assert res[0][0] == "distributed_error"
+    assert res[0][1] < 30.0
