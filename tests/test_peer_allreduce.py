@@ -26,6 +26,51 @@ def test_peer_allreduce_world_one(cuda):
     assert _lib.device_status(reset=True) == 0
 
 
+@pytest.mark.gpu
+def test_peer_allreduce_wait_runs_out(cuda):
+    """Failure detection on the GPU without a fault: rank 0 of a two-rank
+    exchange whose peer never raises its flags (a flag that nothing sets)
+    gives up after the 2 s wait budget at the arrival barrier and again at the
+    exit barrier, records status 0x108 (peer timeout), skips the reduction and
+    returns; the context stays usable for the next call."""
+    import time
+
+    from metallora_b200 import _lib
+    n = 1024  # one CTA
+    buf0, buf1 = torch.randn(n, device=cuda), torch.randn(n, device=cuda)
+    flags0 = torch.zeros(4, dtype=torch.int32, device=cuda)
+    flags1 = torch.zeros(4, dtype=torch.int32, device=cuda)
+    counter = torch.zeros(1, dtype=torch.int32, device=cuda)
+    bufs = torch.tensor([buf0.data_ptr(), buf1.data_ptr()], dtype=torch.int64, device=cuda)
+    fl = torch.tensor([flags0.data_ptr(), flags1.data_ptr()], dtype=torch.int64, device=cuda)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    _lib.device_status(reset=True)
+    out = torch.full_like(buf0, 7.0)
+    t0 = time.monotonic()
+    st = lib.mlora_peer_allreduce(bufs.data_ptr(), fl.data_ptr(), 0, 2, 1, out.data_ptr(), n,
+                                  0.5, counter.data_ptr(), stream)
+    _lib.check(st, "mlora_peer_allreduce")
+    torch.cuda.synchronize()
+    elapsed = time.monotonic() - t0
+    assert _lib.device_status(reset=True) == 0x108
+    assert 3.0 < elapsed < 20.0            # two bounded waits of 2 s
+    assert bool((out == 7.0).all())        # no partial reduction was written
+    assert int(flags1[0]) == 2 and int(counter[0]) == 0  # exit flag raised, counter reset
+    # the context still works: a world-1 exchange right after
+    buf = torch.randn(n, device=cuda)
+    solo = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=cuda)
+    f_solo = torch.zeros(4, dtype=torch.int32, device=cuda)
+    fl_solo = torch.tensor([f_solo.data_ptr()], dtype=torch.int64, device=cuda)
+    out2 = torch.empty_like(buf)
+    st = lib.mlora_peer_allreduce(solo.data_ptr(), fl_solo.data_ptr(), 0, 1, 1, out2.data_ptr(),
+                                  n, 1.0, counter.data_ptr(), stream)
+    _lib.check(st, "mlora_peer_allreduce")
+    torch.cuda.synchronize()
+    assert torch.equal(out2, buf) and _lib.device_status(reset=True) == 0
+
+
 def test_peer_allreduce_rejects_bad_arguments():
     from metallora_b200 import _lib
     lib = _lib.load()
