@@ -105,11 +105,13 @@ def lora_linear_fwd(x2d: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: tor
     _check_2d("A", a, (r, K), dt)
     _check_2d("B", b, (N, r), dt)
     x2d, w0, a, b = (t.contiguous() for t in (x2d, w0, a, b))
-    lib = _lib.load()
     y = torch.empty((M, N), dtype=dt, device=x2d.device)
     saved = None
     if save_xa and dt != torch.float32:
         saved = torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=dt, device=x2d.device)
+    if M == 0:  # no tokens: empty output, nothing to launch
+        return y, saved
+    lib = _lib.load()
     ws = _workspace(lib.mlora_lora_forward_workspace_bytes(M, K, N, r, code), x2d.device)
     st = lib.mlora_lora_forward(_ptr(x2d), _ptr(w0), _ptr(a), _ptr(b), _ptr(y), _ptr(saved), M, K,
                                 N, r, float(alpha), code, _ptr(ws), ws.numel(), _stream())
@@ -168,6 +170,13 @@ def lora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tensor | No
             gdt, flags = dt, _lib.BWD_GRADS_16BIT
         da = torch.empty((r, K), dtype=gdt, device=x2d.device)
         db = torch.empty((N, r), dtype=gdt, device=x2d.device)
+    if M == 0:  # no tokens: the sums over tokens are zero; nothing to launch
+        if not (into and accumulate):
+            da.zero_()
+            db.zero_()
+        if into:
+            return dx, da, db
+        return dx, da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
     ws = _workspace(lib.mlora_lora_backward_workspace_bytes(M, K, N, r, code), x2d.device)
     st = lib.mlora_lora_backward_ex(_ptr(dy2d), _ptr(x2d), _ptr(w0) if need_dx else None,
                                     _ptr(a_p), _ptr(b_p), _ptr(saved_xa), _ptr(dx), _ptr(da),
@@ -213,6 +222,11 @@ def lora_linear_bwd_split(dy2d: torch.Tensor, x2d: torch.Tensor, w0: torch.Tenso
     dx = torch.empty((M, K), dtype=dt, device=x2d.device)
     ws = _workspace(lib.mlora_lora_backward_workspace_bytes(M, K, N, r, code), x2d.device)
     flags = _lib.BWD_ACCUMULATE if accumulate else 0
+    if M == 0:  # no tokens: zero gradients (unless added to), empty dx
+        if not accumulate:
+            da_out.zero_()
+            db_out.zero_()
+        return lambda: dx
 
     def call(phase):
         st = lib.mlora_lora_backward_ex(_ptr(dy2d), _ptr(x2d), _ptr(w0), _ptr(a), _ptr(b),
@@ -237,8 +251,10 @@ def linear(x2d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     N = w.shape[0]
     _check_2d("W", w, (N, K), x2d.dtype)
     x2d, w = x2d.contiguous(), w.contiguous()
-    lib = _lib.load()
     y = torch.empty((M, N), dtype=x2d.dtype, device=x2d.device)
+    if M == 0:
+        return y
+    lib = _lib.load()
     ws = _workspace(lib.mlora_linear_workspace_bytes(M, K, N, code), x2d.device)
     st = lib.mlora_linear(_ptr(x2d), _ptr(w), _ptr(y), M, K, N, code, _ptr(ws), ws.numel(),
                           _stream())
@@ -372,10 +388,12 @@ def qlora_linear_fwd(x2d: torch.Tensor, qw, a: torch.Tensor, b: torch.Tensor, al
     _check_2d("A", a, (r, K), torch.bfloat16)
     _check_2d("B", b, (N, r), torch.bfloat16)
     x2d, a, b = x2d.contiguous(), a.contiguous(), b.contiguous()
-    lib = _lib.load()
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x2d.device)
     saved = (torch.empty((rank_tile(r), (M + 7) // 8 * 8), dtype=torch.bfloat16,
                          device=x2d.device) if save_xa else None)
+    if M == 0:  # no tokens: empty output, nothing to launch
+        return y, saved
+    lib = _lib.load()
     ws = _workspace(_qlora_ws_bytes(lib, qw, M, K, N, r, backward=False), x2d.device)
     st = lib.mlora_qlora_forward_ex(_ptr(x2d), qw.code, _ptr(qw.codes), _ptr(qw.scales),
                                     _ptr(qw.zeros), _ptr(qw.prepared_scales()), qw.group, _ptr(a),
@@ -412,6 +430,13 @@ def qlora_linear_bwd(dy2d: torch.Tensor, x2d: torch.Tensor, qw, a: torch.Tensor,
     else:
         da = torch.empty((r, K), dtype=torch.float32, device=x2d.device)
         db = torch.empty((N, r), dtype=torch.float32, device=x2d.device)
+    if M == 0:  # no tokens: the sums over tokens are zero; nothing to launch
+        if not (into and accumulate):
+            da.zero_()
+            db.zero_()
+        if into:
+            return dx, da, db
+        return dx, da[:r_orig].contiguous(), db[:, :r_orig].contiguous()
     ws = _workspace(_qlora_ws_bytes(lib, qw, M, K, N, r, backward=True, need_w=need_dx),
                     x2d.device)
     st = lib.mlora_qlora_backward_ex(_ptr(dy2d), _ptr(x2d), qw.code, _ptr(qw.codes),
@@ -450,9 +475,11 @@ def multi_lora_fwd(x2d: torch.Tensor, w0: torch.Tensor | None, a_stack: torch.Te
     if ids.dtype != torch.int32 or ids.numel() != M:
         raise ShapeError("ids must be an int32 tensor with one entry per token")
     n = nr // r
-    lib = _lib.load()
     x2d, a_stack, b_stack = x2d.contiguous(), a_stack.contiguous(), b_stack.contiguous()
     y = torch.empty((M, N), dtype=x2d.dtype, device=x2d.device)
+    if M == 0:
+        return y
+    lib = _lib.load()
     code = _dtype_code(x2d)
     ws = _workspace(lib.mlora_multi_lora_forward_workspace_bytes(M, K, N, r, n, code), x2d.device)
     st = lib.mlora_multi_lora_forward(_ptr(x2d), _ptr(w0), _ptr(a_stack), _ptr(b_stack),
@@ -479,9 +506,11 @@ def lora_embedding_fwd(indices: torch.Tensor, table: torch.Tensor, a: torch.Tens
     _check_2d("B", b, (V, r), table.dtype)
     idx = _as_idx(indices)
     T = idx.numel()
-    lib = _lib.load()
     code = _dtype_code(table)
     out = torch.empty((T, D), dtype=table.dtype, device=table.device)
+    if T == 0:
+        return out.reshape(*indices.shape, D)
+    lib = _lib.load()
     ws = _workspace(lib.mlora_lora_embedding_workspace_bytes(T, D, r, code, 0), table.device)
     st = lib.mlora_lora_embedding_forward(_ptr(idx), _ptr(table.contiguous()), _ptr(a.contiguous()),
                                           _ptr(b.contiguous()), _ptr(out), T, V, D, r, float(alpha),
@@ -512,6 +541,11 @@ def lora_embedding_bwd(dy: torch.Tensor, indices: torch.Tensor, a: torch.Tensor,
     else:
         da = torch.empty((r, D), dtype=torch.float32, device=dy.device)
         db = torch.empty((V, r), dtype=torch.float32, device=dy.device)
+    if T == 0:  # no tokens: zero gradients (or nothing added); nothing to launch
+        if not flags:
+            da.zero_()
+            db.zero_()
+        return da, db
     ws = _workspace(lib.mlora_lora_embedding_workspace_bytes(T, D, r, code, 1), dy.device)
     st = lib.mlora_lora_embedding_backward(_ptr(dy2), _ptr(idx), _ptr(sorted_idx), _ptr(order),
                                            _ptr(a.contiguous()), _ptr(b.contiguous()), _ptr(da),
@@ -546,6 +580,8 @@ def lora_kv_cache_update(x2d: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, 
                            ("B_K", bk, (D_kv, r)), ("B_V", bv, (D_kv, r))):
         _check_2d(name, t, shape, x2d.dtype)
     del r_orig
+    if batch == 0:  # no sequences: nothing to write
+        return
     lib = _lib.load()
     code = _dtype_code(x2d)
     ws = _workspace(lib.mlora_lora_kv_cache_workspace_bytes(batch, D_in, D_kv, r, code), x2d.device)
