@@ -1,7 +1,7 @@
 """LoRA training (reference: python/metal_lora/trainer.py).
 
 Keeps the reference's ``TrainingConfig`` (trainer.py:71-100), ``TrainingState``
-(:103-112), ``LoRATrainer`` (``_training_step`` :228-249, ``train`` :251-289,
+(:103-112), ``LoRATrainableModule`` (:115-170), ``LoRATrainer`` (``_training_step`` :228-249, ``train`` :251-289,
 ``save``/``load`` :291-302), ``MetalAdamW`` (:21-68), ``train_lora`` (:305-318)
 and ``quick_finetune`` (:321-331).  The reference's trainer wraps the model in a
 module that never routes its LoRA tensors into the forward (trainer.py:133-170),
@@ -79,6 +79,82 @@ class TrainingState:
     learning_rate: float = 0.0
     tokens_seen: int = 0
     start_time: float = 0.0
+
+
+class LoRATrainableModule(nn.Module):
+    """Makes a model LoRA-trainable (reference: trainer.py:115-170).
+
+    Same constructor, default targets (q/v/k/o_proj), key names and counting
+    methods as the reference wrapper.  The reference keeps A/B in side
+    dictionaries that its forward never reads; here every targeted
+    ``nn.Linear`` becomes a ``LoRALinear``, so the factors are used by the
+    forward.  Like the reference (trainer.py:144-146), A starts as
+    N(0, 0.02^2) and B as zeros; the base weights are frozen
+    (trainer.py:147).  ``get_lora_params`` returns live references to the
+    modules' A/B under the keys ``{module}.lora_A`` / ``{module}.lora_B``
+    (trainer.py:149-154), which is also the key set of ``LoRATrainer.save``."""
+
+    def __init__(self, base_model: nn.Module, rank: int = 16, alpha: float = 32.0,
+                 target_modules: list[str] | None = None, dropout: float = 0.0):
+        super().__init__()
+        self.base_model = base_model
+        self.rank = rank
+        self.alpha = alpha
+        self.dropout = dropout
+        self.target_modules = target_modules or ["q_proj", "v_proj", "k_proj", "o_proj"]
+        self._apply_lora()
+
+    def _lora_layers(self) -> dict[str, LoRALinear]:
+        return {n: m for n, m in self.base_model.named_modules() if isinstance(m, LoRALinear)}
+
+    @torch.no_grad()
+    def _apply_lora(self) -> None:
+        before = set(self._lora_layers())
+        apply_lora_to_model(self.base_model, rank=self.rank, alpha=self.alpha,
+                            target_modules=self.target_modules, dropout=self.dropout)
+        for name, m in self._lora_layers().items():
+            if name not in before:
+                m.A.copy_(torch.randn(m.A.shape, dtype=torch.float32).to(m.A) * 0.02)
+                m.B.zero_()
+        for p in self.base_model.parameters():
+            p.requires_grad_(False)
+        for m in self._lora_layers().values():
+            m.A.requires_grad_(True)
+            m.B.requires_grad_(True)
+
+    def get_lora_params(self) -> dict[str, torch.Tensor]:
+        params = {}
+        for name, m in self._lora_layers().items():
+            params[f"{name}.lora_A"] = m.A
+            params[f"{name}.lora_B"] = m.B
+        return params
+
+    @torch.no_grad()
+    def set_lora_params(self, params: dict[str, torch.Tensor]) -> None:
+        """Copies ``{module}.lora_A`` / ``.lora_B`` values into the modules
+        (trainer.py:156-161); keys of other modules are ignored."""
+        layers = self._lora_layers()
+        for key, value in params.items():
+            for suffix, attr in ((".lora_A", "A"), (".lora_B", "B")):
+                if key.endswith(suffix) and key[:-len(suffix)] in layers:
+                    dst = getattr(layers[key[:-len(suffix)]], attr)
+                    if tuple(value.shape) != tuple(dst.shape):
+                        raise ConfigurationError(f"{key}: shape {tuple(value.shape)} does not "
+                                                 f"match {tuple(dst.shape)}")
+                    dst.copy_(value.to(dst.device, dst.dtype))
+
+    def num_trainable_params(self) -> int:
+        return sum(m.A.numel() + m.B.numel() for m in self._lora_layers().values())
+
+    def num_total_params(self) -> int:
+        """Base parameters plus the LoRA factors (trainer.py:166-167)."""
+        lora = {id(m.A) for m in self._lora_layers().values()} | \
+               {id(m.B) for m in self._lora_layers().values()}
+        base = sum(p.numel() for p in self.base_model.parameters() if id(p) not in lora)
+        return base + self.num_trainable_params()
+
+    def forward(self, *args, **kwargs):
+        return self.base_model(*args, **kwargs)
 
 
 class FlatLoRAParams:

@@ -76,3 +76,41 @@ def test_adapter_file_format(tmp_path):
     load_adapter(other, tmp_path, "mine")
     assert torch.equal(other[0]["q_proj"].B, model[0]["q_proj"].B)
     assert torch.equal(other[0]["q_proj"].A, model[0]["q_proj"].A)
+
+
+def test_lora_trainable_module_on_cpu():
+    """LoRATrainableModule (trainer.py:115-170): targets q/v/k/o_proj by
+    default, freezes the base, A ~ N(0, 0.02^2) and B = 0, reference key names,
+    set/get round trip and parameter counts."""
+    import torch
+    from torch import nn
+
+    from metallora_b200.layers import LoRALinear
+    from metallora_b200.trainer import LoRATrainableModule
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q_proj = nn.Linear(64, 32, bias=False)
+            self.v_proj = nn.Linear(64, 48, bias=False)
+            self.mlp = nn.Linear(64, 64)
+
+    torch.manual_seed(0)
+    base = Block()
+    n_base = sum(p.numel() for p in base.parameters())
+    wrapped = LoRATrainableModule(base, rank=8, alpha=16.0)
+    assert isinstance(base.q_proj, LoRALinear) and isinstance(base.v_proj, LoRALinear)
+    assert isinstance(base.mlp, nn.Linear) and not base.mlp.weight.requires_grad
+    params = wrapped.get_lora_params()
+    assert set(params) == {"q_proj.lora_A", "q_proj.lora_B", "v_proj.lora_A", "v_proj.lora_B"}
+    assert params["q_proj.lora_A"].shape == (8, 64) and params["v_proj.lora_B"].shape == (48, 8)
+    assert not params["q_proj.lora_B"].any()
+    assert 0.01 < float(params["q_proj.lora_A"].std()) < 0.03
+    assert wrapped.num_trainable_params() == 8 * (64 + 32) + 8 * (64 + 48)
+    assert wrapped.num_total_params() == n_base + wrapped.num_trainable_params()
+    new = {k: torch.full_like(v, 0.5) for k, v in params.items()}
+    wrapped.set_lora_params(new)
+    assert all(torch.equal(v, new[k]) for k, v in wrapped.get_lora_params().items())
+    trainable = {n for n, p in wrapped.named_parameters() if p.requires_grad}
+    assert trainable == {"base_model.q_proj.A", "base_model.q_proj.B",
+                         "base_model.v_proj.A", "base_model.v_proj.B"}
