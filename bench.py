@@ -146,46 +146,68 @@ class ClockSampler:
 
 # --------------------------------------------------------- CPU baseline ----
 
+def _bf16(a):
+    """Round-to-nearest-even to bf16, kept in fp32."""
+    a = np.asarray(a, np.float32)
+    b = a.view(np.uint32)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return b.astype(np.uint32).view(np.float32)
+
+
+def _cpu_inputs(tokens: int, seed: int = 0):
+    """The headline workload's inputs for `tokens` tokens (same distributions
+    as our arm), bf16-rounded, in fp32 host arrays."""
+    K, N, r = (WORKLOAD[k] for k in ("in_features", "out_features", "rank"))
+    rng = np.random.default_rng(seed)
+    return {"x": _bf16(rng.standard_normal((tokens, K))),
+            "W": _bf16(rng.standard_normal((N, K)) / 64),
+            "A": _bf16(rng.uniform(-1 / 64, 1 / 64, (r, K))),
+            "B": _bf16(rng.standard_normal((N, r)) * np.sqrt(0.02)),
+            "dy": _bf16(rng.standard_normal((tokens, N)))}
+
+
+def _cpu_step(inp):
+    """One step of the reference's CPU op path (forward, dx, dA, dB) in numpy."""
+    from oracle import lora_oracle as lo
+    alpha = WORKLOAD["alpha"]
+    lo.lora_forward(inp["x"], inp["W"], inp["A"], inp["B"], alpha)
+    lo.lora_grad_x(inp["dy"], inp["W"], inp["A"], inp["B"], alpha)
+    lo.lora_backward(inp["dy"], inp["x"], inp["A"], inp["B"], alpha, None)
+
+
+def _cpu_model() -> str:
+    try:
+        return next((ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo")
+                     if ln.startswith("model name")), "unknown")
+    except OSError:
+        return "unknown"
+
+
+def _blas_threads() -> int:
+    from threadpoolctl import threadpool_info
+    return max([i.get("num_threads", 1) for i in threadpool_info()
+                if i.get("user_api") == "blas"] or [1])
+
+
 def cpu_baseline(tokens: int, reps: int, seed: int = 0):
     """Times the numpy restatement of the reference's CPU op path (forward,
-    dx, dA, dB in fp32 on bf16-rounded inputs) on `tokens` tokens."""
-    from oracle import lora_oracle as lo
-    K, N, r, alpha = (WORKLOAD[k] for k in ("in_features", "out_features", "rank", "alpha"))
-    rng = np.random.default_rng(seed)
-
-    def bf16(a):
-        a = np.asarray(a, np.float32)
-        b = a.view(np.uint32)
-        b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
-        return b.astype(np.uint32).view(np.float32)
-
-    x = bf16(rng.standard_normal((tokens, K)))
-    W = bf16(rng.standard_normal((N, K)) / 64)
-    A = bf16(rng.uniform(-1 / 64, 1 / 64, (r, K)))
-    B = bf16(rng.standard_normal((N, r)) * np.sqrt(0.02))
-    dy = bf16(rng.standard_normal((tokens, N)))
-    from threadpoolctl import threadpool_info, threadpool_limits
+    dx, dA, dB in fp32 on bf16-rounded inputs) on `tokens` tokens; inputs are
+    built before the timed region."""
+    from threadpoolctl import threadpool_limits
+    inp = _cpu_inputs(tokens, seed)
     cores = len(os.sched_getaffinity(0))
     times = []
     # every host core (torchrun caps OpenBLAS at OMP_NUM_THREADS=1 otherwise)
     with threadpool_limits(limits=cores, user_api="blas"):
         for _ in range(reps + 1):
             t = time.perf_counter()
-            lo.lora_forward(x, W, A, B, alpha)
-            lo.lora_grad_x(dy, W, A, B, alpha)
-            lo.lora_backward(dy, x, A, B, alpha, None)
+            _cpu_step(inp)
             times.append(time.perf_counter() - t)
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()
-                     if i.get("user_api") == "blas"] or [1])
+        cores = _blas_threads()
     med = statistics.median(times[1:])  # first run warms caches/threads
-    try:
-        model = next((ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo")
-                      if ln.startswith("model name")), "unknown")
-    except OSError:
-        model = "unknown"
     return {"value": tokens / med, "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{tokens} tokens x {reps} reps of fwd+dx+dA+dB (numpy fp32 on bf16-rounded "
-                      f"inputs, OpenBLAS, {model})",
+                      f"inputs, OpenBLAS, {_cpu_model()})",
             "seconds_per_rep": med}
 
 
@@ -728,17 +750,27 @@ def run_sweep(args):
 # -------------------------------------------------------- reference arm ----
 
 def run_reference(args, rank):
+    """The reference's CPU path on the host cores: inputs for a sample of the
+    workload are built once, then W untimed and K timed steps of the numpy
+    restatement (forward, dx, dA, dB), every step on the same resident inputs
+    (as our arm's `value` leg keeps its inputs in HBM)."""
     if rank != 0:
         return
+    from threadpoolctl import threadpool_limits
     tokens = args.ref_tokens
-    for _ in range(args.warmup):
-        cpu_baseline(tokens, 1)
-    t = time.perf_counter()
-    res = None
-    for _ in range(args.steps):
-        res = cpu_baseline(tokens, 1)
-    elapsed = time.perf_counter() - t
+    inp = _cpu_inputs(tokens)
+    with threadpool_limits(limits=len(os.sched_getaffinity(0)), user_api="blas"):
+        for _ in range(args.warmup):
+            _cpu_step(inp)
+        t = time.perf_counter()
+        for _ in range(args.steps):
+            _cpu_step(inp)
+        elapsed = time.perf_counter() - t
+        cores = _blas_threads()
     value = tokens * args.steps / elapsed
+    res = {"cores": cores,
+           "sample": f"{tokens} tokens per step, {args.steps} steps of fwd+dx+dA+dB (numpy fp32 "
+                     f"on bf16-rounded inputs built once, OpenBLAS, {_cpu_model()})"}
     K, N, r = WORKLOAD["in_features"], WORKLOAD["out_features"], WORKLOAD["rank"]
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus,
@@ -770,7 +802,7 @@ def main():
                     default="lora")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--cpu-reps", type=int, default=3)
-    ap.add_argument("--ref-tokens", type=int, default=256)
+    ap.add_argument("--ref-tokens", type=int, default=2048)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
