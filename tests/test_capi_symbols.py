@@ -69,3 +69,49 @@ def test_invalid_arguments_rejected_before_launch():
     assert st == _lib.MLORA_ERR_INVALID_ARG
     with pytest.raises(Exception):
         _lib.check(_lib.MLORA_ERR_INVALID_ARG, "x")
+
+
+_SWEEP = r'''
+import ctypes as C, json, sys
+sys.path.insert(0, sys.argv[1])
+from metallora_b200 import _lib
+lib = _lib.load()
+host_only = {"mlora_device_supported", "mlora_launch_count", "mlora_profile_enable",
+             "mlora_version"}
+out = {}
+for name in sorted(_lib.SIGNATURES):
+    fn = getattr(lib, name)
+    if fn.restype is not C.c_int or name in host_only:
+        continue
+    for fill in (64, 0):
+        args = []
+        for t in fn.argtypes or []:
+            if t in (C.c_float, C.c_double):
+                args.append(1.0)
+            elif t in (C.c_int, C.c_int32, C.c_int64, C.c_uint32, C.c_uint64, C.c_size_t,
+                       C.c_longlong, C.c_long):
+                args.append(fill)
+            else:
+                args.append(None)
+        out.setdefault(name, []).append(int(fn(*args)))
+print(json.dumps(out))
+'''
+
+
+@pytest.mark.skipif(__import__("torch").cuda.is_available(),
+                    reason="a host-only check: run it where no GPU can be reached")
+def test_every_launching_entry_point_rejects_null_pointers():
+    """Every status-returning entry point, called with NULL pointers (and
+    sizes of 64 or 0), returns a negative status instead of touching memory or
+    a device; the sweep runs in a child process so a crash fails the test."""
+    import json
+    import subprocess
+    import sys
+    root = Path(__file__).resolve().parents[1]
+    p = subprocess.run([sys.executable, "-c", _SWEEP, str(root)], capture_output=True,
+                       text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-2000:]
+    res = json.loads(p.stdout.strip().splitlines()[-1])
+    assert "mlora_lora_forward" in res and "mlora_peer_allreduce" in res
+    bad = {k: v for k, v in res.items() if any(s >= 0 for s in v)}
+    assert not bad, bad
