@@ -26,6 +26,12 @@ launch sequence instead of a Python function they cannot look into:
   layout (kernels/lora_quantized.metal:29-164); autograd registered on
   ``qlora_fwd``.  ``prepared`` is the weight's TMA-ready scale table
   (``QuantizedWeight.prepared_scales()``), or None to build it in the call.
+* ``metal_lora::adamw_step(param, grad, m, v, gpu_state, lr, beta1, beta2,
+  eps, wd, grad_scale)`` -- the in-place AdamW update of one LoRA tensor
+  (kernels.py:615-643; operation order of kernels.py:333-343): param, m and v
+  are updated and grad is zeroed (mutated arguments, no outputs);
+  ``metal_lora::adam_state_step(gpu_state, beta1, beta2)`` advances the device
+  step state [t, beta1^t, beta2^t] (kernels.py:484-499).
 
 Each operator has a fake (shape) implementation, so it traces without a GPU.
 The real implementations are the calls of :mod:`metallora_b200.kernels`; CPU
@@ -282,6 +288,38 @@ def qlora_linear(x: torch.Tensor, qweight: QuantizedWeight, a: torch.Tensor, b: 
         prepared = qw.prepared_scales()
     return torch.ops.metal_lora.qlora_fwd(x, qw.codes, qw.scales, qw.zeros, prepared, qw.scheme,
                                           qw.group, qw.lean, a, b, float(alpha))[0]
+
+
+# ---------------------------------------------------------------- optimizer --
+
+@custom_op(f"{_NS}::adamw_step", mutates_args=("param", "grad", "m", "v"))
+def adamw_step(param: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
+               gpu_state: torch.Tensor, lr: float, beta1: float, beta2: float, eps: float,
+               wd: float, grad_scale: torch.Tensor | None = None) -> None:
+    """In-place AdamW step of one tensor (kernels.py:615-643): param, m, v
+    updated, grad zeroed; ``grad_scale`` (device float[2], element 0) scales
+    the gradient (the trainer's global-norm clip factor)."""
+    _k.lora_adamw_step_metal(param, grad, m, v, gpu_state, lr, beta1, beta2, eps, wd,
+                             grad_scale=grad_scale)
+
+
+@adamw_step.register_fake
+def _adamw_step_fake(param, grad, m, v, gpu_state, lr, beta1, beta2, eps, wd, grad_scale=None):
+    for name, t in (("grad", grad), ("m", m), ("v", v)):
+        if t.dtype != torch.float32 or t.numel() != param.numel():
+            raise ShapeError(f"{name} must be fp32 with param's size")
+    return None
+
+
+@custom_op(f"{_NS}::adam_state_step", mutates_args=("gpu_state",))
+def adam_state_step(gpu_state: torch.Tensor, beta1: float, beta2: float) -> None:
+    """gpu_state := [t+1, beta1^(t+1), beta2^(t+1)] on the device (kernels.py:484-499)."""
+    _k.persistent_gpu_state_step(gpu_state, beta1, beta2)
+
+
+@adam_state_step.register_fake
+def _adam_state_step_fake(gpu_state, beta1, beta2):
+    return None
 
 
 def lora_linear(x: torch.Tensor, w0: torch.Tensor, a: torch.Tensor, b: torch.Tensor,

@@ -252,3 +252,65 @@ def test_qlora_custom_op_matches_module_path(cuda, scheme, lean):
     y2 = torch.ops.metal_lora.qlora_fwd(x, qw.codes, qw.scales, qw.zeros, None, scheme, qw.group,
                                         lean, a, b, 32.0)[0]
     assert torch.equal(y2, res[1][0])
+
+
+def test_adamw_ops_trace_and_errors():
+    """The optimizer operators trace (mutating, no outputs) and keep the
+    kernels' argument rules; CPU tensors raise DeviceError."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    def step(p, g, m, v, st):
+        torch.ops.metal_lora.adam_state_step(st, 0.9, 0.999)
+        torch.ops.metal_lora.adamw_step(p, g, m, v, st, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+        return p, g, m, v, st
+
+    p = torch.randn(16, 8)
+    g, m, v = torch.randn(16, 8), torch.zeros(16, 8), torch.zeros(16, 8)
+    st = torch.tensor([0.0, 1.0, 1.0])
+    gm = make_fx(step, tracing_mode="fake")(p, g, m, v, st)
+    targets = [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+    assert "metal_lora.adamw_step.default" in targets
+    assert "metal_lora.adam_state_step.default" in targets
+    with pytest.raises(DeviceError):
+        torch.ops.metal_lora.adamw_step(p, g, m, v, st, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        fp, fg = torch.empty(16, 8), torch.empty(16, 8, dtype=torch.float16)
+        with pytest.raises(ShapeError):
+            torch.ops.metal_lora.adamw_step(fp, fg, fp.clone(), fp.clone(), torch.empty(3),
+                                            1e-3, 0.9, 0.999, 1e-8, 0.01)
+
+
+@pytest.mark.gpu
+def test_adamw_ops_match_kernel_calls(cuda):
+    """Two AdamW steps through the operators equal, bit for bit, the same
+    steps through kernels.lora_adamw_step_metal (bf16 and fp32 params)."""
+    from torch.library import opcheck
+
+    for dtype in (torch.bfloat16, torch.float32):
+        g0 = torch.Generator(device=cuda).manual_seed(17)
+        p0 = torch.randn(4096 + 5, device=cuda, generator=g0).to(dtype)
+        grads = [torch.randn(p0.numel(), device=cuda, generator=g0) for _ in range(2)]
+        out = []
+        for use_ops in (False, True):
+            p, m, v = p0.clone(), torch.zeros_like(p0, dtype=torch.float32), \
+                torch.zeros_like(p0, dtype=torch.float32)
+            st = kernels.persistent_gpu_state_init(device=cuda)
+            for gr in grads:
+                g = gr.clone()
+                if use_ops:
+                    torch.ops.metal_lora.adam_state_step(st, 0.9, 0.999)
+                    torch.ops.metal_lora.adamw_step(p, g, m, v, st, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+                else:
+                    kernels.persistent_gpu_state_step(st, 0.9, 0.999)
+                    kernels.lora_adamw_step_metal(p, g, m, v, st, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+                assert not g.any()  # the step zeroes the gradient
+            out.append((p, m, v, st))
+        for t1, t2 in zip(*out):
+            assert torch.equal(t1, t2)
+    p = torch.randn(256, device=cuda)
+    args = (p, torch.randn(256, device=cuda), torch.zeros(256, device=cuda),
+            torch.zeros(256, device=cuda), torch.tensor([1.0, 0.9, 0.999], device=cuda),
+            1e-3, 0.9, 0.999, 1e-8, 0.0)
+    opcheck(torch.ops.metal_lora.adamw_step.default, args,
+            test_utils=("test_schema", "test_faketensor"))
