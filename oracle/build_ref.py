@@ -10,7 +10,11 @@ the reference itself.  Inputs are read where they lie in the reference tree:
   (``LORA_FORWARD_FUSED_SOURCE`` :41, ``LORA_BACKWARD_SOURCE`` :249,
   ``LORA_ADAMW_SOURCE`` :314, ``LORA_MAINTENANCE_SOURCE`` :351), pulled out with
   ``ast`` (the module imports MLX, which is not installed, so it is parsed, not
-  imported) and written to ``oracle/_ref/gen/*.inc``.
+  imported) and written to ``oracle/_ref/gen/*.inc``;
+* from ``kernels/lora_kernels.metal``, the ``LoRAConfig`` struct (:12) and the
+  kernels ``lora_multi_adapter`` (:440) and ``lora_kv_cache_update`` (:514),
+  cut out by brace matching into ``oracle/_ref/gen/lora_kernels_subset.inc``
+  (the file as a whole needs simdgroup-matrix types the shim does not have).
 
 Everything this writes goes to ``oracle/_ref/`` (git-ignored).  Nothing here
 runs the reference's build system.  Usage::
@@ -58,6 +62,39 @@ def extract_inline_bodies(kernels_py: Path) -> dict[str, str]:
     return found
 
 
+# blocks of kernels/lora_kernels.metal compiled for the oracle, by their first words
+METAL_BLOCKS = ("struct LoRAConfig", "kernel void lora_multi_adapter",
+                "kernel void lora_kv_cache_update")
+
+
+def extract_metal_blocks(path: Path, heads=METAL_BLOCKS) -> str:
+    """The source text of each named struct / kernel of a .metal file, from
+    its first word to its matching closing brace (and ';' for a struct),
+    each preceded by a #line directive pointing at the original file."""
+    src = path.read_text()
+    out = []
+    for head in heads:
+        start = src.find(head)
+        if start < 0:
+            raise RuntimeError(f"{head!r} not found in {path}")
+        depth, end = 0, -1
+        for k in range(src.index("{", start), len(src)):
+            if src[k] == "{":
+                depth += 1
+            elif src[k] == "}":
+                depth -= 1
+                if depth == 0:
+                    end = k + 1
+                    break
+        if end < 0:
+            raise RuntimeError(f"unbalanced braces after {head!r} in {path}")
+        if head.startswith("struct"):
+            end = src.index(";", end) + 1
+        line = src.count("\n", 0, start) + 1
+        out.append(f'#line {line} "{path.name}"\n{src[start:end]}')
+    return "\n\n".join(out) + "\n"
+
+
 def build(reference: str | os.PathLike | None = None, quiet: bool = False) -> Path | None:
     """Build ``oracle/_ref/libmlref.so``; returns its path, or None when the
     reference tree is absent (the prebuilt library is then used as is)."""
@@ -73,6 +110,8 @@ def build(reference: str | os.PathLike | None = None, quiet: bool = False) -> Pa
     for const, fname in INLINE_BODIES.items():
         body = extract_inline_bodies(kernels_py)[const]
         (gen / fname).write_text(body)
+    (gen / "lora_kernels_subset.inc").write_text(
+        extract_metal_blocks(kernels_dir / "lora_kernels.metal"))
     lib = OUT / "libmlref.so"
     cmd = [
         "g++", "-O2", "-std=c++17", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared",

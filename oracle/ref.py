@@ -167,3 +167,38 @@ def optimizer_step(A, B, grad_A, grad_B, m_A, v_A, m_B, v_B, lr, b1, b2, eps, wd
                                F(lr), F(b1), F(b2), F(eps), F(wd), U(step), U(A.size),
                                U(B.size), U(accum_steps))
     return A, B, gA, gB, mA, vA, mB, vB
+
+
+def multi_adapter(x, W0, adapters_A, adapters_B, adapter_ids, alpha):
+    """kernels/lora_kernels.metal:440-508 (fp32): per-sample adapter over a
+    shared base.  x [B, S, K] (K <= 4096, a multiple of 4), W0 [D, K],
+    adapters_A [n, R, K] (R <= 128), adapters_B [n, D, R], adapter_ids [B]."""
+    x = np.ascontiguousarray(x, np.float32)
+    bsz, seq, K = x.shape
+    n, R, _ = adapters_A.shape
+    D = W0.shape[0]
+    W0, Aa, Ba = (np.ascontiguousarray(t, np.float32) for t in (W0, adapters_A, adapters_B))
+    ids = np.ascontiguousarray(adapter_ids, np.uint32)
+    out = np.zeros((bsz, seq, D), np.float32)
+    lib().mlref_multi_adapter(_p(x), _p(W0), _p(Aa), _p(Ba), _p(ids), _p(out), U(bsz), U(seq),
+                              U(K), U(D), U(R), U(n), F(alpha))
+    return out
+
+
+KV_MAX_SEQ = 8192  # the shader's fixed cache length (lora_kernels.metal:584)
+
+
+def kv_cache_update(x, W_K, W_V, A_K, B_K, A_V, B_V, k_cache, v_cache, cur_pos, alpha):
+    """kernels/lora_kernels.metal:514-586 (fp16 storage): projects one new token
+    per sequence x [B, D] and writes row ``cur_pos`` of the [B, 8192, D]
+    caches; returns the updated copies of (k_cache, v_cache)."""
+    x = np.ascontiguousarray(x, np.float16)
+    bsz, D = x.shape
+    R = A_K.shape[0]
+    ws = [np.ascontiguousarray(t, np.float16) for t in (W_K, W_V, A_K, B_K, A_V, B_V)]
+    kc = np.array(k_cache, np.float16, copy=True)
+    vc = np.array(v_cache, np.float16, copy=True)
+    assert kc.shape == (bsz, KV_MAX_SEQ, D) and vc.shape == kc.shape
+    lib().mlref_kv_cache_update(_p(x), *[_p(w) for w in ws], _p(kc), _p(vc), U(bsz),
+                                U(cur_pos), U(D), U(R), F(alpha))
+    return kc, vc

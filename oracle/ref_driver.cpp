@@ -7,6 +7,10 @@
 //                                    dequant_int4 :17, dequant_nf4 :22)
 //   * kernels/lora_train.metal      (lora_train_forward :27, lora_train_backward :90,
 //                                    lora_optimizer_step :158)
+//   * kernels/lora_kernels.metal    (LoRAConfig :12, lora_multi_adapter :440,
+//                                    lora_kv_cache_update :514; cut out by
+//                                    oracle/build_ref.py into
+//                                    oracle/_ref/gen/lora_kernels_subset.inc)
 //   * the inline MSL bodies of python/metal_lora/kernels.py
 //       LORA_FORWARD_FUSED_SOURCE :41  (the live Metal forward)
 //       LORA_BACKWARD_SOURCE      :249
@@ -34,6 +38,7 @@ thread_local bool msl_emul_final_pass = true;
 
 #include "lora_quantized.metal"
 #include "lora_train.metal"
+#include "lora_kernels_subset.inc"
 
 namespace mlx_inline {
 typedef float T;  // mx.fast.metal_kernel template T = x.dtype; pinned in float32
@@ -228,6 +233,40 @@ void mlref_optimizer_step(uint16_t* A, uint16_t* B, float* grad_A, float* grad_B
   for (uint tid = 0; tid < total; ++tid)
     lora_optimizer_step((half*)A, (half*)B, grad_A, grad_B, m_A, v_A, m_B, v_B, lr, b1, b2, eps,
                         wd, step, A_size, B_size, accum_steps, tid);
+}
+
+// ---- kernels/lora_kernels.metal ------------------------------------------------
+
+// lora_multi_adapter :440-508: one threadgroup of 256 per (256 outputs, token,
+// sample); two barriers -> three passes.  fp32 throughout.
+void mlref_multi_adapter(const float* x, const float* W0, const float* adapters_A,
+                         const float* adapters_B, const uint* adapter_ids, float* out, uint batch,
+                         uint seq, uint K, uint D, uint R, uint num_adapters, float alpha) {
+  LoRAConfig cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.batch_size = batch;
+  cfg.seq_len = seq;
+  cfg.in_features = K;
+  cfg.out_features = D;
+  cfg.rank = R;
+  cfg.alpha = alpha;
+  run_grid((D + 255) / 256, seq, batch, 256, 3, [&](uint3 tgid, uint lid) {
+    lora_multi_adapter(x, W0, adapters_A, adapters_B, adapter_ids, out, cfg, num_adapters, tgid,
+                       lid);
+  });
+}
+
+// lora_kv_cache_update :514-586: one new token per sequence; the caches are
+// [batch, 8192, D] half (the shader's fixed max_seq); two barriers -> three passes.
+void mlref_kv_cache_update(const uint16_t* x, const uint16_t* W_K, const uint16_t* W_V,
+                           const uint16_t* A_K, const uint16_t* B_K, const uint16_t* A_V,
+                           const uint16_t* B_V, uint16_t* K_cache, uint16_t* V_cache, uint batch,
+                           uint cur_pos, uint D, uint R, float alpha) {
+  run_grid((D + 255) / 256, 1, batch, 256, 3, [&](uint3 tgid, uint lid) {
+    lora_kv_cache_update((const half*)x, (const half*)W_K, (const half*)W_V, (const half*)A_K,
+                         (const half*)B_K, (const half*)A_V, (const half*)B_V, (half*)K_cache,
+                         (half*)V_cache, batch, cur_pos, D, R, alpha, tgid, lid);
+  });
 }
 
 }  // extern "C"
