@@ -3,7 +3,7 @@
  *
  * Drop-in boundary for the LoRA-linear hot path of Wilbatronic/MetalLora.  The
  * reference exposes this path as Python functions over MLX arrays
- * (python/metal_lora/ops.py, kernels.py, kernels/*.metal); every entry point
+ * (python/metal_lora/ops.py, kernels.py and the .metal files under kernels/); every entry point
  * below names the reference interface it replaces.
  *
  * Conventions

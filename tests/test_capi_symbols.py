@@ -115,3 +115,41 @@ def test_every_launching_entry_point_rejects_null_pointers():
     assert "mlora_lora_forward" in res and "mlora_peer_allreduce" in res
     bad = {k: v for k, v in res.items() if any(s >= 0 for s in v)}
     assert not bad, bad
+
+
+_C_CALLER = r'''
+#include <stdio.h>
+#include "metallora_b200.h"
+int main(void) {
+  printf("%d %s %zu %zu\n", mlora_version(), mlora_status_string(MLORA_OK),
+         mlora_lora_forward_workspace_bytes(8192, 4096, 4096, 16, MLORA_DTYPE_BF16),
+         mlora_lora_grads_static_scratch_bytes());
+  return mlora_lora_forward(NULL, NULL, NULL, NULL, NULL, NULL, 128, 256, 256, 16, 32.0f,
+                            MLORA_DTYPE_BF16, NULL, 0, NULL) < 0 ? 0 : 1;
+}
+'''
+
+
+@pytest.mark.skipif(__import__("shutil").which("gcc") is None, reason="gcc not installed")
+def test_plain_c_caller(tmp_path):
+    """The header is valid C99 (-Wall -Wextra -pedantic -Werror) and a plain C
+    program links the library and calls its host-only entry points (no GPU
+    needed), getting the same answers as the Python binding."""
+    import subprocess
+    root = Path(__file__).resolve().parents[1]
+    inc, libdir = root / "include", _lib.LIB_PATH.parent
+    subprocess.run(["gcc", "-fsyntax-only", "-std=c99", "-Wall", "-Wextra", "-pedantic",
+                    "-Werror", "-x", "c", str(HEADER)], check=True)
+    src = tmp_path / "caller.c"
+    src.write_text(_C_CALLER)
+    exe = tmp_path / "caller"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{inc}", str(src), f"-L{libdir}",
+                    "-lmetallora_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    version, status, fwd_ws, scratch = out.stdout.split()
+    lib = _lib.load()
+    assert int(version) == lib.mlora_version() and status == "ok"
+    assert int(fwd_ws) == lib.mlora_lora_forward_workspace_bytes(8192, 4096, 4096, 16,
+                                                                 _lib.DTYPE_BF16)
+    assert int(scratch) == lib.mlora_lora_grads_static_scratch_bytes()
