@@ -69,12 +69,36 @@ def flops_per_token(K, N, r):
     return fwd + bwd
 
 
-# DRAM traffic of one lora_gemm_pair_kernel launch of the headline workload
-# (forward, M 8192, K 4096, N 4096, rank block 16), from one ncu capture:
-# dram__bytes_read.sum 111.2 MB + dram__bytes_write.sum 46.4 MB.  Algorithmic
-# bytes: x 64 MiB + W0 32 MiB + rank block 1.125 MiB read, y 64 MiB written.
-GEMM_TRAFFIC_BYTES = 157.5e6
+# The ncu capture of one lora_gemm_pair_kernel launch of this workload
+# (forward y); its dram__bytes_read.sum / dram__bytes_write.sum rows give the
+# roofline line's measured traffic.  Algorithmic bytes of that launch: x
+# 64 MiB + W0 32 MiB + rank block (s.x.A^T 1 MiB, B 128 KiB) read, y 64 MiB
+# written.
+GEMM_PROFILE = Path("profiles") / "lora_gemm_pair_kernel_fwd_bf16_m8192_k4096_n4096_r16.md"
 GEMM_ALGORITHMIC_BYTES = (64 + 32 + 1.125 + 64) * 2 ** 20
+
+
+def profile_traffic(rel_path: Path):
+    """(bytes per launch, source) from the dram__bytes_read.sum and
+    dram__bytes_write.sum rows ("| metric | 111.2 MB |") of a committed ncu
+    summary, or (None, reason)."""
+    f = ROOT / rel_path
+    if not f.is_file():
+        return None, f"{rel_path} missing"
+    vals = {}
+    for ln in f.read_text().splitlines():
+        cells = [c.strip() for c in ln.strip().strip("|").split("|")]
+        if len(cells) >= 2 and cells[0] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            num, _, unit = cells[1].partition(" ")
+            scale = {"B": 1.0, "KB": 1e3, "MB": 1e6, "GB": 1e9}.get(unit.strip(), None)
+            try:
+                vals[cells[0]] = float(num) * scale
+            except (TypeError, ValueError):
+                pass
+    if len(vals) != 2:
+        return None, f"{rel_path} has no dram__bytes_read/write rows"
+    return sum(vals.values()), (f"{rel_path}: ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                "of one forward launch of this workload")
 
 
 def load_peaks():
@@ -86,6 +110,21 @@ def load_peaks():
                 "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
             "source": "fallback"}
+
+
+def pick_peak(peaks, clocks, kind="bf16"):
+    """The roofline denominator for a kernel timed under ``clocks`` (the
+    sampler's summary of the timed region): the burst figure when no sample
+    saw the power cap (a short region at full clock), the power-capped
+    sustained figure otherwise.  Returns (peak, name, why)."""
+    if kind == "hbm":
+        return peaks["hbm_gbs"], f"{peaks['source']} hbm_gbs", "HBM copy bandwidth"
+    capped = "sw_power_cap" in (clocks.get("reasons") or [])
+    if capped:
+        return (peaks["bf16_tflops_sustained"], f"{peaks['source']} bf16_tflops_sustained",
+                "sw_power_cap active during the timed region")
+    return (peaks["bf16_tflops"], f"{peaks['source']} bf16_tflops (burst)",
+            f"no power-cap sample in the timed region (SM {clocks.get('sm_mhz')} MHz)")
 
 
 # --------------------------------------------------------------- clocks ----
@@ -213,6 +252,61 @@ def cpu_baseline(tokens: int, reps: int, seed: int = 0):
 
 # ------------------------------------------------------------- our arm -----
 
+def headline_config(world):
+    """The `config` dict of the headline workload (both arms print it)."""
+    return {**WORKLOAD, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)",
+            "l2": "inputs > L2 (~290 MB resident per GPU), no flush"}
+
+
+def exchange_check(peer, layer, flat_grads, dev, world):
+    """Outside the timed region: the peer kernel's average of the LoRA
+    gradients against an NCCL all-reduce of the same buffer, whether every
+    rank holds the same averaged gradient bits, and whether one AdamW step
+    from them leaves A and B bitwise identical on every rank."""
+    import torch
+    import torch.distributed as dist
+
+    from metallora_b200 import kernels as K
+    from metallora_b200.distributed import replicas_in_sync
+    torch.cuda.synchronize()
+    if peer is not None:
+        src = peer.buffer.clone()   # this step's dA/dB as written by the backward
+        got = flat_grads.clone()    # the peer kernel's average of them
+    else:
+        src = flat_grads.clone()
+        got = None
+    ref = src.clone()
+    dist.all_reduce(ref, op=dist.ReduceOp.SUM)
+    ref.mul_(1.0 / world)
+    out = {"exchange": "peer" if peer is not None else "nccl",
+           "numel": int(src.numel())}
+    if got is not None:
+        diff = (got - ref).abs()
+        scale = ref.abs().max().clamp_min(1e-30)
+        out["bitwise_equal_nccl"] = bool(torch.equal(got, ref))
+        out["max_rel_vs_nccl"] = float(diff.max() / scale)
+        # fp32 sums of `world` terms in another order: a few ulps of the largest
+        bound = 4 * world * 2.0 ** -24
+        out["rel_bound"] = bound
+        ok = out["max_rel_vs_nccl"] <= bound
+    else:
+        got = ref
+        ok = True
+    out["grads_in_sync"] = replicas_in_sync(got)
+    # one AdamW step of A and B from the averaged gradient, then the replicas
+    n_a = layer.A.numel()
+    ab = torch.cat([layer.A.detach().reshape(-1).float(), layer.B.detach().reshape(-1).float()])
+    g = got.clone()
+    m, v = torch.zeros_like(ab), torch.zeros_like(ab)
+    st = K.persistent_gpu_state_init(device=dev)
+    K.persistent_gpu_state_step(st)
+    K.lora_adamw_step_metal(ab, g, m, v, st, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+    out["params_in_sync_after_adamw"] = (replicas_in_sync(ab[:n_a]) and
+                                         replicas_in_sync(ab[n_a:]))
+    out["ok"] = bool(ok and out["grads_in_sync"] and out["params_in_sync_after_adamw"])
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -234,13 +328,15 @@ def run_ours(args, rank, world, local_rank):
     layer = LoRALinear(K, N, rank=r, alpha=alpha, device=dev, dtype=torch.bfloat16)
     with torch.no_grad():
         layer.W0.copy_(torch.randn(N, K, device=dev, generator=g) / 64)
-        layer.A.copy_((torch.rand(r, K, device=dev, generator=g) * 2 - 1) / 64)
-        layer.B.copy_(torch.randn(N, r, device=dev, generator=g) * 0.02 ** 0.5)
+        # A and B are replicated parameters: the same on every rank
+        ga = torch.Generator(device=dev).manual_seed(4321)
+        layer.A.copy_((torch.rand(r, K, device=dev, generator=ga) * 2 - 1) / 64)
+        layer.B.copy_(torch.randn(N, r, device=dev, generator=ga) * 0.02 ** 0.5)
     x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
     dy = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
     flat_grads = None
-    # N > 1: the LoRA gradients accumulate straight into a symmetric buffer and
-    # are averaged by one kernel over NVLink peer memory (NCCL where that is
+    # N > 1: the LoRA gradients go straight into a symmetric buffer and are
+    # averaged by one kernel over NVLink peer memory (NCCL where that is
     # unavailable)
     from metallora_b200.distributed import PeerAllReduce
     n_a, n_b = layer.A.numel(), layer.B.numel()
@@ -271,7 +367,7 @@ def run_ours(args, rank, world, local_rank):
             flat_grads = flat
         return y
 
-    # the clock sampler starts first, so the warm-up also brings the clocks up
+    # one clock sampler for the whole run; each measurement reads its window
     sampler = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else
                            int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
     sampler.start()
@@ -315,22 +411,25 @@ def run_ours(args, rank, world, local_rank):
     # step); the same K steps then run again with them for the kernel breakdown
     ms, launches, _, t_wall0, t_wall1 = timed(False)
     ms_prof, _, prof, _, t_wall2 = timed(True)
-    sampler.stop()
     ms_per_step = ms / args.steps
     value = world * M * args.steps / (ms / 1e3)
+    clocks = sampler.summary(t_wall0, t_wall2)
 
     # roofline: the dominant kernel is the tcgen05 GEMM (forward y and backward dx)
     peaks = load_peaks()
     gemm_ms, gemm_n = prof["gemm"]
     gemm_flops = 2.0 * M * N * (K + r)  # per launch: X.W^T (+ rank block); fwd and dx alike
     achieved = gemm_flops / (gemm_ms / gemm_n / 1e3) / 1e12 if gemm_n else None
-    peak = peaks["bf16_tflops_sustained"]
+    peak, peak_name, peak_why = pick_peak(peaks, clocks)
+    traffic, traffic_src = profile_traffic(GEMM_PROFILE)
     breakdown = {k: {"ms_per_launch": round(v[0] / v[1], 4), "launches": v[1]}
                  for k, v in prof.items() if v[1]}
+    nongemm = ms_prof / args.steps - gemm_ms / args.steps
+
+    grad_check = exchange_check(peer, layer, flat_grads, dev, world) if world > 1 else None
 
     # end-to-end through the public API with host buffers (pinned), overlapped
-    layer._grad_sink = None  # the end-to-end path returns dA/dB to the host through autograd
-    e2e = run_e2e(args, layer, M, K, N, dev, world)
+    e2e = run_e2e(args, layer, M, K, N, dev, world, peer)
 
     total_tflops = world * flops_per_token(K, N, r) * M * args.steps / (ms / 1e3) / 1e12
     line = {
@@ -339,29 +438,39 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations/grads, N(0,1/4096) base, U(+-1/64) A, "
                 "N(0,0.02) B)",
-        "config": {**WORKLOAD, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)",
-                   "grad_exchange": exchange_kind,
-                   "l2": "inputs > L2 (~290 MB resident per GPU), no flush"},
+        "config": headline_config(world),
+        "grad_exchange": exchange_kind,
+        "host_cores_per_rank": host_cores,
         "tflops": round(total_tflops, 1),
+        "step_frac_of_peak": round(total_tflops / world / peak, 4),
         "roofline": {"bound": "tensor", "kernel": "lora_gemm_pair_kernel (tcgen05 cta_group::2)",
                      "achieved": round(achieved, 1) if achieved else None,
                      "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4) if achieved else None,
-                     "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                     "peak_source": peak_name, "peak_why": peak_why,
                      "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4) if achieved else None,
-                     "traffic": GEMM_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
-                                       "forward launch of this workload",
+                     "frac_of_sustained": (round(achieved / peaks["bf16_tflops_sustained"], 4)
+                                           if achieved else None),
+                     "traffic": traffic, "traffic_unit": "bytes per launch",
+                     "traffic_source": traffic_src,
                      "algorithmic_bytes": GEMM_ALGORITHMIC_BYTES,
                      "per_launch_gflop": round(gemm_flops / 1e9, 2),
                      "kernel_timing": f"per-launch events over a second pass of the {args.steps} "
                                       f"steps ({ms_prof / args.steps:.4f} ms/step with events)"},
         "kernels": breakdown,
+        "non_gemm_ms_per_step": round(nongemm, 4),
         "gpu_launches": launches,
-        "clocks": sampler.summary(t_wall0, t_wall2),
+        "clocks": clocks,
         "e2e": e2e,
     }
-    line["config"]["host_cores_per_rank"] = host_cores
+    if grad_check is not None:
+        line["grad_exchange_check"] = grad_check
+    # free the headline tensors before the other configurations
+    del x, dy, layer, flat_grads
+    torch.cuda.empty_cache()
+    if args.workloads == "all":
+        line["workloads"] = run_workloads(args, rank, world, local_rank, sampler)
+    sampler.stop()
     if rank == 0:
         if world == 1:  # the host baseline is taken at N=1 only, on every host core
             if affinity_before:
@@ -370,11 +479,13 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, layer, M, K, N, dev, world):
+def run_e2e(args, layer, M, K, N, dev, world, peer=None):
     """Same step through the public API with host-resident inputs and results:
-    per step, H2D of x and dy from pinned memory and D2H of y, dx, dA, dB.  The
-    two directions run on their own streams (PCIe is full duplex), the next
-    step's inputs load while this step computes."""
+    per step, H2D of x and dy from pinned memory and D2H of y, dx and the LoRA
+    gradients (dA, dB; at N > 1 their average over the ranks, by the same peer
+    exchange as the device-resident leg).  The two directions run on their own
+    streams (PCIe is full duplex), the next step's inputs load while this step
+    computes."""
     import torch
     import torch.distributed as dist
 
@@ -382,19 +493,27 @@ def run_e2e(args, layer, M, K, N, dev, world):
     g = torch.Generator().manual_seed(99)
     xh = [torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory() for _ in range(2)]
     dyh = [torch.randn(M, N, generator=g).to(torch.bfloat16).pin_memory() for _ in range(2)]
+    n_a, n_b = layer.A.numel(), layer.B.numel()
+    if world > 1:
+        grad_shapes = (("grads", (n_a + n_b,), torch.float32),)
+    else:
+        grad_shapes = (("dA", tuple(layer.A.shape), layer.A.dtype),
+                       ("dB", tuple(layer.B.shape), layer.B.dtype))
     outs = {k: [torch.empty(s, dtype=dt).pin_memory() for _ in range(2)]
             for k, s, dt in (("y", (M, N), torch.bfloat16), ("dx", (M, K), torch.bfloat16),
-                             ("dA", tuple(layer.A.shape), layer.A.dtype),
-                             ("dB", tuple(layer.B.shape), layer.B.dtype))}
+                             *grad_shapes)}
     xd = [torch.empty(M, K, device=dev, dtype=torch.bfloat16) for _ in range(2)]
     dyd = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    avg = [torch.empty(n_a + n_b, dtype=torch.float32, device=dev) for _ in range(2)]
     comp = torch.cuda.current_stream()
     copy = torch.cuda.Stream(device=dev)   # host -> device
     drain = torch.cuda.Stream(device=dev)  # device -> host
     h2d = 2 * M * K + 2 * M * N
-    d2h = 2 * M * N + 2 * M * K + layer.A.element_size() * (layer.A.numel() + layer.B.numel())
+    d2h = 2 * M * N + 2 * M * K + sum(
+        int(np.prod(s)) * torch.empty(0, dtype=dt).element_size() for _, s, dt in grad_shapes)
     loaded = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
+    drained = [torch.cuda.Event() for _ in range(2)]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     def load(i):
@@ -419,20 +538,29 @@ def run_e2e(args, layer, M, K, N, dev, world):
         layer.B.grad = None
         y = layer(xin)
         y.backward(dyd[b])
-        ga, gb = layer.A.grad, layer.B.grad
         if world > 1:
-            flat = torch.cat([ga.reshape(-1), gb.reshape(-1)]).float()
-            dist.all_reduce(flat)
+            if i >= 2:  # avg[b] was drained to the host by step i - 2's copy
+                comp.wait_event(drained[b])
+            if peer is not None:
+                peer.allreduce(avg[b])
+            else:
+                flat = torch.cat([layer.A.grad.reshape(-1), layer.B.grad.reshape(-1)]).float()
+                dist.all_reduce(flat)
+                avg[b].copy_(flat.mul_(1.0 / world))
+            grads = ((outs["grads"][b], avg[b]),)
+        else:
+            grads = ((outs["dA"][b], layer.A.grad), (outs["dB"][b], layer.B.grad))
         done[b].record(comp)
         dx = xin.grad
         with torch.cuda.stream(drain):
             drain.wait_event(done[b])
-            for t in (y, dx, ga, gb):
+            for t in (y, dx, *(src for _, src in grads)):
                 t.record_stream(drain)
             outs["y"][b].copy_(y.detach(), non_blocking=True)
             outs["dx"][b].copy_(dx, non_blocking=True)
-            outs["dA"][b].copy_(ga, non_blocking=True)
-            outs["dB"][b].copy_(gb, non_blocking=True)
+            for dst, src in grads:
+                dst.copy_(src, non_blocking=True)
+            drained[b].record(drain)
         xin.grad = None
         xd[b].requires_grad_(False)
     comp.wait_stream(copy)
@@ -448,7 +576,10 @@ def run_e2e(args, layer, M, K, N, dev, world):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "ms_per_step": round(ms / steps, 4),
             "path": "LoRALinear forward+backward, pinned host buffers, H2D and D2H on their "
-                    "own streams overlapped with compute"}
+                    "own streams overlapped with compute" +
+                    (("; LoRA gradients averaged by the " +
+                      ("NVLink peer exchange" if peer is not None else "NCCL all-reduce"))
+                     if world > 1 else "")}
 
 
 # ------------------------------------------------------------ stack (cfg4) --
@@ -511,7 +642,13 @@ def build_stack(dev, seed=0):
     return Stack()
 
 
-def run_stack(args, rank, world, local_rank):
+def stack_measure(args, rank, world, local_rank, steps, warmup, sampler=None, overlap=True):
+    """One configuration of the 32-layer NF4 stack: ``warmup`` untimed and
+    ``steps`` timed LoRATrainer steps (forward, backward, gradient average
+    over the ranks, global-norm clip, AdamW) on this rank's token shard; time
+    is the max over ranks.  ``overlap``: per-layer gradient buckets averaged on
+    a side stream while the backward of earlier layers runs; otherwise one
+    all-reduce of the flat buffer after the backward."""
     import torch
     import torch.distributed as dist
 
@@ -525,18 +662,20 @@ def run_stack(args, rank, world, local_rank):
     cfg = TrainingConfig(rank=STACK["rank"], alpha=STACK["alpha"], learning_rate=1e-4,
                          output_dir="/tmp/mlora_bench_out", log_interval=10 ** 9,
                          save_interval=10 ** 9)
-    tr = LoRATrainer(model, cfg)
+    tr = LoRATrainer(model, cfg, overlap_grad_exchange=overlap)
     b, e = shard_bounds(STACK["tokens"], rank, world)
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     x = torch.randn(1, e - b, STACK["hidden"], device=dev, generator=g).to(torch.bfloat16)
     tgt = torch.randn(1, e - b, STACK["hidden"], device=dev, generator=g).to(torch.bfloat16)
     batch = {"input_ids": x, "target_output": tgt}
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         tr._training_step(batch)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
+    own_sampler = sampler is None
+    if own_sampler:
+        sampler = ClockSampler(local_rank)
+        sampler.start()
+        time.sleep(0.3)
     _lib.profile_read(reset=True)
     _lib.profile_enable(True)
     launches0 = _lib.launch_count()
@@ -547,7 +686,7 @@ def run_stack(args, rank, world, local_rank):
     t0 = time.time()
     ev0.record()
     losses = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         losses.append(tr._training_step(batch)["loss"])
     ev1.record()
     torch.cuda.synchronize()
@@ -557,35 +696,57 @@ def run_stack(args, rank, world, local_rank):
     launches = _lib.launch_count() - launches0
     _lib.profile_enable(False)
     prof = _lib.profile_read(reset=True)
-    sampler.stop()
+    if own_sampler:
+        sampler.stop()
+    clocks = sampler.summary(t0, t1)
     ms = ev0.elapsed_time(ev1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    tokens = STACK["tokens"] * args.steps
+    in_sync = None
+    if world > 1:
+        from metallora_b200.distributed import replicas_in_sync
+        in_sync = replicas_in_sync(tr.params.master)
+    tokens = STACK["tokens"] * steps
     value = tokens / (ms / 1e3)
     tflops = stack_flops_per_token() * value / 1e12
     peaks = load_peaks()
-    g_ms, g_n = prof["gemm"]
-    line = {
+    peak, peak_name, peak_why = pick_peak(peaks, clocks)
+    g_ms = prof["gemm"][0]
+    kern_total = sum(v[0] for v in prof.values())
+    out = {
         "metric": "LoRA projection-stack training step tokens/s (NF4 bases, bf16)",
-        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {**STACK, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)"},
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms / steps, 3), "higher_is_better": True,
+        "scaling": "strong", "dtype": "bf16", "data": "synthetic",
+        "config": {**STACK, "parallelism": f"dp{world} (token shards, LoRA-grad all-reduce)",
+                   "grad_exchange": ("per-layer buckets on a side stream, overlapped with the "
+                                     "backward" if overlap else "one flat all-reduce after the "
+                                     "backward") if world > 1 else "none"},
         "tflops": round(tflops, 1),
-        "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1),
-                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                     "frac": round(tflops / world / peaks["bf16_tflops_sustained"], 4),
-                     "per": "GPU, whole step", "peak_source":
-                         f"{peaks['source']} bf16_tflops_sustained"},
-        "kernels": {k: {"ms_total": round(v[0], 2), "launches": v[1]} for k, v in prof.items() if v[1]},
-        "gemm_share": round(g_ms / max(1e-9, sum(v[0] for v in prof.values())), 3),
+        "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4),
+                     "per": "GPU, whole step", "peak_source": peak_name, "peak_why": peak_why},
+        "kernels_ms_per_step": {k: round(v[0] / steps, 2) for k, v in prof.items() if v[1]},
+        "kernel_launches_per_step": {k: v[1] // steps for k, v in prof.items() if v[1]},
+        "gemm_share_of_kernel_time": round(g_ms / max(1e-9, kern_total), 3),
+        "kernel_ms_per_step": round(kern_total / steps, 2),
         "gpu_launches": launches, "loss_first_last": [losses[0], losses[-1]],
-        "clocks": sampler.summary(t0, t1),
+        "clocks": clocks,
         "mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1),
     }
+    if in_sync is not None:
+        out["replicas_in_sync"] = in_sync
+    del tr, model, x, tgt, batch
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_stack(args, rank, world, local_rank):
+    line = stack_measure(args, rank, world, local_rank, args.steps, args.warmup,
+                         overlap=not args.no_overlap)
+    line["vs_baseline"] = None
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -641,7 +802,14 @@ def events_ms(fn, reps=20, warm=3):
     return e0.elapsed_time(e1) / reps
 
 
-def run_sweep(args):
+def sweep(kind, sampler=None, quick=False):
+    """Measurements of one of the other configurations on cuda:0, one dict per
+    case.  kind: "fp32" (fp32 forward 4096->4096 r16, 2048 tokens, and the
+    merged weight), "nf4" (NF4 11008x4096 block 64, r64, forward and backward
+    at 1/16/512/4096 tokens), "int" (INT4/INT8 group 128, 4096->4096 and
+    4096->14336, r16, forward unmerged and merged), "multi" (per-sample
+    adapters).  ``quick`` keeps the cases the default bench line reports
+    (tokens 1 and 4096 for INT, no lean-path comparison)."""
     import torch
 
     from metallora_b200 import kernels as K
@@ -650,15 +818,29 @@ def run_sweep(args):
     torch.cuda.set_device(dev)
     peaks = load_peaks()
     gen = torch.Generator(device=dev).manual_seed(0)
+    out = []
+
+    def window(t0):
+        return sampler.summary(t0, time.time()) if sampler is not None else {}
+
+    def tensor_roofline(flops, ms, clocks):
+        peak, name, _ = pick_peak(peaks, clocks)
+        ach = flops / ms / 1e9
+        return {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4), "peak_source": name}
+
+    def hbm_roofline(nbytes, ms):
+        ach = nbytes / ms / 1e6
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4),
+                "peak_source": f"{peaks['source']} hbm_gbs", "weights": "HBM-cold (rotated copies)"}
 
     def lora_bytes(qw, W, A, B, M, Kd, N):
         wb = qw.nbytes() if qw is not None else W.numel() * 2
         return wb + (A.numel() + B.numel()) * 2 + 2 * M * (Kd + N)
 
-    def emit(d):
-        print(json.dumps(d), flush=True)
-
-    if args.workload == "fp32":
+    if kind == "fp32":
+        t0 = time.time()
         M, Kd, N, r = 2048, 4096, 4096, 16
         x = torch.randn(M, Kd, device=dev, generator=gen)
         W = torch.randn(N, Kd, device=dev, generator=gen) / 64
@@ -668,14 +850,22 @@ def run_sweep(args):
         Wm = K.merge(W, A, B, 32.0)
         tm = graph_ms(lambda: K.linear(x, Wm))
         y, _ = K.lora_linear_fwd(x, W, A, B, 32.0)
+        ym = K.linear(x, Wm)
         ref = x.double() @ W.double().t() + 2.0 * (x.double() @ A.double().t()) @ B.double().t()
         rel = float((y.double() - ref).norm() / ref.norm())
+        relm = float((ym.double() - ref).norm() / ref.norm())
         fl = 2.0 * M * (Kd * N + Kd * r + r * N)
-        emit({"workload": "fp32_fwd_4096x4096_r16_2048tok", "ms": round(t, 4),
-              "tflops": round(fl / t / 1e9, 1), "merged_ms": round(tm, 4),
-              "rel_err_vs_fp64": rel, "tokens_per_s": round(M / t * 1e3, 1)})
-        return
-    if args.workload == "multi":
+        clocks = window(t0)
+        out.append({"workload": "fp32_fwd_4096x4096_r16_2048tok", "tokens": M, "ms": round(t, 4),
+                    "tflops": round(fl / t / 1e9, 1), "merged_ms": round(tm, 4),
+                    "rel_err_vs_fp64": rel, "merged_rel_err_vs_fp64": relm, "tolerance": 1e-4,
+                    "tokens_per_s": round(M / t * 1e3, 1),
+                    "roofline": {**tensor_roofline(fl, t, clocks),
+                                 "note": "fp32 as 3 bf16 products (hi.hi, hi.lo, lo.hi): "
+                                         "algorithmic fp32 FLOPs over the bf16 peak"},
+                    "clocks": clocks})
+        return out
+    if kind == "multi":
         # per-sample adapters (16 samples x 512 tokens, 4096 -> 4096, r 16)
         from metallora_b200.ops import multi_adapter_forward
         Kd, N, r, S, Bsz = 4096, 4096, 16, 512, 16
@@ -688,18 +878,21 @@ def run_sweep(args):
             # host-side grouping of the ids: timed with events, not a graph
             t = events_ms(lambda: multi_adapter_forward(x, W, A, Bm, ids, 32.0))
             fl = 2.0 * Bsz * S * (Kd * N + Kd * r + r * N)
-            emit({"workload": "multi_adapter_fwd_4096x4096_r16", "tokens": Bsz * S,
-                  "adapters": n, "distinct_in_batch": min(n, Bsz), "ms": round(t, 4),
-                  "tflops": round(fl / t / 1e9, 1)})
+            out.append({"workload": "multi_adapter_fwd_4096x4096_r16", "tokens": Bsz * S,
+                        "adapters": n, "distinct_in_batch": min(n, Bsz), "ms": round(t, 4),
+                        "tflops": round(fl / t / 1e9, 1)})
         t1 = events_ms(lambda: K.lora_linear_fwd(x.reshape(-1, Kd), W, A[0], Bm[0], 32.0))
-        emit({"workload": "single_adapter_fwd_4096x4096_r16", "tokens": Bsz * S, "ms": round(t1, 4)})
-        return
-    if args.workload == "nf4":
+        out.append({"workload": "single_adapter_fwd_4096x4096_r16", "tokens": Bsz * S,
+                    "ms": round(t1, 4)})
+        return out
+    if kind == "nf4":
         cases = [("nf4", 64, 4096, 11008, 64, 128.0, M) for M in (1, 16, 512, 4096)]
     else:
+        toks = (1, 4096) if quick else (1, 16, 128, 512, 4096)
         cases = [(s, 128, 4096, N, 16, 32.0, M) for s in ("int4", "int8") for N in (4096, 14336)
-                 for M in (1, 16, 128, 512, 4096)]
+                 for M in toks]
     for scheme, group, Kd, N, r, alpha, M in cases:
+        t0 = time.time()
         W = (torch.randn(N, Kd, device=dev, generator=gen) / Kd ** 0.5).to(torch.bfloat16)
         qw = quant.quantize(W, scheme, group)
         A = ((torch.rand(r, Kd, device=dev, generator=gen) * 2 - 1) / Kd ** 0.5).to(torch.bfloat16)
@@ -717,73 +910,115 @@ def run_sweep(args):
             tf = graph_ms([lambda c=c: K.qlora_linear_fwd(x, c, A, B, alpha) for c in copies],
                           reps=10, inner=2)
             d["weight_copies"] = len(copies)
+            del copies
         else:
             tf = graph_ms(lambda: K.qlora_linear_fwd(x, qw, A, B, alpha))
         d.update({"fwd_ms": round(tf, 4), "fwd_tflops": round(fl / tf / 1e9, 1),
-                  "fwd_gbs": round(byts / tf / 1e6, 1)})
-        if M > 16:  # the fused in-loop-dequant kernel (lean workspace), for comparison
+                  "fwd_gbs": round(byts / tf / 1e6, 1), "algorithmic_bytes": byts})
+        if M > 16 and not quick:  # the fused in-loop-dequant kernel (lean workspace)
             import dataclasses
             ql = dataclasses.replace(qw, lean=True)
             d["lean_fwd_ms"] = round(graph_ms(lambda: K.qlora_linear_fwd(x, ql, A, B, alpha)), 4)
-        if M <= 16:
-            d["fwd_roofline"] = {"bound": "hbm", "frac": round(byts / tf / 1e6 / peaks["hbm_gbs"], 4)}
-        else:
-            d["fwd_roofline"] = {"bound": "tensor",
-                                 "frac": round(fl / tf / 1e9 / peaks["bf16_tflops"], 4)}
-        if args.workload == "nf4":
+        if kind == "nf4":
             _, saved = K.qlora_linear_fwd(x, qw, A, B, alpha, save_xa=True)
             tb = graph_ms(lambda: K.qlora_linear_bwd(dy, x, qw, A, B, alpha, saved))
             flb = 2.0 * M * (N * Kd + 2 * N * r + 2 * r * Kd)
-            d.update({"bwd_ms": round(tb, 4), "bwd_tflops": round(flb / tb / 1e9, 1)})
+            d.update({"bwd_ms": round(tb, 4), "bwd_tflops": round(flb / tb / 1e9, 1),
+                      "fwd_bwd_tflops": round((fl + flb) / (tf + tb) / 1e9, 1)})
         else:
             Wm = K.merge(quant.dequantize(qw, torch.bfloat16), A, B, alpha)
             if M <= 16:
                 wms = [Wm] + [Wm.clone() for _ in range(int(1.5 * L2_BYTES // (Wm.numel() * 2)))]
                 tm = graph_ms([lambda w=w: K.linear(x, w) for w in wms], reps=10, inner=2)
+                del wms
             else:
                 tm = graph_ms(lambda: K.linear(x, Wm))
             d.update({"merged_fwd_ms": round(tm, 4),
                       "merged_gbs": round((Wm.numel() * 2 + 2 * M * (Kd + N)) / tm / 1e6, 1)})
-        emit(d)
+        clocks = window(t0)
+        if M <= 16:
+            d["fwd_roofline"] = hbm_roofline(byts, tf)
+        else:
+            d["fwd_roofline"] = tensor_roofline(fl, tf, clocks)
+        if "bwd_ms" in d and M > 16:
+            d["fwd_bwd_roofline"] = tensor_roofline(fl + flb, tf + tb, clocks)
+        d["clocks"] = clocks
+        out.append(d)
+        del W, qw, A, B, x, dy
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_workloads(args, rank, world, local_rank, sampler):
+    """The other configurations, measured after the headline: at N = 1 the
+    fp32 forward (cfg0), NF4 (cfg2) and INT4/INT8 (cfg3) cases on cuda:0; at
+    every N the 32-layer NF4 stack training step (cfg4, all ranks)."""
+    out = {}
+
+    def guarded(name, fn):
+        try:
+            out[name] = fn()
+        except Exception as e:  # recorded in the line, not hidden
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+
+    if world == 1:
+        guarded("cfg0_fp32", lambda: sweep("fp32", sampler)[0])
+        guarded("cfg2_nf4", lambda: sweep("nf4", sampler, quick=True))
+        guarded("cfg3_int", lambda: sweep("int", sampler, quick=True))
+    guarded("cfg4_stack", lambda: stack_measure(args, rank, world, local_rank, steps=3, warmup=2,
+                                                sampler=sampler))
+    return out
+
+
+def run_sweep(args):
+    for d in sweep(args.workload):
+        print(json.dumps(d), flush=True)
 
 
 # -------------------------------------------------------- reference arm ----
 
 def run_reference(args, rank):
-    """The reference's CPU path on the host cores: inputs for a sample of the
-    workload are built once, then W untimed and K timed steps of the numpy
-    restatement (forward, dx, dA, dB), every step on the same resident inputs
-    (as our arm's `value` leg keeps its inputs in HBM)."""
+    """The reference's CPU path on the host cores, on the headline workload
+    itself (8192 tokens per step unless --ref-tokens says otherwise): inputs
+    built once, then W untimed and K timed steps of the numpy restatement
+    (forward, dx, dA, dB), every step on the same resident inputs (as our
+    arm's `value` leg keeps its inputs in HBM).  Each step is timed on its
+    own; `value` uses the median step."""
     if rank != 0:
         return
     from threadpoolctl import threadpool_limits
     tokens = args.ref_tokens
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     inp = _cpu_inputs(tokens)
+    times = []
     with threadpool_limits(limits=len(os.sched_getaffinity(0)), user_api="blas"):
         for _ in range(args.warmup):
             _cpu_step(inp)
-        t = time.perf_counter()
         for _ in range(args.steps):
+            t = time.perf_counter()
             _cpu_step(inp)
-        elapsed = time.perf_counter() - t
+            times.append(time.perf_counter() - t)
         cores = _blas_threads()
-    value = tokens * args.steps / elapsed
-    res = {"cores": cores,
-           "sample": f"{tokens} tokens per step, {args.steps} steps of fwd+dx+dA+dB (numpy fp32 "
-                     f"on bf16-rounded inputs built once, OpenBLAS, {_cpu_model()})"}
+    med = statistics.median(times)
+    value = tokens / med
+    sample = (f"{tokens} tokens per step (the full per-GPU batch), median of {args.steps} timed "
+              f"steps after {args.warmup} warm-up, fwd+dx+dA+dB (numpy fp32 on bf16-rounded "
+              f"inputs built once, OpenBLAS, {_cpu_model()}, {cores} threads)")
     K, N, r = WORKLOAD["in_features"], WORKLOAD["out_features"], WORKLOAD["rank"]
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * elapsed / args.steps, 3), "higher_is_better": True,
+        "ms_per_step": round(1e3 * med, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (same distributions as our arm)",
-        "config": {**WORKLOAD, "parallelism": "host CPU, rank 0 only",
-                   "sample_tokens_per_step": tokens},
+        "config": headline_config(world),
         "impl": "reference",
+        "runs_on": "host CPU, rank 0 only",
+        "step_seconds": {"median": round(med, 4), "min": round(min(times), 4),
+                         "max": round(max(times), 4)},
         "tflops": round(flops_per_token(K, N, r) * value / 1e12, 4),
-        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": res["cores"],
-                         "kind": "port", "sample": res["sample"]},
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores,
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "MLX (the reference's CPU backend) cannot be installed here; its pure-MLX op "
@@ -802,7 +1037,12 @@ def main():
                     default="lora")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--cpu-reps", type=int, default=3)
-    ap.add_argument("--ref-tokens", type=int, default=2048)
+    ap.add_argument("--ref-tokens", type=int, default=WORKLOAD["tokens_per_gpu"])
+    ap.add_argument("--workloads", choices=["all", "none"], default="all",
+                    help="after the headline, also measure the other configurations "
+                         "(fp32, NF4, INT4/INT8 at N=1; the NF4 stack at every N)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="--workload stack: one flat all-reduce after the backward")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -323,10 +323,14 @@ MLORA_API int mlora_lora_kv_cache_update(const void* x, const void* wk, const vo
  * same bits on every rank), in one kernel over NVLink peer memory.  bufs and
  * flags are DEVICE arrays of `world` pointers: each rank's buffer and its
  * `world`-word flag array, both in memory every rank can address (e.g.
- * symmetric memory); flags start at 0; seq counts calls from 1; counter is one
- * zeroed device word owned by the caller.  Every rank calls it once per step
- * on its own GPU; when it completes no peer reads this rank's buffer any more.
- * A peer that does not arrive within 2 s sets status 0x108 (no hang).
+ * symmetric memory); flags start at 0; seq counts calls from 1; counter is an
+ * array of 4 device words on this GPU, owned by the caller and zeroed before
+ * the first call.  `out` must not alias this rank's buffer (peers read the
+ * buffer while `out` is written).  Every rank calls it once per step on its
+ * own GPU; when it completes no peer reads this rank's buffer any more.  A
+ * peer that does not arrive within 2 s sets status 0x108 (no hang); the
+ * go/abort decision is taken once for the whole grid, so on a timeout `out`
+ * is left untouched (never partly written).
  * Replaces the NCCL all-reduce of the LoRA gradients for small buffers (the
  * reference has no multi-device path: python/metal_lora/trainer.py:228-249 is
  * single-device). */
@@ -407,8 +411,11 @@ MLORA_API int mlora_grad_norm_clip(const float* grad, int64_t n, float max_norm,
  *   - Shapes whose scratch exceeds the array (see
  *     mlora_lora_grads_static_scratch_bytes) return MLORA_ERR_WORKSPACE.
  *   - The first call on a device looks up the array's device address (once
- *     per device, with that device current); make that first call before any
- *     stream capture.
+ *     per device context, with that device current); make that first call
+ *     before any stream capture.  A failed lookup is not remembered (the next
+ *     call tries again), and a context that is torn down and re-created
+ *     (cudaDeviceReset) gets a fresh lookup on its first call.
+ *   - A device index of 64 or more returns MLORA_ERR_UNSUPPORTED.
  *   - All calls on a device share the array: calls whose work overlaps on the
  *     GPU (different streams, no ordering between them) race and corrupt each
  *     other's results.  Each call clears the parts that must start at zero.

@@ -24,21 +24,70 @@ constexpr size_t kStaticScratchBytes = size_t(32) << 20;  // 32 MiB per device
 static __device__ __align__(256) unsigned char g_lora_grad_scratch[kStaticScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_setup_once[kMaxDevices];
-void* g_scratch_ptr[kMaxDevices] = {};
-cudaError_t g_setup_err[kMaxDevices] = {};
 
-// Device address of the scratch array for the current device (host code only
-// sees a host-side stand-in for the symbol; the real address comes from the
-// runtime, once per device, with that device current).
-void* scratch_address(int device, cudaError_t* err) {
-  std::call_once(g_setup_once[device], [device]() {
+// Per-device cache of the array's device address, valid for the context it
+// was looked up in.  Host code only sees a host-side stand-in for the symbol;
+// the real address comes from the runtime with the device current.  The cache
+// is keyed on the driver's unique context id, so a context torn down and
+// re-created (cudaDeviceReset) gets a fresh lookup instead of a stale address,
+// and only successful lookups are kept: a failed one is retried on the next
+// call.
+struct ScratchSlot {
+  std::mutex mu;
+  unsigned long long ctx_id = 0;
+  bool valid = false;
+  void* ptr = nullptr;
+};
+ScratchSlot g_slot[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (0 when it cannot be read;
+// the address is then looked up again on every call).
+unsigned long long current_context_id() {
+  static std::once_flag once;
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  std::call_once(once, []() {
     void* p = nullptr;
-    g_setup_err[device] = cudaGetSymbolAddress(&p, g_lora_grad_scratch);
-    g_scratch_ptr[device] = (g_setup_err[device] == cudaSuccess) ? p : nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
   });
-  *err = g_setup_err[device];
-  return g_scratch_ptr[device];
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of the scratch array on `device` (which is current).
+void* scratch_address(int device, cudaError_t* err) {
+  ScratchSlot& slot = g_slot[device];
+  std::lock_guard<std::mutex> lock(slot.mu);
+  const unsigned long long id = current_context_id();
+  if (slot.valid && id != 0 && slot.ctx_id == id) {
+    *err = cudaSuccess;
+    return slot.ptr;
+  }
+  void* p = nullptr;
+  *err = cudaGetSymbolAddress(&p, g_lora_grad_scratch);
+  if (*err != cudaSuccess || p == nullptr) {
+    cudaGetLastError();  // not sticky: the next call tries again
+    slot.valid = false;
+    return nullptr;
+  }
+  slot.ptr = p;
+  slot.ctx_id = id;
+  slot.valid = id != 0;
+  return p;
 }
 
 }  // namespace
@@ -47,9 +96,9 @@ extern "C" {
 
 size_t mlora_lora_grads_static_scratch_bytes(void) { return kStaticScratchBytes; }
 
-int mlora_lora_grads_static(const void* dy, const void* x, const void* a, const void* b, float* da,
-                            float* db, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
-                            float clip_value, int dtype, void* stream) {
+int mlora_lora_grads_static(const void* dy, const void* x, const void* a, const void* b,
+                            float* da, float* db, int64_t M, int64_t K, int64_t N, int64_t r,
+                            float alpha, float clip_value, int dtype, void* stream) {
   if (dtype != MLORA_DTYPE_BF16 && dtype != MLORA_DTYPE_F16) {
     mlora::set_error("mlora_lora_grads_static takes BF16 or F16 inputs");
     return MLORA_ERR_UNSUPPORTED;
@@ -68,12 +117,18 @@ int mlora_lora_grads_static(const void* dy, const void* x, const void* a, const 
   }
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess || device < 0 || device >= kMaxDevices) {
+  if (e != cudaSuccess) {
     mlora::set_error(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
   }
+  if (device < 0 || device >= kMaxDevices) {
+    mlora::set_error("mlora_lora_grads_static: device index " + std::to_string(device) +
+                     " exceeds the " + std::to_string(kMaxDevices) +
+                     "-device limit of the built-in scratch");
+    return MLORA_ERR_UNSUPPORTED;
+  }
   void* scratch = scratch_address(device, &e);
-  if (e != cudaSuccess || scratch == nullptr) {
+  if (scratch == nullptr) {
     mlora::set_error(std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
   }

@@ -4,9 +4,13 @@
 // pointers from the caller).  One kernel per rank and step:
 //   1. publish: make this rank's buffer visible system-wide, then raise its
 //      flag in every peer's flag array to 2*seq-1;
-//   2. every CTA waits (bounded) until all peers' flags in its own array reach
-//      2*seq-1, then sums the peers' buffers in rank order -- the same
-//      operations on every rank, so the results are bitwise identical;
+//   2. block 0 alone waits (bounded) until all peers' flags in its own array
+//      reach 2*seq-1 and records one go/abort verdict for the whole grid in
+//      this GPU's counter words; the other CTAs wait for that verdict on a
+//      local word (with back-off, so they do not load NVLink or L2 while a
+//      kernel beside them computes).  With "go" every CTA sums the peers'
+//      buffers in rank order -- the same operations on every rank, so the
+//      results are bitwise identical; with "abort" no CTA writes `out`;
 //   3. the last CTA to finish raises its flag in every peer to 2*seq and waits
 //      for all peers to reach it: when the kernel has completed, no peer reads
 //      this rank's buffer any more, so the caller may overwrite it.
@@ -47,6 +51,19 @@ __device__ bool wait_flags(const uint32_t* mine, int world, uint32_t target, uin
   return true;
 }
 
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// counter words (this GPU's memory, zeroed once by the caller):
+//   [0] CTAs done with this call (the last one resets it)
+//   [1] seq of the latest verdict, [2] that verdict (1 = go, 0 = abort)
 __global__ void __launch_bounds__(256) peer_allreduce_kernel(
     float* const* __restrict__ bufs, uint32_t* const* __restrict__ flags, int rank, int world,
     uint32_t seq, float* __restrict__ out, long long n, float scale, uint32_t* counter,
@@ -55,11 +72,37 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(
   __shared__ int last_s;
   const uint32_t t1 = 2u * seq - 1u, t2 = 2u * seq;
   const uint32_t* mine = flags[rank];
-  if (blockIdx.x == 0 && threadIdx.x < world) {
-    __threadfence_system();  // this rank's buffer, written by earlier kernels
-    st_release_sys(flags[threadIdx.x] + rank, t1);
+  if (blockIdx.x == 0) {
+    if (threadIdx.x < world) {
+      __threadfence_system();  // this rank's buffer, written by earlier kernels
+      st_release_sys(flags[threadIdx.x] + rank, t1);
+    }
+    if (threadIdx.x == 0) {
+      const int ok = wait_flags(mine, world, t1, status) ? 1 : 0;
+      counter[2] = static_cast<uint32_t>(ok);
+      st_release_gpu(counter + 1, seq);  // publishes the verdict word above
+      ok_s = ok;
+    }
+  } else if (threadIdx.x == 0) {
+    // block 0 decides within its own 2 s budget; this wait only bounds a
+    // grid whose block 0 never ran
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t ns = 32;
+    int ok = 0;
+    for (;;) {
+      if (ld_acquire_gpu(counter + 1) == seq) {
+        ok = static_cast<int>(__ldcg(counter + 2));
+        break;
+      }
+      if (globaltimer_ns() - t0 > 2 * MLORA_WAIT_BUDGET_NS) {
+        record_status(status, kDevPeerTimeout);
+        break;
+      }
+      __nanosleep(ns);
+      if (ns < 1024) ns *= 2;
+    }
+    ok_s = ok;
   }
-  if (threadIdx.x == 0) ok_s = wait_flags(mine, world, t1, status) ? 1 : 0;
   __syncthreads();
   if (ok_s) {
     const long long n4 = n / 4;

@@ -166,7 +166,8 @@ class PeerAllReduce:
         self._hb = symm_mem.rendezvous(self.buffer, name)
         self._hf = symm_mem.rendezvous(self.flags, name)
         dist.barrier(self.group)
-        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        # arrival count, verdict seq and verdict (this GPU's memory)
+        self.counter = torch.zeros(4, dtype=torch.int32, device=dev)
         self.seq = 0
 
     @classmethod
@@ -197,3 +198,108 @@ class PeerAllReduce:
             self.counter.data_ptr(), torch.cuda.current_stream().cuda_stream)
         self._lib.check(st, "mlora_peer_allreduce")
         return out
+
+
+class BucketedGradExchange:
+    """Averages a flat gradient buffer over the ranks in buckets, each started
+    as soon as the backward has written its part, so the exchange of later
+    layers' gradients runs while earlier layers' backward still computes.
+
+    ``members`` lists, in the flat buffer's order, the (begin, end) element
+    range each gradient producer (one LoRALinear) writes.  Consecutive members
+    are grouped into buckets of at least ``bucket_bytes``.  ``ready(i)`` is
+    called once producer i's gradients are enqueued on the current stream;
+    when every member of a bucket is ready, the bucket's slice is all-reduced
+    (mean) -- on CUDA on a side stream after an event on the producing stream,
+    elsewhere (gloo on CPU) at once.  ``finish()`` starts any bucket that did
+    not fire (producers that took no part in this backward), in bucket order,
+    and makes the current stream wait for the exchange.
+
+    Every rank must run the same backward (the same producers in the same
+    order), so that all ranks issue the same collectives in the same order.  A
+    producer that reports twice in one step (a layer applied twice in one
+    forward) raises DistributedError: its bucket would be averaged before all
+    of its gradient had arrived."""
+
+    def __init__(self, flat: torch.Tensor, members: list[tuple[int, int]], group=None,
+                 bucket_bytes: int = 4 << 20):
+        self.flat = flat
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.nccl = dist.get_backend(group) == "nccl"
+        self.buckets: list[tuple[int, int, list[int]]] = []
+        self.bucket_of: list[int] = []
+        cur: list[int] = []
+        start = None
+        elt = flat.element_size()
+        for i, (b, e) in enumerate(members):
+            if cur and b != members[cur[-1]][1]:
+                raise ValueError("members must tile the flat buffer contiguously")
+            if not cur:
+                start = b
+            cur.append(i)
+            self.bucket_of.append(len(self.buckets))
+            if (e - start) * elt >= bucket_bytes or i == len(members) - 1:
+                self.buckets.append((start, e, cur))
+                cur = []
+        self.cuda = flat.is_cuda
+        self.stream = torch.cuda.Stream(device=flat.device) if self.cuda else None
+        self.armed = True
+        self.fired_order: list[int] = []
+        self._reset()
+
+    def _reset(self) -> None:
+        self.seen = [False] * len(self.bucket_of)
+        self.pending = [len(m) for _, _, m in self.buckets]
+        self.fired = [False] * len(self.buckets)
+        self.fired_order = []
+
+    def _fire(self, k: int) -> None:
+        b, e, _ = self.buckets[k]
+        if not self.fired_order:
+            maybe_inject_fault("before_allreduce", self.rank)
+        self.fired[k] = True
+        self.fired_order.append(k)
+        part = self.flat[b:e]
+        try:
+            if self.cuda:
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream(self.flat.device))
+                self.stream.wait_event(ev)
+                with torch.cuda.stream(self.stream):
+                    if self.nccl:
+                        dist.all_reduce(part, op=dist.ReduceOp.AVG, group=self.group)
+                    else:
+                        dist.all_reduce(part, group=self.group)
+                        part.mul_(1.0 / self.world)
+            else:
+                dist.all_reduce(part, group=self.group)
+                part.mul_(1.0 / self.world)
+        except RuntimeError as err:
+            raise DistributedError(
+                f"gradient bucket all-reduce failed on rank {self.rank} of {self.world}: "
+                f"{str(err).splitlines()[0] if str(err) else type(err).__name__}") from err
+
+    def ready(self, i: int) -> None:
+        """Producer i's gradients are enqueued on the current stream."""
+        if not self.armed:
+            return
+        if self.seen[i]:
+            raise DistributedError(
+                f"gradient producer {i} reported twice in one step (a layer used twice in one "
+                "forward); construct the trainer with overlap_grad_exchange=False")
+        self.seen[i] = True
+        k = self.bucket_of[i]
+        self.pending[k] -= 1
+        if self.pending[k] == 0:
+            self._fire(k)
+
+    def finish(self) -> None:
+        """Fires what is left and joins the exchange into the current stream."""
+        for k in range(len(self.buckets)):
+            if not self.fired[k]:
+                self._fire(k)
+        if self.cuda:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self.stream)
+        self._reset()

@@ -15,8 +15,10 @@ Flat buffers: every A and B of the model is a view into one fp32 master array
 (the factors the optimizer updates), with a compute-dtype copy (bf16 when the
 base weights are bf16) refreshed by one copy per step, and one fp32 gradient
 array that the backward kernels accumulate into.  The clip is then one
-reduction kernel and AdamW one kernel launch for all adapters; under
-data parallelism the gradient array is one NCCL all-reduce.
+reduction kernel and AdamW one kernel launch for all adapters.  Under data
+parallelism the gradient array is averaged over the ranks in per-layer buckets
+(NCCL on a side stream), each started as soon as the backward has written it,
+so the exchange overlaps the backward of the layers before it.
 """
 from __future__ import annotations
 
@@ -27,10 +29,11 @@ from dataclasses import dataclass, field
 from pathlib import Path
 
 import torch
+import torch.distributed as dist
 from torch import nn
 
 from . import kernels as _k
-from .distributed import average_gradients
+from .distributed import BucketedGradExchange, average_gradients
 from .exceptions import ConfigurationError
 from .layers import LoRALinear
 from .logging import logger
@@ -200,6 +203,20 @@ class FlatLoRAParams:
                                      self.compute[ob:ob + nb].view(sb))
         self.refresh_compute()
 
+    def attach_exchange(self, group=None, bucket_bytes: int = 4 << 20):
+        """A BucketedGradExchange over the flat gradient buffer, with each
+        layer's gradient sink calling it once its dA/dB are written."""
+        members = []
+        for name, m in self.layers:
+            oa = self.slices[f"{name}.A"][0]
+            ob, nb, _ = self.slices[f"{name}.B"]
+            members.append((oa, ob + nb))
+        ex = BucketedGradExchange(self.grad, members, group, bucket_bytes)
+        for i, (_, m) in enumerate(self.layers):
+            ga, gb = m._grad_sink[:2]
+            m._grad_sink = (ga, gb, True, lambda i=i: ex.ready(i))
+        return ex
+
     def refresh_compute(self) -> None:
         """Copies the fp32 masters into the compute-dtype views (one kernel)."""
         if self.compute is not None:
@@ -253,7 +270,7 @@ class LoRATrainer:
     """LoRA trainer (reference: trainer.py:173-302)."""
 
     def __init__(self, model: nn.Module, config: TrainingConfig | None = None,
-                 process_group=None):
+                 process_group=None, overlap_grad_exchange: bool = True):
         self.config = config or TrainingConfig()
         c = self.config
         if not any(isinstance(m, LoRALinear) for m in model.modules()):
@@ -267,6 +284,13 @@ class LoRATrainer:
         self.state = TrainingState()
         self.group = process_group
         self._micro = 0
+        # data parallel: per-layer gradient buckets averaged on a side stream
+        # while the backward of earlier layers runs (None: one all-reduce of
+        # the flat buffer after the backward)
+        self.exchange = None
+        if overlap_grad_exchange and dist.is_available() and dist.is_initialized() and \
+                dist.get_world_size(process_group) > 1:
+            self.exchange = self.params.attach_exchange(process_group)
         self._clip = torch.ones(2, dtype=torch.float32, device=self.params.master.device)
         Path(c.output_dir).mkdir(parents=True, exist_ok=True)
 
@@ -292,7 +316,12 @@ class LoRATrainer:
 
     def backward(self, batch: dict[str, torch.Tensor]) -> torch.Tensor:
         """Forward + backward of one micro-batch; LoRA gradients accumulate in
-        the flat fp32 buffer."""
+        the flat fp32 buffer (under data parallelism, the last micro-batch
+        before an optimizer step also starts each layer bucket's average as
+        soon as its gradients are written)."""
+        if self.exchange is not None:
+            gas = max(1, self.config.gradient_accumulation_steps)
+            self.exchange.armed = (self._micro + 1) % gas == 0
         loss = self._compute_loss(batch)
         scale = 1.0 / max(1, self.config.gradient_accumulation_steps)
         (loss * scale).backward()
@@ -302,7 +331,10 @@ class LoRATrainer:
         """Data-parallel average (one all-reduce), global-norm clip
         (trainer.py:237-240), AdamW; all on the device, no host sync."""
         g = self.params.grad
-        average_gradients(g, self.group)
+        if self.exchange is not None:
+            self.exchange.finish()
+        else:
+            average_gradients(g, self.group)
         if self.config.max_grad_norm > 0:
             _k.grad_norm_clip(g, self.config.max_grad_norm, out=self._clip)
             self.optimizer.update(self._clip[:1])

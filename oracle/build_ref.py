@@ -17,9 +17,12 @@ the reference itself.  Inputs are read where they lie in the reference tree:
   (the file as a whole needs simdgroup-matrix types the shim does not have).
 
 Everything this writes goes to ``oracle/_ref/`` (git-ignored).  Nothing here
-runs the reference's build system.  Usage::
+runs the reference's build system.  The reference tree must be named, by
+argument or by the ``MLORA_REFERENCE_DIR`` environment variable; there is no
+default location.  Usage::
 
-    python oracle/build_ref.py [--reference /path/to/MetalLora]
+    python oracle/build_ref.py --reference /path/to/MetalLora
+    MLORA_REFERENCE_DIR=/path/to/MetalLora python oracle/build_ref.py
 """
 from __future__ import annotations
 
@@ -32,7 +35,6 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-DEFAULT_REFERENCE = "/root/reference"
 
 # kernels.py string constant -> generated include name
 INLINE_BODIES = {
@@ -96,9 +98,16 @@ def extract_metal_blocks(path: Path, heads=METAL_BLOCKS) -> str:
 
 
 def build(reference: str | os.PathLike | None = None, quiet: bool = False) -> Path | None:
-    """Build ``oracle/_ref/libmlref.so``; returns its path, or None when the
-    reference tree is absent (the prebuilt library is then used as is)."""
-    ref = Path(reference or os.environ.get("MLORA_REFERENCE_DIR", DEFAULT_REFERENCE))
+    """Build ``oracle/_ref/libmlref.so``; returns its path, or None when no
+    reference tree is named or the named one is absent (the prebuilt library
+    is then used as is)."""
+    named = reference or os.environ.get("MLORA_REFERENCE_DIR")
+    if not named:
+        if not quiet:
+            print("[oracle/_ref] no reference tree named (--reference or MLORA_REFERENCE_DIR); "
+                  "skipping", file=sys.stderr)
+        return None
+    ref = Path(named)
     kernels_py = ref / "python" / "metal_lora" / "kernels.py"
     kernels_dir = ref / "kernels"
     if not kernels_py.is_file() or not (kernels_dir / "lora_quantized.metal").is_file():
@@ -127,6 +136,10 @@ def build(reference: str | os.PathLike | None = None, quiet: bool = False) -> Pa
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=None)
+    ap.add_argument("--reference", default=None,
+                    help="reference tree (default: $MLORA_REFERENCE_DIR)")
     args = ap.parse_args()
-    build(args.reference)
+    if not (args.reference or os.environ.get("MLORA_REFERENCE_DIR")):
+        ap.error("name the reference tree with --reference or MLORA_REFERENCE_DIR")
+    if build(args.reference) is None:
+        sys.exit(1)

@@ -141,3 +141,80 @@ def test_peer_failure_surfaces_as_error(mode):
     assert res[1][0] == "injected"
     assert res[0][0] == "distributed_error"
     assert res[0][1] < 30.0
+
+
+def _bucket_worker(rank, world, port, q):
+    from metallora_b200.distributed import BucketedGradExchange
+    from metallora_b200.exceptions import DistributedError
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=30))
+    try:
+        # seven producers of 3..9 floats; buckets of >= 32 bytes (8 floats)
+        sizes = [3, 4, 5, 6, 7, 8, 9]
+        members, off = [], 0
+        for n in sizes:
+            members.append((off, off + n))
+            off += n
+        flat = torch.zeros(off)
+        ex = BucketedGradExchange(flat, members, bucket_bytes=32)
+        buckets = [m for _, _, m in ex.buckets]
+        res = {"buckets": buckets}
+        for step in range(2):
+            # the backward writes producers last-to-first; producer 1 takes no
+            # part in this step (finish() must still average its bucket)
+            for i in reversed(range(len(sizes))):
+                if i == 1:
+                    continue
+                b, e = members[i]
+                flat[b:e] = float((rank + 1) * (i + 1) + step)
+                ex.ready(i)
+            b, e = members[1]
+            flat[b:e] = float((rank + 1) * 2 + step)
+            fired_before_finish = list(ex.fired_order)
+            ex.finish()
+            res[f"fired{step}"] = fired_before_finish
+            res[f"flat{step}"] = flat.tolist()
+        # disarmed (a micro-batch before the last): nothing fires
+        ex.armed = False
+        ex.ready(6)
+        res["disarmed_fired"] = list(ex.fired_order)
+        ex.armed = True
+        ex.ready(6)
+        try:
+            ex.ready(6)
+            res["double"] = "no error"
+        except DistributedError:
+            res["double"] = "error"
+        ex.finish()
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_bucketed_exchange():
+    """Per-layer gradient buckets: grouping, firing as soon as all members
+    reported (in backward order), averaging, finish() for silent producers,
+    disarming between micro-batches and the double-report error."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    r0 = res[0]
+    assert r0["buckets"] == [[0, 1, 2], [3, 4], [5], [6]]
+    # backward order 6,5,4,3,2,0: buckets 3, 2 and 1 fire as they complete;
+    # bucket 0 waits for producer 1 until finish()
+    assert r0["fired0"] == [3, 2, 1] and r0["fired1"] == [3, 2, 1]
+    sizes = [3, 4, 5, 6, 7, 8, 9]
+    for step in range(2):
+        want = []
+        for i, n in enumerate(sizes):
+            want += [1.5 * (i + 1) + step] * n  # mean over ranks of (rank+1)(i+1)+step
+        assert r0[f"flat{step}"] == want and res[1][f"flat{step}"] == want
+    assert r0["disarmed_fired"] == [] and r0["double"] == "error"

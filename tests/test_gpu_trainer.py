@@ -80,6 +80,12 @@ def _model(dev, dtype=torch.bfloat16, seed=0):
     return m
 
 
+def _bf16(a):
+    """fp64 -> bf16 (round to nearest even) -> fp64, as torch rounds."""
+    t = torch.from_numpy(np.asarray(a, np.float64).astype(np.float32)).to(torch.bfloat16)
+    return t.float().numpy().astype(np.float64)
+
+
 def test_trainer_gradients_and_step_match_oracle(cuda):
     from metallora_b200.layers import LoRALinear
     from metallora_b200.trainer import LoRATrainer, TrainingConfig
@@ -102,21 +108,24 @@ def test_trainer_gradients_and_step_match_oracle(cuda):
     Aq, Bq, Av, Bv = (f(t) for t in (q._compute_ab[0], q._compute_ab[1], v._compute_ab[0],
                                      v._compute_ab[1]))
     X = f(x).reshape(-1, 256)
-    H = lo.lora_forward(X, f(q.W0), Aq, Bq, 32.0, np.float64)
-    Hb = H.astype(np.float32).astype(np.float64)  # the hidden state is stored in bf16
-    Y = lo.lora_forward(Hb, f(v.W0), Av, Bv, 32.0, np.float64)
+    # every tensor the GPU path stores in bf16 between the two layers is
+    # rounded to bf16 here too: the hidden state, the output, its gradient
+    # (autograd hands the bf16 output a bf16 gradient) and the hidden state's
+    # gradient
+    H = _bf16(lo.lora_forward(X, f(q.W0), Aq, Bq, 32.0, np.float64))
+    Y = _bf16(lo.lora_forward(H, f(v.W0), Av, Bv, 32.0, np.float64))
     T = f(tgt).reshape(-1, 256)
     assert abs(float(loss) - np.mean((Y - T) ** 2)) / np.mean((Y - T) ** 2) < 2e-2
-    dY = 2 * (Y - T) / Y.size
-    gAv, gBv = lo.lora_backward(dY, Hb, Av, Bv, 32.0, None, np.float64)
-    dH = lo.lora_grad_x(dY, f(v.W0), Av, Bv, 32.0, np.float64)
+    dY = _bf16(2 * (Y - T) / Y.size)
+    gAv, gBv = lo.lora_backward(dY, H, Av, Bv, 32.0, None, np.float64)
+    dH = _bf16(lo.lora_grad_x(dY, f(v.W0), Av, Bv, 32.0, np.float64))
     gAq, gBq = lo.lora_backward(dH, X, Aq, Bq, 32.0, None, np.float64)
     got = {k: t.cpu().numpy() for k, t in tr.params.named_tensors().items()}  # masters (before)
     grads = {n: tr.params.grad[o:o + c].view(s).cpu().numpy()
              for n, (o, c, s) in tr.params.slices.items()}
     for name, ref in (("q_proj.A", gAq), ("q_proj.B", gBq), ("v_proj.A", gAv),
                       ("v_proj.B", gBv)):
-        assert rel_err(grads[name], ref) < 5e-2, name
+        assert rel_err(grads[name], ref) < 2e-2, name  # the bf16 tolerance
     # optimizer step = clip + AdamW on the device gradient, vs the oracle
     flat_g = tr.params.grad.cpu().numpy().copy()
     flat_p = tr.params.master.cpu().numpy().copy()

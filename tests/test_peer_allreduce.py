@@ -1,19 +1,23 @@
 """Peer all-reduce (mlora_peer_allreduce).  On one GPU the kernel runs its full
 protocol against itself (world 1: flags, counter reset, sequence numbers);
-the multi-rank protocol runs in bench.py under torchrun on several GPUs."""
+the multi-rank protocol runs in bench.py under torchrun on several GPUs, where
+every N > 1 line compares it with an NCCL all-reduce of the same buffer."""
 import pytest
 import torch
 
 
+def _ptrs(ts, dev):
+    return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=dev)
+
+
 @pytest.mark.gpu
-def test_peer_allreduce_world_one(cuda):
+@pytest.mark.parametrize("n", [4099, 148 * 256 * 4 * 3 + 5])  # one CTA / a full grid
+def test_peer_allreduce_world_one(cuda, n):
     from metallora_b200 import _lib
-    n = 4099  # a tail past the float4 body
     buf = torch.randn(n, device=cuda)
     flags = torch.zeros(4, dtype=torch.int32, device=cuda)
-    counter = torch.zeros(1, dtype=torch.int32, device=cuda)
-    bufs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=cuda)
-    fl = torch.tensor([flags.data_ptr()], dtype=torch.int64, device=cuda)
+    counter = torch.zeros(4, dtype=torch.int32, device=cuda)
+    bufs, fl = _ptrs([buf], cuda), _ptrs([flags], cuda)
     lib = _lib.load()
     for seq in range(1, 4):
         out = torch.empty_like(buf)
@@ -23,26 +27,27 @@ def test_peer_allreduce_world_one(cuda):
         torch.cuda.synchronize()
         assert torch.equal(out, buf * 0.5)
         assert int(flags[0]) == 2 * seq and int(counter[0]) == 0
+        assert int(counter[1]) == seq and int(counter[2]) == 1  # the grid's verdict: go
     assert _lib.device_status(reset=True) == 0
 
 
 @pytest.mark.gpu
-def test_peer_allreduce_wait_runs_out(cuda):
+@pytest.mark.parametrize("n", [1024, 148 * 256 * 4 * 2])  # one CTA / every SM
+def test_peer_allreduce_wait_runs_out(cuda, n):
     """Failure detection on the GPU without a fault: rank 0 of a two-rank
     exchange whose peer never raises its flags (a flag that nothing sets)
     gives up after the 2 s wait budget at the arrival barrier and again at the
-    exit barrier, records status 0x108 (peer timeout), skips the reduction and
-    returns; the context stays usable for the next call."""
+    exit barrier, records status 0x108 (peer timeout), skips the reduction in
+    every CTA (one verdict for the whole grid) and returns; the context stays
+    usable for the next call."""
     import time
 
     from metallora_b200 import _lib
-    n = 1024  # one CTA
     buf0, buf1 = torch.randn(n, device=cuda), torch.randn(n, device=cuda)
     flags0 = torch.zeros(4, dtype=torch.int32, device=cuda)
     flags1 = torch.zeros(4, dtype=torch.int32, device=cuda)
-    counter = torch.zeros(1, dtype=torch.int32, device=cuda)
-    bufs = torch.tensor([buf0.data_ptr(), buf1.data_ptr()], dtype=torch.int64, device=cuda)
-    fl = torch.tensor([flags0.data_ptr(), flags1.data_ptr()], dtype=torch.int64, device=cuda)
+    counter = torch.zeros(4, dtype=torch.int32, device=cuda)
+    bufs, fl = _ptrs([buf0, buf1], cuda), _ptrs([flags0, flags1], cuda)
     lib = _lib.load()
     stream = torch.cuda.current_stream().cuda_stream
     torch.cuda.synchronize()
@@ -56,14 +61,15 @@ def test_peer_allreduce_wait_runs_out(cuda):
     elapsed = time.monotonic() - t0
     assert _lib.device_status(reset=True) == 0x108
     assert 3.0 < elapsed < 20.0            # two bounded waits of 2 s
-    assert bool((out == 7.0).all())        # no partial reduction was written
+    assert bool((out == 7.0).all())        # no CTA wrote a partial reduction
     assert int(flags1[0]) == 2 and int(counter[0]) == 0  # exit flag raised, counter reset
+    assert int(counter[1]) == 1 and int(counter[2]) == 0  # the grid's verdict: abort
     # the context still works: a world-1 exchange right after
     buf = torch.randn(n, device=cuda)
-    solo = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=cuda)
     f_solo = torch.zeros(4, dtype=torch.int32, device=cuda)
-    fl_solo = torch.tensor([f_solo.data_ptr()], dtype=torch.int64, device=cuda)
+    solo, fl_solo = _ptrs([buf], cuda), _ptrs([f_solo], cuda)
     out2 = torch.empty_like(buf)
+    counter.zero_()
     st = lib.mlora_peer_allreduce(solo.data_ptr(), fl_solo.data_ptr(), 0, 1, 1, out2.data_ptr(),
                                   n, 1.0, counter.data_ptr(), stream)
     _lib.check(st, "mlora_peer_allreduce")
