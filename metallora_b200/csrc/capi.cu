@@ -253,10 +253,12 @@ int check_ptrs16(std::initializer_list<const void*> ptrs) {
 
 // ---- decode plan (M <= 16, bf16, K % 32 == 0) ------------------------------
 struct GemvPlan {
-  int splits;
-  uint32_t* counters;
-  size_t counter_bytes;
+  bool split;
+  int ctas;
+  uint32_t* flags;
+  size_t flag_bytes;
   float* st;
+  float* rt;
   float* partials;
   size_t bytes;
 };
@@ -265,55 +267,61 @@ bool use_gemv(int64_t M, int64_t K, int dtype) {
   return M <= kGemvMaxTokens && K % 32 == 0 && dtype == MLORA_DTYPE_BF16;
 }
 
-GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int scheme) {
+GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int scheme,
+                   int64_t group) {
   GemvPlan p;
-  p.splits = decode_config(scheme, M, N, K, r).splits;
+  const DecodeConfig cfg = decode_config(scheme, M, N, K, r, group);
+  p.split = cfg.split_blocks;
+  p.ctas = cfg.ctas;
   Carve c(ws);
-  p.counter_bytes = static_cast<size_t>(gemv_row_blocks(N)) * 4;
-  p.counters = static_cast<uint32_t*>(c.take(p.counter_bytes));
+  p.flag_bytes = p.split ? static_cast<size_t>(p.ctas) * 4 : 0;
+  p.flags = p.split ? static_cast<uint32_t*>(c.take(p.flag_bytes)) : nullptr;
   p.st = static_cast<float*>(
       c.take(static_cast<size_t>(rank_small_splits(K)) * M * (r > 0 ? r : 1) * 4));
-  p.partials = static_cast<float*>(c.take(static_cast<size_t>(p.splits) * M * N * 4));
+  p.rt = r > 0 ? static_cast<float*>(c.take(static_cast<size_t>(M) * N * 4)) : nullptr;
+  p.partials = p.split ? static_cast<float*>(c.take(static_cast<size_t>(p.ctas) * M * 128 * 4))
+                       : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
 
-// Decode-size forward: counters, sT = s.x.A^T (if a), split-K GEMV + rank term.
+// Decode-size forward: sT = s.x.A^T (if a) with the partial flags zeroed,
+// the rank term sT.B^T, then the stream-K GEMV adding it (the three launch
+// as a programmatic-dependent chain).
 int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
              int64_t group, const void* a, const void* b, void* y, int64_t M, int64_t K,
              int64_t N, int64_t r, float alpha, void* workspace, size_t workspace_bytes,
              cudaStream_t s, int64_t ldy = 0) {
-  const GemvPlan need = plan_gemv(nullptr, M, K, N, r, scheme);
+  const GemvPlan need = plan_gemv(nullptr, M, K, N, r, scheme, group);
   if (workspace == nullptr || workspace_bytes < need.bytes)
     return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
-  const GemvPlan p = plan_gemv(workspace, M, K, N, r, scheme);
-  // split counters: zeroed by the rank kernel when there is one, else by a
-  // memset; a single split uses none
+  const GemvPlan p = plan_gemv(workspace, M, K, N, r, scheme, group);
+  // partial flags: zeroed by the rank kernel when there is one, else by a
+  // memset; no shared row block uses none
   int rc;
-  if (a == nullptr && p.splits > 1) {
-    cudaError_t e = cudaMemsetAsync(p.counters, 0, p.counter_bytes, s);
+  if (a == nullptr && p.split) {
+    cudaError_t e = cudaMemsetAsync(p.flags, 0, p.flag_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "memset");
   }
   if (a != nullptr &&
-      (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.counters,
-                              p.splits > 1 ? static_cast<int64_t>(p.counter_bytes / 4) : 0, s)))
+      (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.flags,
+                              p.split ? p.ctas : 0, s)))
     return rc;
+  if (a != nullptr && (rc = launch_rank_up(p.st, K, b, M, N, r, p.rt, s))) return rc;
   GemvArgs g;
   g.scheme = scheme;
   g.x = x;
   g.w = w;
   g.scales_t = scales_t;
-  g.b = a != nullptr ? b : nullptr;
-  g.st = p.st;
+  g.rt = a != nullptr ? p.rt : nullptr;
   g.y = y;
   g.partials = p.partials;
-  g.counters = p.counters;
+  g.flags = p.flags;
   g.M = M;
   g.N = N;
   g.K = K;
   g.r = r;
   g.group = group;
-  g.splits = p.splits;
   g.ldy = ldy;
   return launch_gemv(g, s);
 }
@@ -623,7 +631,7 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
 
 // ---- plain linear and merge plans ----------------------------------------
 size_t linear_ws(int64_t M, int64_t K, int64_t N, int dtype) {
-  if (use_gemv(M, K, dtype)) return plan_gemv(nullptr, M, K, N, 0, 0).bytes;
+  if (use_gemv(M, K, dtype)) return plan_gemv(nullptr, M, K, N, 0, 0, 64).bytes;
   if (dtype != MLORA_DTYPE_F32) return 0;
   return plan_forward_f32(nullptr, M, K, N, 1, false).bytes;
 }
@@ -761,7 +769,7 @@ size_t mlora_lora_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int64
   if (M <= 0 || K <= 0 || N <= 0 || r <= 0) return 0;
   if (dtype == MLORA_DTYPE_F32) return plan_forward_f32(nullptr, M, K, N, r, true).bytes;
   size_t bytes = plan_forward(nullptr, M, K, r, true).bytes;
-  if (use_gemv(M, K, dtype)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r, 0).bytes);
+  if (use_gemv(M, K, dtype)) bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r, 0, 64).bytes);
   return bytes;
 }
 
@@ -1070,7 +1078,7 @@ size_t staged_w_bytes(int64_t N, int64_t K) { return align_up(static_cast<size_t
 size_t qfwd_lean_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int scheme, int64_t group) {
   size_t bytes = plan_forward(nullptr, M, K, r, true).bytes + qscales_bytes(N, K, group);
   if (use_gemv(M, K, MLORA_DTYPE_BF16))
-    bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r, scheme).bytes + qscales_bytes(N, K, group));
+    bytes = std::max(bytes, plan_gemv(nullptr, M, K, N, r, scheme, group).bytes + qscales_bytes(N, K, group));
   return bytes;
 }
 

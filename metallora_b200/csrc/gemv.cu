@@ -3,15 +3,39 @@
 //   sT[m, j] = s * sum_k x[m, k] A[j, k]                             (lora_rank_small_kernel)
 //   y[m, n]  = sum_k W[n, k] x[m, k] + sum_j B[n, j] sT[m, j]        (lora_decode_kernel)
 //
-// lora_decode_kernel is persistent.  Work items are (128-row block, k-split)
-// pairs; per CTA:
-//   warp 0      TMA producer: per stage, one [128 rows x 128 bytes] box of
-//               weight rows (128-byte swizzle) and, for quantised bases, the
-//               matching box of the prepared scale table [groups, rows];
-//   warps 2..   tensor cores: each owns two 16-row tiles and issues
+// lora_decode_kernel is persistent, one CTA per SM.  The weight is cut into
+// units of (128-row block, one stage of k); unit u = row_block * S + stage,
+// and CTA i streams the contiguous unit range [U i / P, U (i + 1) / P) of the
+// U units (stream-K), so every SM gets the same number of weight bytes to
+// within one stage whatever the shape.  A CTA's range splits at row-block
+// boundaries into segments:
+//   whole    a complete row block: summed here and written to y;
+//   publish  the part of a row block before its end (the range's last
+//            segment): summed here and stored as this CTA's one fp32 partial
+//            [M, 128], then a flag is raised;
+//   finish   the end of a row block that began in earlier CTAs (the range's
+//            first segment): once their flags are up, their partials are
+//            added in CTA order, then this CTA's own sum, and y is written.
+// Each CTA streams its publish segment first and its finish segment last, so
+// a finisher only ever waits for lower CTAs' first segments: no cycles, and
+// the summation order is fixed by the shape (bitwise repeatable).
+//
+// Per CTA:
+//   warp 0      TMA producer: per stage one [128 rows x 128 bytes] box of
+//               weight rows (128-byte swizzle), the matching box of the
+//               prepared scale table [groups, rows] (quantised bases) and the
+//               tokens' [x_rows x 64] boxes of x for the stage's k range
+//               (128-byte swizzle; rows past M are zero-filled);
+//   warp 1      waits for the rank kernel (programmatic dependent launch),
+//               folds its sT partials into shared memory, raises this CTA's
+//               partial flag, pre-sums the partials a finish segment needs and
+//               computes the rank term sum_j B[n, j] sT[m, j] of every row
+//               block this CTA writes, while the consumers stream;
+//   warps 2..9  tensor cores: 2 row groups (64 rows, four 16-row tiles each)
+//               x 4 k-groups (the stage's 64-wide k quads dealt round-robin);
 //               mma.m16n8k16 with the WEIGHTS as the A operand and the tokens
-//               (staged once per item in shared memory) as B, so one token
-//               fragment feeds both tiles.
+//               as B, so one token fragment feeds four tiles; the k-groups'
+//               sums meet in shared memory in fixed order at segment end.
 // Dequantisation never multiplies per weight:
 //   NF4   a 256-entry table (one copy per lane, so lookups never conflict) maps
 //         a code byte to the bf16 pair (L[lo], L[hi]) of the reference's
@@ -23,10 +47,12 @@
 // Every product is therefore exact up to the bf16 rounding of the NF4 levels,
 // and each scale applies once per quad in fp32: within the bf16 tolerance of
 // the reference's dequantise-then-multiply order, and deterministic.
-// With one k-split per row block the fragments get the rank-r term and are
-// written to y directly; otherwise split partials go to a workspace and the
-// last CTA of each row block sums them in split order, adds the rank-r term
-// and writes y.
+//
+// k order inside a 64-wide quad: lane q of an MMA step b takes k
+// 16q + 4 (b ^ f) .. + 3, f = q >> 1 for the 4-bit schemes (0 otherwise).
+// The weights of lane q for the whole quad are then one contiguous 8-byte
+// word pair, and the token fragment reads of the 32 lanes fall on distinct
+// bank pairs of the swizzled x box (two wavefronts, the minimum).
 #include <algorithm>
 #include <atomic>
 #include <string>
@@ -39,12 +65,23 @@
 namespace mlora {
 namespace {
 
-constexpr int kDecRows = 128;     // output rows per work item
-constexpr int kRowGroups = 4;     // MMA warps per k part, 32 rows (two 16-row tiles) each
-constexpr int kBoxBytes = 128;    // inner extent of one TMA box (128-byte swizzle)
-constexpr int kStageBytes = kDecRows * kBoxBytes;  // 16 KB
+constexpr int kDecRows = 128;     // output rows per row block
+constexpr int kBoxBytes = 128;    // inner extent of one weight box (128-byte swizzle)
+constexpr int kStageBytes = kDecRows * kBoxBytes;  // 16 KB of weights per stage
 constexpr int kMaxTok = 16;
-constexpr int kSmemPerSm = 227 * 1024;
+constexpr int kRowGroups = 2;     // consumer warps per k-group, 64 rows each
+constexpr int kKG = 4;            // k-groups
+constexpr int kTiles = 4;         // 16-row MMA tiles per consumer warp
+constexpr int kConsumers = kRowGroups * kKG;
+constexpr int kDecThreads = 64 + 32 * kConsumers;  // 320
+// Dynamic shared memory of the decode CTA: the SM's 227 KB less the static
+// barriers and 20 KB left for the small rank kernels that run beside it as
+// programmatic dependents/primaries (they then need not wait for an SM).
+constexpr int kSmemMax = 227 * 1024 - 1024 - 20 * 1024;
+// Threads of the rank kernels: few, so that their registers fit beside a
+// decode CTA on the same SM.
+constexpr int kRankThreads = 64;
+constexpr int kMaxStages = 8;
 
 // scheme 0 = dense bf16 weights, else QuantScheme.
 template <int kScheme>
@@ -53,35 +90,26 @@ struct Dec {
   static constexpr int kStageK = kBoxBytes * 8 / kBits;  // k per stage: 64 / 128 / 256
   static constexpr int kQuads = kStageK / 64;            // 64-wide k quads per stage
   static constexpr int kQuadBytes = 64 * kBits / 8;      // bytes of one quad of one row
+  static constexpr int kWords = kQuadBytes / 16;         // 32-bit words per lane per row per quad
   static constexpr bool kScaled = kScheme != 0;
-  static constexpr int kStages = 4;
-  // NF4 pair table: 256 entries, one copy per 16 lanes (at most 2-way bank
-  // conflicts), small enough for two CTAs per SM
-  static constexpr int kLutCopies = 16;
+  static constexpr bool kFlip = kScheme == kNF4 || kScheme == kINT4;
+  static constexpr int kLutCopies = 32;
   static constexpr int kLutBytes = kScheme == kNF4 ? 256 * kLutCopies * 4 : 0;
-  static constexpr int kScaleSlot = 4 * kDecRows * 4;  // up to 4 groups x 128 rows x 4 bytes
-  static constexpr int kScaleBytes = kScaled ? kStages * kScaleSlot : 0;
-  static constexpr int kMinBlocks = 2;  // registers sized for two CTAs per SM
-  // k parts: the quads of each stage are dealt round-robin to kKS groups of
-  // kRowGroups MMA warps (more warps to hide the table-lookup latency of NF4);
-  // the groups' accumulators are summed in order at the end of each item
-  static constexpr int kKS = 1;
-  static constexpr int kConsumers = kRowGroups * kKS;
-  static constexpr int kThreads = 64 + 32 * kConsumers;
-  static constexpr int kRedBytes = (kKS - 1) * kRowGroups * 32 * 16 * 4;
 };
 
 struct DecParams {
-  const __nv_bfloat16* x;  // [M, K]
-  const __nv_bfloat16* b;  // [N, r] (nullptr: no rank term)
-  const float* st;         // [st_splits, M, r] partial sums of s.x.A^T
-  int st_splits;
-  __nv_bfloat16* y;        // [M, N]
-  float* partials;         // [splits, M, N]
-  uint32_t* counters;      // [row blocks]
-  int M, N, K, r, group, gps;  // gps: scale-table groups per stage box
-  int splits, kspan, items, row_blocks;
-  long long ldy;  // row stride of y
+  const float* rt;         // [M, N] rank term s.(x.A^T).B^T (nullptr: none)
+  __nv_bfloat16* y;        // [M, ldy]
+  long long ldy;
+  float* partials;         // [ctas, M, 128]: one per CTA
+  uint32_t* flags;         // [ctas], zeroed before the launch
+  int M, N, K, group, gps;
+  int S;                   // stages per row block
+  long long units;         // row blocks * S
+  int stages;              // ring depth
+  int x_rows;              // token rows of one x box (8 or 16)
+  int x_slot, scale_slot;  // bytes per stage
+  int off_x, off_scale, off_lut, off_red, off_rt, off_psum, off_rtf;  // from the aligned base
   uint32_t* status;
 };
 
@@ -100,23 +128,33 @@ __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // The four A-fragment words of one 16-row tile for MMA step b of a quad:
-// {row g: k+0,1 | row g+8: k+0,1 | row g: k+2,3 | row g+8: k+2,3}, k = 16q + 4b
-// within the quad (INT4 pairs (k, k+2) and (k+1, k+3) instead; its tokens are
-// staged in that order).  w0 / w1: the lane's words of rows g / g+8; z0 / z1:
-// their offset words.
+// {row g: k+0,1 | row g+8: k+0,1 | row g: k+2,3 | row g+8: k+2,3} with
+// k = 16q + 4 bb, bb = b ^ f (INT4 pairs (k, k+2) and (k+1, k+3) instead; its
+// token fragments are permuted to match).  w0 / w1: the lane's words of rows
+// g / g+8; z0 / z1: their offset words; odd: bb & 1 for this lane.
 template <int kScheme, int kWords>
 __device__ __forceinline__ void a_frags(const uint32_t (&w0)[kWords], const uint32_t (&w1)[kWords],
-                                        uint32_t z0, uint32_t z1, int b, const uint32_t* lut_lane,
-                                        uint32_t (&a)[4]) {
+                                        uint32_t z0, uint32_t z1, int b, bool odd,
+                                        const uint32_t* lut_lane, uint32_t (&a)[4]) {
   if constexpr (kScheme == 0) {
     a[0] = w0[2 * b];
     a[2] = w0[2 * b + 1];
     a[1] = w1[2 * b];
     a[3] = w1[2 * b + 1];
   } else if constexpr (kScheme == kNF4) {
-    // word b/2 holds k 8(b/2)..+7; its bytes 2(b%2), 2(b%2)+1 are k+0,1 and k+2,3
-    const uint32_t s0 = (b & 1) ? 0x4442u : 0x4440u, s1 = (b & 1) ? 0x4443u : 0x4441u;
+    // word b/2 holds k 8(b/2)..+7; its bytes 2(bb%2), 2(bb%2)+1 are k+0,1 and k+2,3
+    const uint32_t s0 = odd ? 0x4442u : 0x4440u, s1 = odd ? 0x4443u : 0x4441u;
     const uint32_t u0 = w0[b >> 1], u1 = w1[b >> 1];
     constexpr int kC = Dec<kScheme>::kLutCopies;
     a[0] = lut_lane[__byte_perm(u0, 0, s0) * kC];
@@ -124,7 +162,7 @@ __device__ __forceinline__ void a_frags(const uint32_t (&w0)[kWords], const uint
     a[1] = lut_lane[__byte_perm(u1, 0, s0) * kC];
     a[3] = lut_lane[__byte_perm(u1, 0, s1) * kC];
   } else if constexpr (kScheme == kINT4) {
-    const uint32_t sel = (b & 1) ? 0x4342u : 0x4140u;  // code bytes -> bits 0-7 and 16-23
+    const uint32_t sel = odd ? 0x4342u : 0x4140u;  // code bytes -> bits 0-7 and 16-23
     const uint32_t t0 = __byte_perm(w0[b >> 1], 0, sel), t1 = __byte_perm(w1[b >> 1], 0, sel);
     a[0] = bf16x2_sub((t0 & 0x000F000Fu) | 0x43004300u, z0);         // (k, k+2)
     a[2] = bf16x2_sub(((t0 >> 4) & 0x000F000Fu) | 0x43004300u, z0);  // (k+1, k+3)
@@ -179,439 +217,521 @@ __device__ __forceinline__ void add_rank_term(const __nv_bfloat16* brow, const f
   }
 }
 
+// ------------------------------------------------------------- work split --
+
+__device__ __forceinline__ long long unit_begin(long long units, int cta, int ctas) {
+  return units * cta / ctas;
+}
+
+// One CTA's segments in processing order: [publish], whole blocks, [finish].
+struct DecPlan {
+  bool has_pub, has_fin;
+  int pub_rb, pub_s0, pub_s1;  // publish segment (ends before its block's end)
+  int fin_rb, fin_s0;          // finish segment [fin_s0, S)
+  int w_lo, n_whole;           // whole blocks w_lo .. w_lo + n_whole - 1
+  int n_seg;
+};
+
+__device__ __forceinline__ DecPlan make_plan(const DecParams& p, int cta, int ctas) {
+  DecPlan pl;
+  const long long u0 = unit_begin(p.units, cta, ctas), u1 = unit_begin(p.units, cta + 1, ctas);
+  const int ra = static_cast<int>(u0 / p.S), rb_last = static_cast<int>((u1 - 1) / p.S);
+  const int sa = static_cast<int>(u0 - static_cast<long long>(ra) * p.S);
+  const int eb = static_cast<int>(u1 - static_cast<long long>(rb_last) * p.S);  // end stage in last block
+  pl.has_pub = pl.has_fin = false;
+  pl.pub_rb = pl.pub_s0 = pl.pub_s1 = pl.fin_rb = pl.fin_s0 = 0;
+  if (ra == rb_last) {
+    const bool begins = sa == 0, ends = eb == p.S;
+    pl.w_lo = ra;
+    pl.n_whole = (begins && ends) ? 1 : 0;
+    if (!ends) {
+      pl.has_pub = true;
+      pl.pub_rb = ra;
+      pl.pub_s0 = sa;
+      pl.pub_s1 = eb;
+    } else if (!begins) {
+      pl.has_fin = true;
+      pl.fin_rb = ra;
+      pl.fin_s0 = sa;
+    }
+  } else {
+    int lo = ra + 1, hi = rb_last - 1;  // whole blocks between the ends
+    if (sa == 0) {
+      lo = ra;
+    } else {
+      pl.has_fin = true;
+      pl.fin_rb = ra;
+      pl.fin_s0 = sa;
+    }
+    if (eb == p.S) {
+      hi = rb_last;
+    } else {
+      pl.has_pub = true;
+      pl.pub_rb = rb_last;
+      pl.pub_s0 = 0;
+      pl.pub_s1 = eb;
+    }
+    pl.w_lo = lo;
+    pl.n_whole = hi >= lo ? hi - lo + 1 : 0;
+  }
+  pl.n_seg = (pl.has_pub ? 1 : 0) + pl.n_whole + (pl.has_fin ? 1 : 0);
+  return pl;
+}
+
+// kind: 0 whole, 1 publish, 2 finish
+__device__ __forceinline__ void plan_segment(const DecPlan& pl, int S, int t, int& rb, int& s0,
+                                             int& s1, int& kind) {
+  if (pl.has_pub) {
+    if (t == 0) {
+      rb = pl.pub_rb;
+      s0 = pl.pub_s0;
+      s1 = pl.pub_s1;
+      kind = 1;
+      return;
+    }
+    --t;
+  }
+  if (t < pl.n_whole) {
+    rb = pl.w_lo + t;
+    s0 = 0;
+    s1 = S;
+    kind = 0;
+    return;
+  }
+  rb = pl.fin_rb;
+  s0 = pl.fin_s0;
+  s1 = S;
+  kind = 2;
+}
+
+// First CTA whose range holds unit u.
+__device__ __forceinline__ int unit_owner(long long units, int ctas, long long u) {
+  int j = static_cast<int>(u * ctas / units);
+  if (j >= ctas) j = ctas - 1;
+  while (j + 1 < ctas && unit_begin(units, j + 1, ctas) <= u) ++j;
+  while (j > 0 && unit_begin(units, j, ctas) > u) --j;
+  return j;
+}
+
 template <int kScheme, int kNT>
-__global__ void __launch_bounds__(Dec<kScheme>::kThreads, Dec<kScheme>::kMinBlocks)
+__global__ void __launch_bounds__(kDecThreads, 1)
     lora_decode_kernel(const __grid_constant__ CUtensorMap wmap,
-                       const __grid_constant__ CUtensorMap smap, const DecParams p) {
+                       const __grid_constant__ CUtensorMap smap,
+                       const __grid_constant__ CUtensorMap xmap, const DecParams p) {
   using D = Dec<kScheme>;
-  constexpr int kWords = D::kQuadBytes / 16;  // 32-bit words per lane per row per quad: 2/4/8
+  constexpr int kWords = D::kWords;
   extern __shared__ uint8_t smem_raw[];
-  // ring (1024-byte aligned for the 128-byte swizzle) | scale slots | lut |
-  // k-part partial sums | rank term per row | sT [M, r] | tokens [M, kspan + 4]
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  const uint32_t* scl = reinterpret_cast<const uint32_t*>(ring + D::kStages * kStageBytes);
-  uint32_t* lut = reinterpret_cast<uint32_t*>(ring + D::kStages * kStageBytes + D::kScaleBytes);
-  float* red = reinterpret_cast<float*>(ring + D::kStages * kStageBytes + D::kScaleBytes +
-                                        D::kLutBytes);
-  float* rt = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(red) + D::kRedBytes);
-  float* sts = rt + kMaxTok * kDecRows;
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sts + ((kMaxTok * p.r + 3) & ~3));
-  __shared__ __align__(8) uint64_t full_bar[D::kStages];
-  __shared__ __align__(8) uint64_t empty_bar[D::kStages];
-  __shared__ __align__(8) uint64_t st_bar;    // sT folded into shared memory
-  __shared__ __align__(8) uint64_t rt_full;   // rank term of the current item's rows ready
+  // weight ring (1024-byte aligned for the 128-byte swizzle) | x ring | scale
+  // ring | lut | k-group sums | rank term [M, 128] | earlier partials [M, 128] |
+  // the finish block's rank term [M, 128]
+  uint8_t* base = align_smem<1024>(smem_raw);
+  uint8_t* ring = base;
+  uint8_t* xring = base + p.off_x;
+  const uint8_t* sring = base + p.off_scale;
+  uint32_t* lut = reinterpret_cast<uint32_t*>(base + p.off_lut);
+  float* red = reinterpret_cast<float*>(base + p.off_red);
+  float* rt = reinterpret_cast<float*>(base + p.off_rt);
+  float* psum = reinterpret_cast<float*>(base + p.off_psum);
+  float* rtf = reinterpret_cast<float*>(base + p.off_rtf);
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t pub_done;  // this CTA's partial is in global memory
+  __shared__ __align__(8) uint64_t rt_full;   // rank term (and earlier partials) of a block ready
   __shared__ __align__(8) uint64_t rt_empty;  // ... and consumed
-  __shared__ uint32_t last_flag;
+  __shared__ __align__(8) uint64_t fin_ready; // the finish block's partials and rank term
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int stages_per_item = p.kspan / D::kStageK;
-  const int xstride = p.kspan + 4;  // bf16 elements: rows 8 bytes off a 128-byte multiple
+  const int cta = blockIdx.x, ctas = gridDim.x;
+  // the CTA's plan lives in shared memory (read where needed, not held in
+  // registers through the stage loops)
+  __shared__ DecPlan pl_s;
+  const DecPlan& pl = pl_s;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < D::kStages; ++s) {
+    pl_s = make_plan(p, cta, ctas);
+    for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], D::kConsumers);
+      mbar_init(&empty_bar[s], kConsumers);
     }
-    mbar_init(&st_bar, 1);
+    mbar_init(&pub_done, kRowGroups);
     mbar_init(&rt_full, 1);
     mbar_init(&rt_empty, kRowGroups);
+    mbar_init(&fin_ready, 1);
     fence_mbarrier_init();
   }
-  if constexpr (kScheme == kNF4) {
-    // lut[e * kLutCopies + c] = (bf16 L[e & 15], bf16 L[e >> 4]) for every copy c
-    for (int i = threadIdx.x; i < 256 * D::kLutCopies; i += blockDim.x) {
-      const int e = i / D::kLutCopies;
-      lut[i] = pack2<__nv_bfloat16>(kNF4Levels[e & 15], kNF4Levels[e >> 4]);
+  // set-up barrier 2: the producer arrives as soon as the mbarriers are
+  // initialised and starts streaming; the other warps first build the table
+  if (warp == 0) {
+    named_bar_arrive(2, kDecThreads);
+  } else {
+    if constexpr (kScheme == kNF4) {
+      // lut[e * 32 + c] = (bf16 L[e & 15], bf16 L[e >> 4]) for every lane c
+      for (int i = threadIdx.x - 32; i < 256 * D::kLutCopies; i += blockDim.x - 32) {
+        const int e = i / D::kLutCopies;
+        lut[i] = pack2<__nv_bfloat16>(kNF4Levels[e & 15], kNF4Levels[e >> 4]);
+      }
     }
+    named_bar_sync(2, kDecThreads);
   }
-  __syncthreads();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       prefetch_tmap(&wmap);
+      prefetch_tmap(&xmap);
       if constexpr (D::kScaled) prefetch_tmap(&smap);
-      const uint32_t stage_tx = kStageBytes + (D::kScaled ? p.gps * kDecRows * 4 : 0);
+      const uint32_t stage_tx = kStageBytes + (D::kScaled ? p.gps * kDecRows * 4 : 0) +
+                                D::kQuads * p.x_rows * 128;
       bool ok = true;
-      uint32_t it = 0;
-      for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int rb = item % p.row_blocks, split = item / p.row_blocks;
-        const int kb0 = split * p.kspan * D::kBits / 8;
-        for (int sl = 0; sl < stages_per_item; ++sl) {
-          const int s = it % D::kStages;
-          if (!mbar_wait(&empty_bar[s], ((it / D::kStages) & 1) ^ 1, p.status, kDevTimeoutEmpty)) {
+      uint32_t issued = 0;
+      int slot = 0;
+      uint32_t phase = 0;
+      for (int t = 0; t < pl.n_seg && ok; ++t) {
+        int rb, s0, s1, kind;
+        plan_segment(pl, p.S, t, rb, s0, s1, kind);
+        for (int s = s0; s < s1; ++s) {
+          if (!mbar_wait(&empty_bar[slot], phase ^ 1, p.status, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[s], stage_tx);
-          tma_load_2d(ring + s * kStageBytes, &wmap, &full_bar[s], kb0 + sl * kBoxBytes,
+          mbar_arrive_expect_tx(&full_bar[slot], stage_tx);
+          tma_load_2d(ring + slot * kStageBytes, &wmap, &full_bar[slot], s * kBoxBytes,
                       rb * kDecRows);
           if constexpr (D::kScaled)  // [gps groups x 128 rows] of the prepared scale table
-            tma_load_2d(ring + D::kStages * kStageBytes + s * D::kScaleSlot, &smap, &full_bar[s],
-                        rb * kDecRows, (split * p.kspan + sl * D::kStageK) / p.group);
-          ++it;
+            tma_load_2d(const_cast<uint8_t*>(sring) + slot * p.scale_slot, &smap,
+                        &full_bar[slot], rb * kDecRows, (s * D::kStageK) / p.group);
+#pragma unroll
+          for (int j = 0; j < D::kQuads; ++j)  // the tokens' k range of this stage
+            tma_load_2d(xring + slot * p.x_slot + j * p.x_rows * 128, &xmap, &full_bar[slot],
+                        s * D::kStageK + 64 * j, 0);
+          ++issued;
+          if (++slot == p.stages) {
+            slot = 0;
+            phase ^= 1;
+          }
         }
       }
       // drain: every issued stage has landed before this thread (and so the
       // CTA's shared memory) may go away
-      for (uint32_t k = it > static_cast<uint32_t>(D::kStages) ? it - D::kStages : 0; k < it; ++k)
-        mbar_wait(&full_bar[k % D::kStages], (k / D::kStages) & 1, p.status, kDevTimeoutDrain);
+      const uint32_t st = static_cast<uint32_t>(p.stages);
+      for (uint32_t k = issued > st ? issued - st : 0; k < issued; ++k)
+        mbar_wait(&full_bar[k % st], (k / st) & 1, p.status, kDevTimeoutDrain);
     }
     return;
   }
   if (warp == 1) {
     // ---------------------------------------------------------- rank warp --
-    // sT from the preceding rank kernel (this grid's programmatic primary):
-    // wait for it, fold its k-slices in order into shared memory; then, with
-    // a single k-split, the rank term sum_j B[n, j] sT[m, j] of each item's
-    // rows (4 rows per lane), concurrently with the consumers' stage loop.
-    // B's rows of this CTA's first item go to L2 before the wait.
-    auto prefetch_b = [&](int item) {
-      if (p.b == nullptr || p.splits != 1 || item >= p.items) return;
-      const int rb = item % p.row_blocks;
-      const int rows = min(kDecRows, p.N - rb * kDecRows);
-      const char* base = reinterpret_cast<const char*>(p.b + static_cast<long long>(rb) * kDecRows * p.r);
-      for (int off = lane * 128; off < rows * p.r * 2; off += 32 * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+    // rows [rb*128, +128) of the rank term (computed by the preceding rank
+    // kernels over all N) into shared memory: dst[m, row]
+    auto copy_rt = [&](int rb, float* dst) {
+      for (int i = lane; i < p.M * kDecRows; i += 32) {
+        const int m = i / kDecRows, row = i % kDecRows, n = rb * kDecRows + row;
+        dst[i] = n < p.N ? __ldcg(p.rt + static_cast<long long>(m) * p.N + n) : 0.f;
+      }
     };
-    prefetch_b(blockIdx.x);
+    // the rank term comes from this grid's programmatic primary (the rank
+    // kernels, which also zeroed the partial flags)
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (p.b != nullptr) {
-      for (int i = lane; i < p.M * p.r; i += 32) {
-        float v = 0.f;
-        for (int s0 = 0; s0 < p.st_splits; s0 += 8) {  // loads in flight together
-          float t8[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            t8[u] = s0 + u < p.st_splits
-                        ? __ldcg(p.st + static_cast<long long>(s0 + u) * p.M * p.r + i)
-                        : 0.f;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) v += t8[u];
-        }
-        sts[i] = v;
-      }
+    if (p.rt != nullptr && pl.has_fin) copy_rt(pl.fin_rb, rtf);
+    int w = 0;  // whole blocks whose rank term is staged
+    if (pl.n_whole > 0) {  // the first one at once (its buffer starts free)
+      if (p.rt != nullptr) copy_rt(pl.w_lo, rt);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rt_full);
+      w = 1;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&st_bar);
-    if (p.splits == 1) {
-      uint32_t k = 0;
-      for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++k) {
-        const int rb = item % p.row_blocks;
-        prefetch_b(item + gridDim.x);
-        if (!mbar_wait(&rt_empty, (k & 1) ^ 1, p.status, kDevTimeoutEmpty)) break;
-        for (int rr = lane; rr < kDecRows; rr += 32) {
-          float out[kMaxTok];
-#pragma unroll
-          for (int m = 0; m < kMaxTok; ++m) out[m] = 0.f;
-          const int n = rb * kDecRows + rr;
-          if (p.b != nullptr && n < p.N)
-            add_rank_term(p.b + static_cast<long long>(n) * p.r, sts, p.M, p.r, out);
-#pragma unroll
-          for (int m = 0; m < kMaxTok; ++m)
-            if (m < p.M) rt[m * kDecRows + rr] = out[m];
+    if (pl.has_pub) {
+      // the consumers stored this CTA's partial (and fenced): raise its flag
+      // before waiting for anyone else's, so flags never wait on one another
+      const bool ok = mbar_wait(&pub_done, 0, p.status, kDevTimeoutReduce);
+      if (lane == 0 && ok) st_release_gpu(p.flags + cta, 1u);
+    }
+    if (pl.has_fin) {
+      // the partials of the CTAs before this one that cover the start of the
+      // finish block (their publish segments come first), summed in CTA
+      // (= k) order, ready long before this CTA streams the block's end
+      const int jlo = unit_owner(p.units, ctas, static_cast<long long>(pl.fin_rb) * p.S);
+      bool ok = true;
+      const uint64_t t0 = globaltimer_ns();
+      for (int j = jlo; j < cta && ok; ++j) {
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(p.flags + j) == 0u) {
+          if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > MLORA_WAIT_BUDGET_NS) {
+            record_status(p.status, kDevTimeoutReduce);
+            ok = false;
+            break;
+          }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rt_full);
       }
+      const int n4 = p.M * kDecRows / 4;
+      const float4* parts = reinterpret_cast<const float4*>(p.partials);
+      float4* ps4 = reinterpret_cast<float4*>(psum);
+      for (int i = lane; i < n4; i += 32) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = jlo; j0 < cta && ok; j0 += 8) {
+          float4 v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)  // up to eight publishers' loads in flight
+            v[u] = j0 + u < cta ? __ldcg(parts + static_cast<long long>(j0 + u) * n4 + i)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {  // in publisher order
+            if (j0 + u < cta) {
+              acc.x += v[u].x;
+              acc.y += v[u].y;
+              acc.z += v[u].z;
+              acc.w += v[u].w;
+            }
+          }
+        }
+        ps4[i] = acc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&fin_ready);
+    }
+    for (; w < pl.n_whole; ++w) {
+      if (!mbar_wait(&rt_empty, (w & 1) ^ 1, p.status, kDevTimeoutEmpty)) break;
+      if (p.rt != nullptr) copy_rt(pl.w_lo + w, rt);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rt_full);
     }
     return;
   }
 
   // ------------------------------------------------------------ consumers ----
   // Every consumer thread passes every named barrier, also after a timed-out
-  // wait (then it skips the remaining waits and math), so none can be stranded.
-  constexpr int kAll = 32 * D::kConsumers;  // consumer threads (named barrier 1)
-  constexpr int kLead = 32 * kRowGroups;    // k part 0 threads (named barrier 2)
+  // wait (then it skips the math), so none can be stranded.
+  constexpr int kAll = 32 * kConsumers;  // named barrier 1
   const int cw = warp - 2;
-  const int rg = cw % kRowGroups;           // 32-row group
-  const int kp = cw / kRowGroups;           // k part
-  const int ct = threadIdx.x - 64;          // k part 0: 0..127 = row within the block
+  const int rg = cw % kRowGroups;        // 64-row group
+  const int kg = cw / kRowGroups;        // k-group
   const int g = lane >> 2, q = lane & 3;
-  const uint32_t* lut_lane = lut + (lane % D::kLutCopies);
+  const int fq = D::kFlip ? (q >> 1) : 0;
+  const uint32_t* lut_lane = lut + lane;
   bool ok = true;
-  uint32_t it = 0;
-  uint32_t items_done = 0;  // this CTA's items so far (rt_full parity)
+  int slot = 0;
+  uint32_t phase = 0;
+  uint32_t writes = 0;  // row blocks written so far (rt_full parity)
 
-  for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
-    const int rb = item % p.row_blocks, split = item / p.row_blocks;
-    const int k0 = split * p.kspan;
-    // this item's token slice: M rows x kspan (zero beyond K); rows >= M are
-    // never read.  Loads go out in batches of 8 per thread before any store.
-    named_bar_sync(1, kAll);
-    {
-      const int chunks = p.M * (p.kspan / 8);
-      for (int i0 = 0; i0 < chunks; i0 += 8 * kAll) {
-        uint4 v[8];
+  for (int t = 0; t < pl.n_seg; ++t) {
+    int rb, s0, s1, kind;
+    plan_segment(pl, p.S, t, rb, s0, s1, kind);
+    float acc[kTiles][kNT][4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = i0 + u * kAll + ct;
-          const int m = i / (p.kspan / 8), c = (i % (p.kspan / 8)) * 8;
-          v[u] = make_uint4(0, 0, 0, 0);
-          if (i < chunks && k0 + c < p.K)
-            v[u] = __ldg(
-                reinterpret_cast<const uint4*>(p.x + static_cast<long long>(m) * p.K + k0 + c));
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = i0 + u * kAll + ct;
-          if (i >= chunks) break;
-          const int m = i / (p.kspan / 8), c = (i % (p.kspan / 8)) * 8;
-          uint4 w4 = v[u];
-          if constexpr (kScheme == kINT4) {  // (k0, k2, k1, k3) within each group of four
-            w4 = make_uint4(__byte_perm(v[u].x, v[u].y, 0x5410), __byte_perm(v[u].x, v[u].y, 0x7632),
-                            __byte_perm(v[u].z, v[u].w, 0x5410), __byte_perm(v[u].z, v[u].w, 0x7632));
-          }
-          uint2* dst = reinterpret_cast<uint2*>(xs + m * xstride + c);
-          dst[0] = make_uint2(w4.x, w4.y);
-          dst[1] = make_uint2(w4.z, w4.w);
-        }
-      }
-    }
-    named_bar_sync(1, kAll);
-
-    float acc[2][kNT][4];
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
+    for (int i = 0; i < kTiles; ++i)
 #pragma unroll
       for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[t][nt][c] = 0.f;
+        for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.f;
 
-    for (int sl = 0; sl < stages_per_item; ++sl, ++it) {
-      const int s = it % D::kStages;
+    for (int s = s0; s < s1; ++s) {
       // warp-uniform, so the __syncwarp below always sees all 32 lanes
       ok = __all_sync(0xffffffffu,
-                      ok && mbar_wait(&full_bar[s], (it / D::kStages) & 1, p.status,
-                                      kDevTimeoutFull));
-      if (!ok) continue;
-      const uint8_t* stage = ring + s * kStageBytes;
+                      ok && mbar_wait(&full_bar[slot], phase, p.status, kDevTimeoutFull));
+      if (ok) {
+        const uint8_t* stage = ring + slot * kStageBytes;
+        const uint8_t* xst = xring + slot * p.x_slot;
+        const uint32_t* scl = reinterpret_cast<const uint32_t*>(sring + slot * p.scale_slot);
+        // this warp's quad of the stage, if any (quads are dealt round-robin
+        // over the k-groups along the row block's k); one copy of the body
+        const int j = ((kg - s * D::kQuads) % kKG + kKG) % kKG;
+        if (j < D::kQuads) {
+          // the lane's words of rows g and g+8 of the four tiles (swizzled 16-byte chunks)
+          uint32_t w[kTiles][2][kWords];
+          uint2 e[kTiles][2];
 #pragma unroll
-      for (int j = 0; j < D::kQuads; ++j) {
-        if (D::kKS > 1 && (sl * D::kQuads + j) % D::kKS != kp) continue;  // another k part's
-        // the lane's words of rows g and g+8 of both tiles (swizzled 16-byte chunks)
-        uint32_t w[2][2][kWords];
-        uint2 e[2][2];
+          for (int i = 0; i < kTiles; ++i) {
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int row = rg * 32 + t * 16 + h * 8 + g;
-            const uint8_t* rp = stage + row * kBoxBytes;
-            if constexpr (kWords == 2) {
-              const int off = j * D::kQuadBytes + 8 * q;
-              const uint2 v = *reinterpret_cast<const uint2*>(
-                  rp + ((((off >> 4) ^ g) << 4) | (off & 15)));
-              w[t][h][0] = v.x;
-              w[t][h][1] = v.y;
-            } else if constexpr (kWords == 4) {
-              const int chunk = (j * D::kQuadBytes >> 4) + q;
-              const uint4 v = *reinterpret_cast<const uint4*>(rp + ((chunk ^ g) << 4));
-              w[t][h][0] = v.x;
-              w[t][h][1] = v.y;
-              w[t][h][2] = v.z;
-              w[t][h][3] = v.w;
-            } else {
-              const uint4 v0 = *reinterpret_cast<const uint4*>(rp + (((2 * q) ^ g) << 4));
-              const uint4 v1 = *reinterpret_cast<const uint4*>(rp + (((2 * q + 1) ^ g) << 4));
-              w[t][h][0] = v0.x;
-              w[t][h][1] = v0.y;
-              w[t][h][2] = v0.z;
-              w[t][h][3] = v0.w;
-              w[t][h][4] = v1.x;
-              w[t][h][5] = v1.y;
-              w[t][h][6] = v1.z;
-              w[t][h][7] = v1.w;
-            }
-            if constexpr (D::kScaled) {
-              // prepared table: NF4 absmax (fp32) or (scale, zero) fp16 pair
-              const uint32_t wv = scl[s * (D::kScaleSlot / 4) + ((j * 64) / p.group) * kDecRows + row];
-              if constexpr (kScheme == kNF4) {
-                e[t][h] = make_uint2(wv, 0);
+            for (int h = 0; h < 2; ++h) {
+              const int row = rg * 64 + i * 16 + h * 8 + g;
+              const uint8_t* rp = stage + row * kBoxBytes;
+              if constexpr (kWords == 2) {
+                const int off = j * D::kQuadBytes + 8 * q;
+                const uint2 v = *reinterpret_cast<const uint2*>(
+                    rp + ((((off >> 4) ^ g) << 4) | (off & 15)));
+                w[i][h][0] = v.x;
+                w[i][h][1] = v.y;
+              } else if constexpr (kWords == 4) {
+                const int chunk = (j * D::kQuadBytes >> 4) + q;
+                const uint4 v = *reinterpret_cast<const uint4*>(rp + ((chunk ^ g) << 4));
+                w[i][h][0] = v.x;
+                w[i][h][1] = v.y;
+                w[i][h][2] = v.z;
+                w[i][h][3] = v.w;
               } else {
-                const __half2 sz = *reinterpret_cast<const __half2*>(&wv);
-                const float zf = __high2float(sz);
-                e[t][h].x = __float_as_uint(__low2float(sz));
-                e[t][h].y = kScheme == kINT4 ? pack2<__nv_bfloat16>(128.f + zf, 128.f + zf)  // exact
-                                             : __float_as_uint(8388608.f + zf);              // exact
+                const uint4 v0 = *reinterpret_cast<const uint4*>(rp + (((2 * q) ^ g) << 4));
+                const uint4 v1 = *reinterpret_cast<const uint4*>(rp + (((2 * q + 1) ^ g) << 4));
+                w[i][h][0] = v0.x;
+                w[i][h][1] = v0.y;
+                w[i][h][2] = v0.z;
+                w[i][h][3] = v0.w;
+                w[i][h][4] = v1.x;
+                w[i][h][5] = v1.y;
+                w[i][h][6] = v1.z;
+                w[i][h][7] = v1.w;
               }
-            } else {
-              e[t][h] = make_uint2(0, 0);
+              if constexpr (D::kScaled) {
+                // prepared table: NF4 absmax (fp32) or (scale, zero) fp16 pair
+                const uint32_t wv = scl[((j * 64) / p.group) * kDecRows + row];
+                if constexpr (kScheme == kNF4) {
+                  e[i][h] = make_uint2(wv, 0);
+                } else {
+                  const __half2 sz = *reinterpret_cast<const __half2*>(&wv);
+                  const float zf = __high2float(sz);
+                  e[i][h].x = __float_as_uint(__low2float(sz));
+                  e[i][h].y = kScheme == kINT4 ? pack2<__nv_bfloat16>(128.f + zf, 128.f + zf)  // exact
+                                               : __float_as_uint(8388608.f + zf);              // exact
+                }
+              } else {
+                e[i][h] = make_uint2(0, 0);
+              }
             }
           }
-        }
-        float tmp[2][kNT][4];
+          float tmp[kTiles][kNT][4];
 #pragma unroll
-        for (int t = 0; t < 2; ++t)
+          for (int i = 0; i < kTiles; ++i)
 #pragma unroll
-          for (int nt = 0; nt < kNT; ++nt)
+            for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tmp[t][nt][c] = 0.f;
+              for (int c = 0; c < 4; ++c) tmp[i][nt][c] = 0.f;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          uint2 xb[kNT];
-          const int kk = sl * D::kStageK + j * 64 + 16 * q + 4 * b;  // k within the item
-#pragma unroll
-          for (int nt = 0; nt < kNT; ++nt)
-            xb[nt] = (nt * 8 + g < p.M)
-                         ? *reinterpret_cast<const uint2*>(xs + (nt * 8 + g) * xstride + kk)
-                         : make_uint2(0, 0);
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            uint32_t a[4];
-            a_frags<kScheme, kWords>(w[t][0], w[t][1], e[t][0].y, e[t][1].y, b, lut_lane, a);
+          for (int b = 0; b < 4; ++b) {
+            const int bb = b ^ fq;
+            const bool odd = (bb & 1) != 0;
+            uint2 xb[kNT];
 #pragma unroll
             for (int nt = 0; nt < kNT; ++nt) {
-              if constexpr (D::kScaled)
-                mma16816(tmp[t][nt], a, xb[nt].x, xb[nt].y);
-              else
-                mma16816(acc[t][nt], a, xb[nt].x, xb[nt].y);
+              // token row nt*8 + g of quad j's x box: 8 bytes at k 16q + 4bb
+              const uint8_t* xr = xst + (j * p.x_rows + nt * 8 + g) * 128;
+              const int chunk = 2 * q + (bb >> 1);
+              uint2 v = *reinterpret_cast<const uint2*>(xr + ((chunk ^ g) << 4) + 8 * (bb & 1));
+              if constexpr (kScheme == kINT4)  // (k, k+2) and (k+1, k+3)
+                v = make_uint2(__byte_perm(v.x, v.y, 0x5410), __byte_perm(v.x, v.y, 0x7632));
+              xb[nt] = v;
+            }
+#pragma unroll
+            for (int i = 0; i < kTiles; ++i) {
+              uint32_t a[4];
+              a_frags<kScheme, kWords>(w[i][0], w[i][1], e[i][0].y, e[i][1].y, b, odd, lut_lane,
+                                       a);
+#pragma unroll
+              for (int nt = 0; nt < kNT; ++nt) {
+                if constexpr (D::kScaled)
+                  mma16816(tmp[i][nt], a, xb[nt].x, xb[nt].y);
+                else
+                  mma16816(acc[i][nt], a, xb[nt].x, xb[nt].y);
+              }
             }
           }
-        }
-        if constexpr (D::kScaled) {
+          if constexpr (D::kScaled) {
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const float s0 = __uint_as_float(e[t][0].x), s1 = __uint_as_float(e[t][1].x);
+            for (int i = 0; i < kTiles; ++i) {
+              const float sc0 = __uint_as_float(e[i][0].x), sc1 = __uint_as_float(e[i][1].x);
 #pragma unroll
-            for (int nt = 0; nt < kNT; ++nt) {
-              acc[t][nt][0] = fmaf(s0, tmp[t][nt][0], acc[t][nt][0]);
-              acc[t][nt][1] = fmaf(s0, tmp[t][nt][1], acc[t][nt][1]);
-              acc[t][nt][2] = fmaf(s1, tmp[t][nt][2], acc[t][nt][2]);
-              acc[t][nt][3] = fmaf(s1, tmp[t][nt][3], acc[t][nt][3]);
+              for (int nt = 0; nt < kNT; ++nt) {
+                acc[i][nt][0] = fmaf(sc0, tmp[i][nt][0], acc[i][nt][0]);
+                acc[i][nt][1] = fmaf(sc0, tmp[i][nt][1], acc[i][nt][1]);
+                acc[i][nt][2] = fmaf(sc1, tmp[i][nt][2], acc[i][nt][2]);
+                acc[i][nt][3] = fmaf(sc1, tmp[i][nt][3], acc[i][nt][3]);
+              }
             }
           }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[s]);
+      if (lane == 0) mbar_arrive(&empty_bar[slot]);
+      if (++slot == p.stages) {
+        slot = 0;
+        phase ^= 1;
+      }
     }
 
-    if constexpr (D::kKS > 1) {
-      // k parts 1.. hand their sums to part 0, which adds them in part order
-      float* mine = red + ((kp - 1) * kRowGroups + rg) * 32 * 16 + lane * 16;
-      if (kp > 0) {
+    // k-groups 1..3 hand their sums to k-group 0, which adds them in order
+    if (kg > 0) {
 #pragma unroll
-        for (int t = 0; t < 2; ++t)
+      for (int i = 0; i < kTiles; ++i)
+#pragma unroll
+        for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            red[((((kg - 1) * kRowGroups + rg) * kTiles + i) * kNT + nt) * 128 + c * 32 + lane] =
+                acc[i][nt][c];
+    }
+    named_bar_sync(1, kAll);
+    if (kg == 0) {
+#pragma unroll
+      for (int k2 = 1; k2 < kKG; ++k2)
+#pragma unroll
+        for (int i = 0; i < kTiles; ++i)
 #pragma unroll
           for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) mine[(t * kNT + nt) * 4 + c] = acc[t][nt][c];
-      }
-      named_bar_sync(1, kAll);
-      if (kp > 0) continue;
-#pragma unroll
-      for (int k2 = 1; k2 < D::kKS; ++k2) {
-        const float* theirs = red + ((k2 - 1) * kRowGroups + rg) * 32 * 16 + lane * 16;
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-          for (int nt = 0; nt < kNT; ++nt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[t][nt][c] += theirs[(t * kNT + nt) * 4 + c];
-      }
+            for (int c = 0; c < 4; ++c)
+              acc[i][nt][c] +=
+                  red[((((k2 - 1) * kRowGroups + rg) * kTiles + i) * kNT + nt) * 128 + c * 32 + lane];
     }
-    // from here on k part 0 only (kLead threads, named barrier 2)
+    named_bar_sync(1, kAll);  // the sums are read: k-groups 1..3 may go on
+    if (kg != 0) continue;
 
-    if (p.splits == 1) {
-      // whole k range in this item: fragments + the rank warp's per-row rank
-      // term go straight to y (rows g, g+8; tokens 2q, 2q+1)
-      const bool have_rt = mbar_wait(&rt_full, items_done & 1, p.status, kDevTimeoutFull);
-      ++items_done;
+    // C fragment: rows (g, g+8) of each tile = output rows; columns (2q, 2q+1)
+    // of each 8-token tile = tokens
+    if (kind == 1) {
+      float* part = p.partials + static_cast<long long>(cta) * p.M * kDecRows;
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
+      for (int i = 0; i < kTiles; ++i)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int row = rg * 32 + t * 16 + h * 8 + g;
-          const int n = rb * kDecRows + row;
-          if (n >= p.N) continue;
+          const int row = rg * 64 + i * 16 + h * 8 + g;
 #pragma unroll
-          for (int nt = 0; nt < kNT; ++nt) {
-            const int m0 = nt * 8 + 2 * q;
-            if (m0 >= p.M) continue;
-            const float r0 = have_rt ? rt[m0 * kDecRows + row] : 0.f;
-            p.y[static_cast<long long>(m0) * p.ldy + n] = __float2bfloat16_rn(acc[t][nt][2 * h] + r0);
-            if (m0 + 1 < p.M) {
-              const float r1 = have_rt ? rt[(m0 + 1) * kDecRows + row] : 0.f;
-              p.y[static_cast<long long>(m0 + 1) * p.ldy + n] =
-                  __float2bfloat16_rn(acc[t][nt][2 * h + 1] + r1);
+          for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int m = nt * 8 + 2 * q + c;
+              if (m < p.M) __stcg(part + m * kDecRows + row, acc[i][nt][2 * h + c]);
             }
-          }
         }
-      }
+      __threadfence();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&rt_empty);
+      if (lane == 0) mbar_arrive(&pub_done);
       continue;
     }
-
-    // partial tile: C rows = output rows (g, g+8), columns = tokens (2q, 2q+1)
-    float* part = p.partials + static_cast<long long>(split) * p.M * p.N;
+    // whole: the rank term from rt (cycled with the rank warp); finish: the
+    // earlier CTAs' partials and the rank term from their own buffers
+    const bool have = kind == 2 ? mbar_wait(&fin_ready, 0, p.status, kDevTimeoutFull)
+                                : mbar_wait(&rt_full, writes & 1, p.status, kDevTimeoutFull);
+    if (kind == 0) ++writes;
+    const float* rterm = kind == 2 ? rtf : rt;
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int i = 0; i < kTiles; ++i)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int n = rb * kDecRows + rg * 32 + t * 16 + h * 8 + g;
+        const int row = rg * 64 + i * 16 + h * 8 + g;
+        const int n = rb * kDecRows + row;
+        if (n >= p.N) continue;
 #pragma unroll
-        for (int nt = 0; nt < kNT; ++nt) {
+        for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int m = nt * 8 + 2 * q + c;
-            if (m < p.M && n < p.N)
-              __stcg(part + static_cast<long long>(m) * p.N + n, acc[t][nt][2 * h + c]);
+            if (m >= p.M) continue;
+            float v = acc[i][nt][2 * h + c];
+            if (kind == 2 && have) v = psum[m * kDecRows + row] + v;
+            if (p.rt != nullptr && have) v += rterm[m * kDecRows + row];
+            p.y[static_cast<long long>(m) * p.ldy + n] = __float2bfloat16_rn(v);
           }
-        }
       }
-    }
-    __threadfence();
-    named_bar_sync(2, kLead);
-    if (ct == 0) {
-      // counters are zeroed by the programmatic primary (or a memset before it)
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      const uint32_t ticket = atomicAdd(&p.counters[rb], 1u);
-      last_flag = ticket == static_cast<uint32_t>(p.splits - 1) ? 1u : 0u;
-      if (last_flag) p.counters[rb] = 0;
-    }
-    named_bar_sync(2, kLead);
-    if (last_flag == 0) continue;
-    __threadfence();
-    mbar_wait(&st_bar, 0, p.status, kDevTimeoutFull);  // sT folded by the rank warp
-    // last CTA of this row block: one thread per output row sums the splits
-    // in order and adds the rank term
-    const int n = rb * kDecRows + ct;
-    if (n < p.N) {
-      float out[kMaxTok];
-#pragma unroll
-      for (int m = 0; m < kMaxTok; ++m) {
-        out[m] = 0.f;
-        if (m < p.M) {
-          for (int s0 = 0; s0 < p.splits; s0 += 8) {  // loads in flight together
-            float t8[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              t8[u] = s0 + u < p.splits
-                          ? __ldcg(p.partials + (static_cast<long long>(s0 + u) * p.M + m) * p.N + n)
-                          : 0.f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) out[m] += t8[u];
-          }
-        }
-      }
-      if (p.b != nullptr) add_rank_term(p.b + static_cast<long long>(n) * p.r, sts, p.M, p.r, out);
-#pragma unroll
-      for (int m = 0; m < kMaxTok; ++m)
-        if (m < p.M) p.y[static_cast<long long>(m) * p.ldy + n] = __float2bfloat16_rn(out[m]);
-    }
+    __syncwarp();
+    if (lane == 0 && kind == 0) mbar_arrive(&rt_empty);
   }
 }
 
 // Partial sums of sT[m, j] = scale * sum_k x[m, k] A[j, k] for m < M <= 16:
-// CTA (j, s) covers the s-th k slice; thread t takes 8-wide chunks t, t + 256,
-// ... and loads the A chunk and every token's chunk at once (one round of
-// memory latency for slices up to 2048), then the CTA reduces in a fixed
-// order.  It signals its dependent grid (the decode kernel) at once so that
-// grid streams weights meanwhile; the decode kernel adds the slices in order.
-__global__ void __launch_bounds__(256) lora_rank_small_kernel(
+// CTA (j, s) covers the s-th k slice (512 k); thread t takes the 8-wide chunk
+// t and loads the A chunk and every token's chunk at once (one round of
+// memory latency), then the CTA reduces in a fixed order.  It signals its
+// dependent grids (the rank-term kernel, then the decode kernel) at once so
+// they start meanwhile; the rank-term kernel adds the slices in order.
+__global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ a, int M, int K, int r,
     int kslice, float scale, float* __restrict__ st, uint32_t* __restrict__ counters,
     int n_counters) {
@@ -620,14 +740,14 @@ __global__ void __launch_bounds__(256) lora_rank_small_kernel(
   // first ticket, so zeroing here needs no separate memset)
   if (blockIdx.x == 0 && blockIdx.y == 0)
     for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
-  __shared__ float red[8][kMaxTok];
+  __shared__ float red[kRankThreads / 32][kMaxTok];
   const int j = blockIdx.x, split = blockIdx.y;
   const int k0 = split * kslice, k1 = min(K, k0 + kslice);
   float acc[kMaxTok];
 #pragma unroll
   for (int m = 0; m < kMaxTok; ++m) acc[m] = 0.f;
   const __nv_bfloat16* ar = a + static_cast<long long>(j) * K;
-  for (int k = k0 + threadIdx.x * 8; k < k1; k += 256 * 8) {
+  for (int k = k0 + threadIdx.x * 8; k < k1; k += kRankThreads * 8) {
     const uint4 av = __ldg(reinterpret_cast<const uint4*>(ar + k));
     uint4 xv[kMaxTok];
 #pragma unroll
@@ -662,45 +782,93 @@ __global__ void __launch_bounds__(256) lora_rank_small_kernel(
   if (threadIdx.x < M) {
     float v = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v += red[i][threadIdx.x];
+    for (int i = 0; i < kRankThreads / 32; ++i) v += red[i][threadIdx.x];
     st[(static_cast<long long>(split) * M + threadIdx.x) * r + j] = v * scale;
   }
 }
 
-int bits_of(int scheme) { return scheme == 0 ? 16 : (scheme == kINT8 ? 8 : 4); }
-int stage_k_of(int scheme) { return kBoxBytes * 8 / bits_of(scheme); }
 
-// Shared memory of one CTA: fixed regions, sT [16, r], tokens [M, kspan + 4].
-template <int kScheme>
-size_t smem_bytes_t(int64_t M, int64_t r, int64_t kspan) {
-  using D = Dec<kScheme>;
-  return 1024 + static_cast<size_t>(D::kStages) * kStageBytes + D::kScaleBytes + D::kLutBytes +
-         D::kRedBytes + static_cast<size_t>(kMaxTok) * kDecRows * 4 +
-         static_cast<size_t>((kMaxTok * (r > 0 ? r : 1) + 3) & ~3) * 4 +
-         static_cast<size_t>(M * (kspan + 4) * 2 + 15) / 16 * 16;
+// The decode path's rank term rt[m, n] = sum_j B[n, j] sT[m, j] for every row
+// n of the weight, sT the fold (in split order) of the rank kernel's
+// partials.  A programmatic dependent of that kernel (waits for it before
+// reading sT) and the primary of the decode kernel, which reads rt only in
+// its rank warp after its own griddepcontrol.wait; both launch at once, so
+// this pass over B (N x r bf16) overlaps the decode kernel's weight stream.
+__global__ void __launch_bounds__(kRankThreads) lora_rank_up_kernel(const float* __restrict__ st,
+                                                           int st_splits,
+                                                           const __nv_bfloat16* __restrict__ b,
+                                                           int M, int N, int r,
+                                                           float* __restrict__ rt) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  extern __shared__ float sts[];  // [M, r]
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int i = threadIdx.x; i < M * r; i += blockDim.x) {
+    float v = 0.f;
+    for (int s0 = 0; s0 < st_splits; ++s0) v += __ldcg(st + static_cast<long long>(s0) * M * r + i);
+    sts[i] = v;
+  }
+  __syncthreads();
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float out[kMaxTok];
+#pragma unroll
+  for (int m = 0; m < kMaxTok; ++m) out[m] = 0.f;
+  add_rank_term(b + static_cast<long long>(n) * r, sts, M, r, out);
+#pragma unroll
+  for (int m = 0; m < kMaxTok; ++m)
+    if (m < M) rt[static_cast<long long>(m) * N + n] = out[m];
 }
 
-size_t smem_bytes(int scheme, int64_t M, int64_t r, int64_t kspan) {
-  switch (scheme) {
-    case 0: return smem_bytes_t<0>(M, r, kspan);
-    case kNF4: return smem_bytes_t<kNF4>(M, r, kspan);
-    case kINT4: return smem_bytes_t<kINT4>(M, r, kspan);
-    default: return smem_bytes_t<kINT8>(M, r, kspan);
-  }
+int bits_of(int scheme) { return scheme == 0 ? 16 : (scheme == kINT8 ? 8 : 4); }
+int stage_k_of(int scheme) { return kBoxBytes * 8 / bits_of(scheme); }
+int quads_of(int scheme) { return stage_k_of(scheme) / 64; }
+int x_rows_of(int64_t M) { return M <= 8 ? 8 : 16; }
+int gps_of(int scheme, int64_t group) {
+  return scheme == 0 ? 1 : static_cast<int>(std::max<int64_t>(1, stage_k_of(scheme) / group));
+}
+
+// Shared-memory layout of one CTA (offsets from the 1024-byte aligned base).
+struct DecLayout {
+  int x_slot, scale_slot;
+  int off_x, off_scale, off_lut, off_red, off_rt, off_psum, off_rtf;
+  int bytes;  // including the alignment slack
+};
+
+DecLayout dec_layout(int scheme, int64_t M, int64_t group, int stages) {
+  DecLayout L;
+  const int xr = x_rows_of(M), kNT = xr / 8;
+  L.x_slot = quads_of(scheme) * xr * 128;
+  L.scale_slot = scheme == 0 ? 0 : gps_of(scheme, group) * kDecRows * 4;
+  L.off_x = stages * kStageBytes;
+  L.off_scale = L.off_x + stages * L.x_slot;
+  L.off_lut = L.off_scale + stages * L.scale_slot;
+  const int lut = scheme == kNF4 ? 256 * 32 * 4 : 0;
+  L.off_red = L.off_lut + lut;
+  const int red = (kKG - 1) * kRowGroups * kTiles * kNT * 128 * 4;
+  L.off_rt = L.off_red + red;
+  const int tok = static_cast<int>(M) * kDecRows * 4;
+  L.off_psum = L.off_rt + tok;
+  L.off_rtf = L.off_psum + tok;
+  L.bytes = 1024 + L.off_rtf + tok;
+  return L;
 }
 
 template <int kScheme, int kNT>
 int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t s) {
   using D = Dec<kScheme>;
   const int64_t row_bytes = a.K * D::kBits / 8;
-  CUtensorMap map;
-  if (!make_tmap_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, static_cast<uint64_t>(row_bytes),
+  CUtensorMap wmap, xmap;
+  if (!make_tmap_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, static_cast<uint64_t>(row_bytes),
                     static_cast<uint64_t>(a.N), static_cast<uint64_t>(row_bytes), kBoxBytes,
                     kDecRows, true))
     return MLORA_ERR_CUDA;
+  const int xr = x_rows_of(a.M);
+  if (!make_tmap_2d_16b(&xmap, a.x, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M),
+                        static_cast<uint64_t>(a.K), 64, static_cast<uint32_t>(xr)))
+    return MLORA_ERR_CUDA;
   const int64_t group = a.group > 0 ? a.group : 64;
-  const int gps = static_cast<int>(std::max<int64_t>(1, D::kStageK / group));
-  CUtensorMap smap = map;
+  const int gps = gps_of(kScheme, group);
+  CUtensorMap smap = wmap;
   if constexpr (D::kScaled) {
     if (a.scales_t == nullptr) {
       set_error("decode: quantised weight without its prepared scale table");
@@ -713,46 +881,53 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
                       static_cast<uint32_t>(gps), false))
       return MLORA_ERR_CUDA;
   }
+  const DecLayout L = dec_layout(kScheme, a.M, group, cfg.stages);
   DecParams p;
-  p.x = static_cast<const __nv_bfloat16*>(a.x);
-  p.b = static_cast<const __nv_bfloat16*>(a.b);
-  p.st = a.st;
-  p.st_splits = a.b != nullptr ? rank_small_splits(a.K) : 0;
+  p.rt = a.rt;
   p.y = static_cast<__nv_bfloat16*>(a.y);
+  p.ldy = a.ldy > 0 ? a.ldy : a.N;
   p.partials = a.partials;
-  p.counters = a.counters;
+  p.flags = a.flags;
   p.M = static_cast<int>(a.M);
   p.N = static_cast<int>(a.N);
   p.K = static_cast<int>(a.K);
-  p.r = static_cast<int>(a.r);
   p.group = static_cast<int>(group);
   p.gps = gps;
-  p.splits = cfg.splits;
-  p.kspan = cfg.kspan;
-  p.row_blocks = static_cast<int>(gemv_row_blocks(a.N));
-  p.items = p.row_blocks * cfg.splits;
-  p.ldy = a.ldy > 0 ? a.ldy : a.N;
+  p.S = static_cast<int>((a.K + D::kStageK - 1) / D::kStageK);
+  p.units = static_cast<long long>(gemv_row_blocks(a.N)) * p.S;
+  p.stages = cfg.stages;
+  p.x_rows = xr;
+  p.x_slot = L.x_slot;
+  p.scale_slot = L.scale_slot;
+  p.off_x = L.off_x;
+  p.off_scale = L.off_scale;
+  p.off_lut = L.off_lut;
+  p.off_red = L.off_red;
+  p.off_rt = L.off_rt;
+  p.off_psum = L.off_psum;
+  p.off_rtf = L.off_rtf;
   p.status = device_status_ptr();
-  const size_t smem = static_cast<size_t>(cfg.smem);
   auto kern = lora_decode_kernel<kScheme, kNT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+                                       static_cast<int>(cfg.smem));
   if (e != cudaSuccess) {
     set_error(std::string("decode attribute: ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
   }
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(cfg.ctas));
-  lc.blockDim = dim3(D::kThreads);
-  lc.dynamicSmemBytes = smem;
+  lc.blockDim = dim3(kDecThreads);
+  lc.dynamicSmemBytes = static_cast<size_t>(cfg.smem);
   lc.stream = s;
+  // a programmatic dependent of the rank kernels that precede it (which
+  // write nothing this kernel reads before griddepcontrol.wait)
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = 1;
+  lc.numAttrs = a.rt != nullptr ? 1 : 0;
   LaunchScope scope(kKindGemv, s);
-  e = cudaLaunchKernelEx(&lc, kern, map, smap, p);
+  e = cudaLaunchKernelEx(&lc, kern, wmap, smap, xmap, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("decode launch: ") + cudaGetErrorString(e));
@@ -771,43 +946,23 @@ int launch_decode_scheme(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_
 
 int64_t gemv_row_blocks(int64_t N) { return (N + kDecRows - 1) / kDecRows; }
 
-DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r) {
+DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r, int64_t group) {
   const int sk = stage_k_of(scheme);
-  const int64_t total = (K + sk - 1) / sk;  // stages over K
-  const int64_t rb = gemv_row_blocks(N);
-  const int sms = num_sms();
-  const size_t fixed = smem_bytes(scheme, M, r, 0);  // everything but the token slice's k
-  DecodeConfig best{1, static_cast<int>(total * sk), 1, static_cast<int>(fixed)};
-  double best_cost = 1e30;
-  for (int per_sm = 2; per_sm >= 1; --per_sm) {  // CTAs per SM (shared memory decides)
-    const int64_t cap = std::min<int64_t>(227 * 1024, kSmemPerSm / per_sm - 1024);
-    if (static_cast<int64_t>(fixed) + M * sk * 2 > cap) continue;
-    const int64_t kspan_max = ((cap - static_cast<int64_t>(fixed)) / (M * 2) / sk) * sk;
-    const int64_t slots = static_cast<int64_t>(sms) * per_sm;
-    for (int64_t per = 1; per <= total; ++per) {  // stages per split
-      if (per * sk > kspan_max) break;
-      const int64_t splits = (total + per - 1) / per;
-      if (splits > 64) continue;
-      const int64_t items = rb * splits;
-      const int64_t ctas = items < slots ? items : slots;
-      const int64_t rounds = (items + ctas - 1) / ctas;
-      // Time in units of one stage of one CTA: the per-item fixed latency
-      // (token staging, first TMA, epilogue; larger with split partials), a
-      // stretch when few SMs stream, the split partials' traffic in stages
-      const double active = static_cast<double>(ctas < sms ? ctas : sms);
-      const double stretch = std::max(1.0, 0.55 * sms / active);
-      const double fixed_t = splits == 1 ? 6.0 : 12.0;
-      const double part = 2.0 * splits * M * N * 4 / (kStageBytes * static_cast<double>(ctas));
-      const double cost = rounds * (per * stretch + fixed_t) + part;
-      if (cost < best_cost) {
-        best_cost = cost;
-        best = DecodeConfig{static_cast<int>(splits), static_cast<int>(per * sk),
-                            static_cast<int>(ctas),
-                            static_cast<int>(smem_bytes(scheme, M, r, per * sk))};
-      }
-    }
-  }
-  return best;
+  const int64_t S = (K + sk - 1) / sk;
+  const int64_t units = gemv_row_blocks(N) * S;
+  const int64_t ctas = std::min<int64_t>(num_sms(), units);
+  const int64_t g = group > 0 ? group : 64;
+  int stages = kMaxStages;
+  while (stages > 2 && dec_layout(scheme, M, g, stages).bytes > kSmemMax) --stages;
+  DecodeConfig c;
+  c.ctas = static_cast<int>(ctas);
+  c.stages = stages;
+  c.smem = dec_layout(scheme, M, g, stages).bytes;
+  // some row block is shared between CTAs (then partials and flags are used)
+  c.split_blocks = false;
+  for (int64_t j = 1; j < ctas && !c.split_blocks; ++j)
+    if ((units * j / ctas) % S != 0) c.split_blocks = true;
+  return c;
 }
 
 int launch_gemv(const GemvArgs& a, cudaStream_t s) {
@@ -815,9 +970,13 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
     set_error("decode path takes at most 16 tokens");
     return MLORA_ERR_UNSUPPORTED;
   }
-  const DecodeConfig cfg = decode_config(a.scheme, a.M, a.N, a.K, a.r);
-  if (cfg.splits != a.splits) {
-    set_error("decode: workspace planned for a different split count");
+  const DecodeConfig cfg = decode_config(a.scheme, a.M, a.N, a.K, a.r, a.group);
+  if (cfg.smem > kSmemMax) {
+    set_error("decode: shared memory for rank " + std::to_string(a.r) + " exceeds the limit");
+    return MLORA_ERR_UNSUPPORTED;
+  }
+  if (cfg.split_blocks && (a.flags == nullptr || a.partials == nullptr)) {
+    set_error("decode: workspace without partials and flags for a split row block");
     return MLORA_ERR_INVALID_ARG;
   }
   switch (a.scheme) {
@@ -829,9 +988,45 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   }
 }
 
+int launch_rank_up(const float* st, int64_t K, const void* b, int64_t M, int64_t N, int64_t r,
+                   float* rt, cudaStream_t s) {
+  // same shared-memory carveout as the decode kernel beside it (a hint, set
+  // once per device)
+  static std::atomic<bool> carve_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !carve_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(lora_rank_up_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+      cudaGetLastError();  // a hint only: clear the error, launch without it
+    else if (dev < 64)
+      carve_set[dev].store(true, std::memory_order_release);
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>((N + kRankThreads - 1) / kRankThreads));
+  lc.blockDim = dim3(kRankThreads);
+  lc.dynamicSmemBytes = static_cast<size_t>(M * r * 4);
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  LaunchScope scope(kKindGemv, s);
+  cudaError_t e = cudaLaunchKernelEx(&lc, lora_rank_up_kernel, st, rank_small_splits(K),
+                                     static_cast<const __nv_bfloat16*>(b), static_cast<int>(M),
+                                     static_cast<int>(N), static_cast<int>(r), rt);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("rank_up launch: ") + cudaGetErrorString(e));
+    return MLORA_ERR_CUDA;
+  }
+  return MLORA_OK;
+}
+
 int rank_small_splits(int64_t K) {
-  const int64_t s = (K + 2047) / 2048;  // ~2048 k per CTA
-  return static_cast<int>(s < 1 ? 1 : (s > 16 ? 16 : s));
+  const int64_t s = (K + 511) / 512;  // ~512 k per CTA: one 8-wide chunk per thread
+  return static_cast<int>(s < 1 ? 1 : (s > 32 ? 32 : s));
 }
 
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
@@ -852,7 +1047,7 @@ int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_
   LaunchScope scope(kKindGemv, s);
   const int splits = rank_small_splits(K);
   const int64_t kslice = ((K + splits - 1) / splits + 7) / 8 * 8;
-  lora_rank_small_kernel<<<dim3(static_cast<unsigned>(r), static_cast<unsigned>(splits)), 256, 0,
+  lora_rank_small_kernel<<<dim3(static_cast<unsigned>(r), static_cast<unsigned>(splits)), kRankThreads, 0,
                            s>>>(static_cast<const __nv_bfloat16*>(x),
                                 static_cast<const __nv_bfloat16*>(a), static_cast<int>(M),
                                 static_cast<int>(K), static_cast<int>(r),

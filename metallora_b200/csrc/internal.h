@@ -115,29 +115,34 @@ struct GemvArgs {
   const void* x = nullptr;         // bf16 [M, K]
   const void* w = nullptr;         // codes or bf16 weights, rows of the [N, K] weight
   const void* scales_t = nullptr;  // prepared scale table [G, prepared_ld(N)] (quantised)
-  const void* b = nullptr;       // bf16 [N, r] or nullptr
-  const float* st = nullptr;     // fp32 [rank_small_splits(K), M, r] partials of s.x.A^T
+  const float* rt = nullptr;     // fp32 [M, N] rank term s.(x.A^T).B^T, or nullptr
   void* y = nullptr;             // bf16 [M, N]
-  float* partials = nullptr;     // [splits, M, N]
-  uint32_t* counters = nullptr;  // [gemv_row_blocks(N)] zeroed
+  float* partials = nullptr;     // [ctas, M, 128]: one partial row block per CTA
+  uint32_t* flags = nullptr;     // [ctas] zeroed (partial published)
   int64_t M = 0, N = 0, K = 0, r = 0, group = 64;
   int64_t ldy = 0;  // row stride of y (0: N)
-  int splits = 1;
 };
 constexpr int64_t kGemvMaxTokens = 16;
-// Decode launch shape: k-splits per 128-row block, k per split, persistent CTAs.
+// Decode launch shape: persistent CTAs (one per SM at most) over the stream-K
+// unit range, ring depth, shared memory; split_blocks: some 128-row block is
+// shared between CTAs (partials and flags needed).
 struct DecodeConfig {
-  int splits;
-  int kspan;
   int ctas;
+  int stages;
   int smem;  // dynamic shared memory per CTA (bytes)
+  bool split_blocks;
 };
-DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r);
+DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t r, int64_t group);
 int64_t gemv_row_blocks(int64_t N);
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 int rank_small_splits(int64_t K);
+// The decode path's rank term rt [M, N] from the sT partials of
+// launch_rank_small (a programmatic dependent of it; the decode kernel is one
+// of this).
+int launch_rank_up(const float* st, int64_t K, const void* b, int64_t M, int64_t N, int64_t r,
+                   float* rt, cudaStream_t s);
 // sT partials for the decode path; also zeroes the decode kernel's n_counters
-// split counters.
+// partial flags.
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
                       float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s);
 

@@ -39,6 +39,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Rounds the dynamic shared-memory base up to kAlign bytes by pointer
+// arithmetic on the shared array itself, so the result stays a shared-space
+// pointer and accesses through it compile to ld/st.shared (a pointer rebuilt
+// from an integer becomes a generic pointer).
+template <uint32_t kAlign>
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* p) {
+  const uint32_t a = smem_u32(p);
+  return p + ((kAlign - (a & (kAlign - 1u))) & (kAlign - 1u));
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -389,6 +399,12 @@ __device__ __forceinline__ bool elect_one() {
 // Named barrier among `nthreads` threads (multiple of 32) using id `id` (1..15).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Arrives on a named barrier without waiting for it (the other participants
+// wait with named_bar_sync).
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 template <typename T>

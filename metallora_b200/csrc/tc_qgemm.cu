@@ -146,8 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_scales, const QGemmParams p) {
   using Tr = QTraits<kScheme>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint8_t* xs = smem;
   uint8_t* ws = xs + kStagesX * kXTileBytes;
   uint8_t* rs = ws + kStagesW * kWTileBytes;

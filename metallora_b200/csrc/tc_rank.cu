@@ -231,8 +231,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
   constexpr int S = num_stages(R);
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * stage_bytes(R));
   uint64_t* empty_bar = full_bar + S;
   uint64_t* done_bar = empty_bar + S;
@@ -365,8 +364,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                  const WgradParams p) {
   constexpr int S = num_stages(R);
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * stage_bytes(R));
   uint64_t* empty_bar = full_bar + S;
   uint64_t* done_bar = empty_bar + S;
