@@ -258,7 +258,6 @@ struct GemvPlan {
   uint32_t* flags;
   size_t flag_bytes;
   float* st;
-  float* rt;
   float* partials;
   size_t bytes;
 };
@@ -278,7 +277,6 @@ GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int sch
   p.flags = p.split ? static_cast<uint32_t*>(c.take(p.flag_bytes)) : nullptr;
   p.st = static_cast<float*>(
       c.take(static_cast<size_t>(rank_small_splits(K)) * M * (r > 0 ? r : 1) * 4));
-  p.rt = r > 0 ? static_cast<float*>(c.take(static_cast<size_t>(M) * N * 4)) : nullptr;
   p.partials = p.split ? static_cast<float*>(c.take(static_cast<size_t>(p.ctas) * M * 128 * 4))
                        : nullptr;
   p.bytes = align_up(c.off, 256);
@@ -286,8 +284,7 @@ GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int sch
 }
 
 // Decode-size forward: sT = s.x.A^T (if a) with the partial flags zeroed,
-// the rank term sT.B^T, then the stream-K GEMV adding it (the three launch
-// as a programmatic-dependent chain).
+// then the stream-K GEMV with the rank term (a programmatic dependent).
 int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
              int64_t group, const void* a, const void* b, void* y, int64_t M, int64_t K,
              int64_t N, int64_t r, float alpha, void* workspace, size_t workspace_bytes,
@@ -307,13 +304,13 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
       (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.flags,
                               p.split ? p.ctas : 0, s)))
     return rc;
-  if (a != nullptr && (rc = launch_rank_up(p.st, K, b, M, N, r, p.rt, s))) return rc;
   GemvArgs g;
   g.scheme = scheme;
   g.x = x;
   g.w = w;
   g.scales_t = scales_t;
-  g.rt = a != nullptr ? p.rt : nullptr;
+  g.b = a != nullptr ? b : nullptr;
+  g.st = p.st;
   g.y = y;
   g.partials = p.partials;
   g.flags = p.flags;

@@ -12,7 +12,7 @@
 //   whole    a complete row block: summed here and written to y;
 //   publish  the part of a row block before its end (the range's last
 //            segment): summed here and stored as this CTA's one fp32 partial
-//            [M, 128], then a flag is raised;
+//            [M, 128], then the consumers raise this CTA's flag;
 //   finish   the end of a row block that began in earlier CTAs (the range's
 //            first segment): once their flags are up, their partials are
 //            added in CTA order, then this CTA's own sum, and y is written.
@@ -26,11 +26,12 @@
 //               prepared scale table [groups, rows] (quantised bases) and the
 //               tokens' [x_rows x 64] boxes of x for the stage's k range
 //               (128-byte swizzle; rows past M are zero-filled);
-//   warp 1      waits for the rank kernel (programmatic dependent launch),
-//               folds its sT partials into shared memory, raises this CTA's
-//               partial flag, pre-sums the partials a finish segment needs and
-//               computes the rank term sum_j B[n, j] sT[m, j] of every row
-//               block this CTA writes, while the consumers stream;
+//   warps 1, 10, 11  (rank warps) wait for the rank kernel (programmatic
+//               dependent launch), fold its sT partials into shared memory,
+//               compute the rank term sum_j B[n, j] sT[m, j] of every row block
+//               this CTA writes (mma.m16n8k16, tiles split three ways) while
+//               the consumers stream, and pre-sum the partials a finish
+//               segment needs;
 //   warps 2..9  tensor cores: 2 row groups (64 rows, four 16-row tiles each)
 //               x 4 k-groups (the stage's 64-wide k quads dealt round-robin);
 //               mma.m16n8k16 with the WEIGHTS as the A operand and the tokens
@@ -73,14 +74,10 @@ constexpr int kRowGroups = 2;     // consumer warps per k-group, 64 rows each
 constexpr int kKG = 4;            // k-groups
 constexpr int kTiles = 4;         // 16-row MMA tiles per consumer warp
 constexpr int kConsumers = kRowGroups * kKG;
-constexpr int kDecThreads = 64 + 32 * kConsumers;  // 320
-// Dynamic shared memory of the decode CTA: the SM's 227 KB less the static
-// barriers and 20 KB left for the small rank kernels that run beside it as
-// programmatic dependents/primaries (they then need not wait for an SM).
-constexpr int kSmemMax = 227 * 1024 - 1024 - 20 * 1024;
-// Threads of the rank kernels: few, so that their registers fit beside a
-// decode CTA on the same SM.
-constexpr int kRankThreads = 64;
+constexpr int kRankWarps = 3;     // warp 1 and the two last warps
+constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 384
+constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic; the static barriers take the rest
+constexpr int kRankThreads = 256;            // rank kernel
 constexpr int kMaxStages = 8;
 
 // scheme 0 = dense bf16 weights, else QuantScheme.
@@ -98,18 +95,20 @@ struct Dec {
 };
 
 struct DecParams {
-  const float* rt;         // [M, N] rank term s.(x.A^T).B^T (nullptr: none)
+  const __nv_bfloat16* b;  // [N, r] (nullptr: no rank term)
+  const float* st;         // [st_splits, M, r] partial sums of s.x.A^T
+  int st_splits;
   __nv_bfloat16* y;        // [M, ldy]
   long long ldy;
   float* partials;         // [ctas, M, 128]: one per CTA
   uint32_t* flags;         // [ctas], zeroed before the launch
-  int M, N, K, group, gps;
+  int M, N, K, r, group, gps;
   int S;                   // stages per row block
   long long units;         // row blocks * S
   int stages;              // ring depth
   int x_rows;              // token rows of one x box (8 or 16)
   int x_slot, scale_slot;  // bytes per stage
-  int off_x, off_scale, off_lut, off_red, off_rt, off_psum, off_rtf;  // from the aligned base
+  int off_x, off_scale, off_lut, off_red, off_rt, off_psum, off_rtf, off_sts;  // from the aligned base
   uint32_t* status;
 };
 
@@ -184,36 +183,51 @@ __device__ __forceinline__ void a_frags(const uint32_t (&w0)[kWords], const uint
   }
 }
 
-// out[m] += sum_j B[n, j] sT[m, j] for one row (brow = B + n*r; sts = [M, r]
-// in shared memory); the row's loads go out 8 at a time.
-__device__ __forceinline__ void add_rank_term(const __nv_bfloat16* brow, const float* sts, int M,
-                                              int r, float (&out)[kMaxTok]) {
-  for (int j0 = 0; j0 < r; j0 += 64) {
-    uint4 bv[8];
+// dst[m * 128 + row] = sum_j B[n, j] sT[m, j] for the 16-row tiles
+// tile0, tile0 + tstep, ... of a row block (n = rb * 128 + row; rows past N
+// give 0), on the tensor cores: B's rows are the A operand (fragments loaded
+// from global memory, L2-resident after a prefetch) and sT, rounded to bf16 as
+// the tensor-core paths' saved x.A^T is, the B operand; fp32 accumulation.
+// sts = [M, r] fp32 in shared memory; r is a multiple of 8.
+template <int kNT>
+__device__ __forceinline__ void rank_rows(const __nv_bfloat16* b, const float* sts, int M, int N,
+                                          int r, int rb, int tile0, int tstep, int lane,
+                                          float* dst) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int tile = tile0; tile < kDecRows / 16; tile += tstep) {
+    const int row = tile * 16 + g;
+    const int n0 = rb * kDecRows + row, n1 = n0 + 8;
+    const uint32_t* b0p = reinterpret_cast<const uint32_t*>(b + static_cast<long long>(n0 < N ? n0 : 0) * r);
+    const uint32_t* b1p = reinterpret_cast<const uint32_t*>(b + static_cast<long long>(n1 < N ? n1 : 0) * r);
+    float c[kNT][4];
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
-      bv[u] = j0 + 8 * u < r ? __ldg(reinterpret_cast<const uint4*>(brow + j0 + 8 * u))
-                             : make_uint4(0, 0, 0, 0);
+    for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      if (j0 + 8 * u >= r) break;
-      const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&bv[u]);
-      float bf[8];
+      for (int e = 0; e < 4; ++e) c[nt][e] = 0.f;
+    for (int j0 = 0; j0 < r; j0 += 16) {
+      const int ja = j0 + 2 * q, jb = ja + 8;  // rank pairs (ja, ja+1), (jb, jb+1)
+      uint32_t a[4];
+      a[0] = n0 < N && ja < r ? __ldg(b0p + ja / 2) : 0u;
+      a[1] = n1 < N && ja < r ? __ldg(b1p + ja / 2) : 0u;
+      a[2] = n0 < N && jb < r ? __ldg(b0p + jb / 2) : 0u;
+      a[3] = n1 < N && jb < r ? __ldg(b1p + jb / 2) : 0u;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(bp[i]);
-        bf[2 * i] = f.x;
-        bf[2 * i + 1] = f.y;
-      }
-#pragma unroll
-      for (int m = 0; m < kMaxTok; ++m) {
-        if (m < M) {
-          const float* sm = sts + m * r + j0 + 8 * u;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) out[m] = fmaf(bf[i], sm[i], out[m]);
-        }
+      for (int nt = 0; nt < kNT; ++nt) {
+        const int m = nt * 8 + g;
+        const float* sm = sts + m * r;
+        const uint32_t x0 = m < M && ja < r ? pack2<__nv_bfloat16>(sm[ja], sm[ja + 1]) : 0u;
+        const uint32_t x1 = m < M && jb < r ? pack2<__nv_bfloat16>(sm[jb], sm[jb + 1]) : 0u;
+        mma16816(c[nt], a, x0, x1);
       }
     }
+    // C fragment: rows (row, row + 8) x tokens (nt*8 + 2q, +1)
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int m = nt * 8 + 2 * q + (e & 1);
+        if (m < M) dst[m * kDecRows + row + (e >> 1) * 8] = c[nt][e];
+      }
   }
 }
 
@@ -323,7 +337,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   // weight ring (1024-byte aligned for the 128-byte swizzle) | x ring | scale
   // ring | lut | k-group sums | rank term [M, 128] | earlier partials [M, 128] |
-  // the finish block's rank term [M, 128]
+  // the finish block's rank term [M, 128] | sT [M, r]
   uint8_t* base = align_smem<1024>(smem_raw);
   uint8_t* ring = base;
   uint8_t* xring = base + p.off_x;
@@ -333,9 +347,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   float* rt = reinterpret_cast<float*>(base + p.off_rt);
   float* psum = reinterpret_cast<float*>(base + p.off_psum);
   float* rtf = reinterpret_cast<float*>(base + p.off_rtf);
+  float* sts = reinterpret_cast<float*>(base + p.off_sts);
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-  __shared__ __align__(8) uint64_t pub_done;  // this CTA's partial is in global memory
   __shared__ __align__(8) uint64_t rt_full;   // rank term (and earlier partials) of a block ready
   __shared__ __align__(8) uint64_t rt_empty;  // ... and consumed
   __shared__ __align__(8) uint64_t fin_ready; // the finish block's partials and rank term
@@ -353,10 +367,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kConsumers);
     }
-    mbar_init(&pub_done, kRowGroups);
-    mbar_init(&rt_full, 1);
+    mbar_init(&rt_full, kRankWarps);
     mbar_init(&rt_empty, kRowGroups);
-    mbar_init(&fin_ready, 1);
+    mbar_init(&fin_ready, kRankWarps);
     fence_mbarrier_init();
   }
   // set-up barrier 2: the producer arrives as soon as the mbarriers are
@@ -419,37 +432,60 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
     return;
   }
-  if (warp == 1) {
-    // ---------------------------------------------------------- rank warp --
-    // rows [rb*128, +128) of the rank term (computed by the preceding rank
-    // kernels over all N) into shared memory: dst[m, row]
-    auto copy_rt = [&](int rb, float* dst) {
-      for (int i = lane; i < p.M * kDecRows; i += 32) {
-        const int m = i / kDecRows, row = i % kDecRows, n = rb * kDecRows + row;
-        dst[i] = n < p.N ? __ldcg(p.rt + static_cast<long long>(m) * p.N + n) : 0.f;
-      }
+  if (warp == 1 || warp >= 2 + kConsumers) {
+    // --------------------------------------------------------- rank warps --
+    // three warps fold sT and pre-sum the finish block's earlier partials
+    // together; the 16-row tiles of every rank term are dealt round-robin
+    // over the three
+    const int rw = warp == 1 ? 0 : warp - (1 + kConsumers);
+    constexpr int kRankAll = 32 * kRankWarps;  // named barrier 3
+    auto prefetch_rows = [&](int rb) {  // B rows of a row block this CTA writes, to L2
+      if (p.b == nullptr) return;
+      const int rows = min(kDecRows, p.N - rb * kDecRows);
+      const char* bp = reinterpret_cast<const char*>(p.b + static_cast<long long>(rb) * kDecRows * p.r);
+      for (int off = (rw * 32 + lane) * 128; off < rows * p.r * 2; off += kRankAll * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(bp + off));
     };
-    // the rank term comes from this grid's programmatic primary (the rank
-    // kernels, which also zeroed the partial flags)
+    auto rows_of = [&](int rb, float* dst) {  // this warp's tiles of the block
+      rank_rows<kNT>(p.b, sts, p.M, p.N, p.r, rb, rw, kRankWarps, lane, dst);
+    };
+    if (pl.has_fin) prefetch_rows(pl.fin_rb);
+    if (pl.n_whole > 0) prefetch_rows(pl.w_lo);
+    // sT comes from the preceding rank kernel (this grid's programmatic
+    // primary), which also zeroed the partial flags
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (p.rt != nullptr && pl.has_fin) copy_rt(pl.fin_rb, rtf);
+    if (p.b != nullptr) {
+      for (int i = rw * 32 + lane; i < p.M * p.r; i += kRankAll) {
+        float v = 0.f;
+        for (int s0 = 0; s0 < p.st_splits; s0 += 8) {  // loads in flight together
+          float t8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            t8[u] = s0 + u < p.st_splits
+                        ? __ldcg(p.st + static_cast<long long>(s0 + u) * p.M * p.r + i)
+                        : 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v += t8[u];
+        }
+        sts[i] = v;
+      }
+      named_bar_sync(3, kRankAll);
+      // the rank terms of the finish block and of the first whole block while
+      // the consumers stream (the finish block is streamed last)
+      if (pl.has_fin) rows_of(pl.fin_rb, rtf);
+    }
     int w = 0;  // whole blocks whose rank term is staged
     if (pl.n_whole > 0) {  // the first one at once (its buffer starts free)
-      if (p.rt != nullptr) copy_rt(pl.w_lo, rt);
+      if (p.b != nullptr) rows_of(pl.w_lo, rt);
       __syncwarp();
       if (lane == 0) mbar_arrive(&rt_full);
       w = 1;
     }
-    if (pl.has_pub) {
-      // the consumers stored this CTA's partial (and fenced): raise its flag
-      // before waiting for anyone else's, so flags never wait on one another
-      const bool ok = mbar_wait(&pub_done, 0, p.status, kDevTimeoutReduce);
-      if (lane == 0 && ok) st_release_gpu(p.flags + cta, 1u);
-    }
     if (pl.has_fin) {
       // the partials of the CTAs before this one that cover the start of the
       // finish block (their publish segments come first), summed in CTA
-      // (= k) order, ready long before this CTA streams the block's end
+      // (= k) order, ready long before this CTA streams the block's end; the
+      // three rank warps take every third group of 32 float4s
       const int jlo = unit_owner(p.units, ctas, static_cast<long long>(pl.fin_rb) * p.S);
       bool ok = true;
       const uint64_t t0 = globaltimer_ns();
@@ -466,32 +502,45 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const int n4 = p.M * kDecRows / 4;
       const float4* parts = reinterpret_cast<const float4*>(p.partials);
       float4* ps4 = reinterpret_cast<float4*>(psum);
-      for (int i = lane; i < n4; i += 32) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j0 = jlo; j0 < cta && ok; j0 += 8) {
-          float4 v[8];
+      for (int i0 = rw * 32 + lane; i0 < n4; i0 += 4 * kRankAll) {
+        float4 acc[4];
 #pragma unroll
-          for (int u = 0; u < 8; ++u)  // up to eight publishers' loads in flight
-            v[u] = j0 + u < cta ? __ldcg(parts + static_cast<long long>(j0 + u) * n4 + i)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = jlo; j0 < cta && ok; j0 += 2) {
+          float4 v[2][4];  // two publishers x four float4s in flight
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {  // in publisher order
-            if (j0 + u < cta) {
-              acc.x += v[u].x;
-              acc.y += v[u].y;
-              acc.z += v[u].z;
-              acc.w += v[u].w;
+          for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = i0 + u * kRankAll;
+              v[jj][u] = j0 + jj < cta && i < n4
+                             ? __ldcg(parts + static_cast<long long>(j0 + jj) * n4 + i)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {  // in publisher order
+            if (j0 + jj < cta) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                acc[u].x += v[jj][u].x;
+                acc[u].y += v[jj][u].y;
+                acc[u].z += v[jj][u].z;
+                acc[u].w += v[jj][u].w;
+              }
             }
           }
         }
-        ps4[i] = acc;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kRankAll < n4) ps4[i0 + u * kRankAll] = acc[u];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&fin_ready);
     }
     for (; w < pl.n_whole; ++w) {
+      if (w + 1 < pl.n_whole) prefetch_rows(pl.w_lo + w + 1);
       if (!mbar_wait(&rt_empty, (w & 1) ^ 1, p.status, kDevTimeoutEmpty)) break;
-      if (p.rt != nullptr) copy_rt(pl.w_lo + w, rt);
+      if (p.b != nullptr) rows_of(pl.w_lo + w, rt);
       __syncwarp();
       if (lane == 0) mbar_arrive(&rt_full);
     }
@@ -690,9 +739,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
               if (m < p.M) __stcg(part + m * kDecRows + row, acc[i][nt][2 * h + c]);
             }
         }
+      // every writer fences its stores, then one thread raises this CTA's flag
+      // (after the rank kernel, which zeroed the flags, has completed)
       __threadfence();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pub_done);
+      named_bar_sync(4, 32 * kRowGroups);
+      if (rg == 0 && lane == 0) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        st_release_gpu(p.flags + cta, 1u);
+      }
       continue;
     }
     // whole: the rank term from rt (cycled with the rank warp); finish: the
@@ -716,7 +770,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (m >= p.M) continue;
             float v = acc[i][nt][2 * h + c];
             if (kind == 2 && have) v = psum[m * kDecRows + row] + v;
-            if (p.rt != nullptr && have) v += rterm[m * kDecRows + row];
+            if (p.b != nullptr && have) v += rterm[m * kDecRows + row];
             p.y[static_cast<long long>(m) * p.ldy + n] = __float2bfloat16_rn(v);
           }
       }
@@ -726,11 +780,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 }
 
 // Partial sums of sT[m, j] = scale * sum_k x[m, k] A[j, k] for m < M <= 16:
-// CTA (j, s) covers the s-th k slice (512 k); thread t takes the 8-wide chunk
-// t and loads the A chunk and every token's chunk at once (one round of
-// memory latency), then the CTA reduces in a fixed order.  It signals its
-// dependent grids (the rank-term kernel, then the decode kernel) at once so
-// they start meanwhile; the rank-term kernel adds the slices in order.
+// CTA (j, s) covers the s-th k slice (~2048 k); thread t takes the 8-wide
+// chunks t, t + 256, ... and loads the A chunk and every token's chunk at once
+// (one round of memory latency for slices up to 2048), then the CTA reduces
+// in a fixed order.  It signals its dependent grid (the decode kernel) at
+// once so that grid streams weights meanwhile; the decode kernel adds the
+// slices in order.
 __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ a, int M, int K, int r,
     int kslice, float scale, float* __restrict__ st, uint32_t* __restrict__ counters,
@@ -788,37 +843,6 @@ __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
 }
 
 
-// The decode path's rank term rt[m, n] = sum_j B[n, j] sT[m, j] for every row
-// n of the weight, sT the fold (in split order) of the rank kernel's
-// partials.  A programmatic dependent of that kernel (waits for it before
-// reading sT) and the primary of the decode kernel, which reads rt only in
-// its rank warp after its own griddepcontrol.wait; both launch at once, so
-// this pass over B (N x r bf16) overlaps the decode kernel's weight stream.
-__global__ void __launch_bounds__(kRankThreads) lora_rank_up_kernel(const float* __restrict__ st,
-                                                           int st_splits,
-                                                           const __nv_bfloat16* __restrict__ b,
-                                                           int M, int N, int r,
-                                                           float* __restrict__ rt) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  extern __shared__ float sts[];  // [M, r]
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int i = threadIdx.x; i < M * r; i += blockDim.x) {
-    float v = 0.f;
-    for (int s0 = 0; s0 < st_splits; ++s0) v += __ldcg(st + static_cast<long long>(s0) * M * r + i);
-    sts[i] = v;
-  }
-  __syncthreads();
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  float out[kMaxTok];
-#pragma unroll
-  for (int m = 0; m < kMaxTok; ++m) out[m] = 0.f;
-  add_rank_term(b + static_cast<long long>(n) * r, sts, M, r, out);
-#pragma unroll
-  for (int m = 0; m < kMaxTok; ++m)
-    if (m < M) rt[static_cast<long long>(m) * N + n] = out[m];
-}
-
 int bits_of(int scheme) { return scheme == 0 ? 16 : (scheme == kINT8 ? 8 : 4); }
 int stage_k_of(int scheme) { return kBoxBytes * 8 / bits_of(scheme); }
 int quads_of(int scheme) { return stage_k_of(scheme) / 64; }
@@ -830,11 +854,11 @@ int gps_of(int scheme, int64_t group) {
 // Shared-memory layout of one CTA (offsets from the 1024-byte aligned base).
 struct DecLayout {
   int x_slot, scale_slot;
-  int off_x, off_scale, off_lut, off_red, off_rt, off_psum, off_rtf;
+  int off_x, off_scale, off_lut, off_red, off_rt, off_psum, off_rtf, off_sts;
   int bytes;  // including the alignment slack
 };
 
-DecLayout dec_layout(int scheme, int64_t M, int64_t group, int stages) {
+DecLayout dec_layout(int scheme, int64_t M, int64_t r, int64_t group, int stages) {
   DecLayout L;
   const int xr = x_rows_of(M), kNT = xr / 8;
   L.x_slot = quads_of(scheme) * xr * 128;
@@ -849,7 +873,8 @@ DecLayout dec_layout(int scheme, int64_t M, int64_t group, int stages) {
   const int tok = static_cast<int>(M) * kDecRows * 4;
   L.off_psum = L.off_rt + tok;
   L.off_rtf = L.off_psum + tok;
-  L.bytes = 1024 + L.off_rtf + tok;
+  L.off_sts = L.off_rtf + tok;
+  L.bytes = 1024 + L.off_sts + static_cast<int>((M * (r > 0 ? r : 1) * 4 + 15) / 16 * 16);
   return L;
 }
 
@@ -881,9 +906,12 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
                       static_cast<uint32_t>(gps), false))
       return MLORA_ERR_CUDA;
   }
-  const DecLayout L = dec_layout(kScheme, a.M, group, cfg.stages);
+  const DecLayout L = dec_layout(kScheme, a.M, a.r, group, cfg.stages);
   DecParams p;
-  p.rt = a.rt;
+  p.b = static_cast<const __nv_bfloat16*>(a.b);
+  p.st = a.st;
+  p.st_splits = a.b != nullptr ? rank_small_splits(a.K) : 0;
+  p.r = static_cast<int>(a.r);
   p.y = static_cast<__nv_bfloat16*>(a.y);
   p.ldy = a.ldy > 0 ? a.ldy : a.N;
   p.partials = a.partials;
@@ -906,6 +934,7 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   p.off_rt = L.off_rt;
   p.off_psum = L.off_psum;
   p.off_rtf = L.off_rtf;
+  p.off_sts = L.off_sts;
   p.status = device_status_ptr();
   auto kern = lora_decode_kernel<kScheme, kNT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -919,13 +948,13 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   lc.blockDim = dim3(kDecThreads);
   lc.dynamicSmemBytes = static_cast<size_t>(cfg.smem);
   lc.stream = s;
-  // a programmatic dependent of the rank kernels that precede it (which
-  // write nothing this kernel reads before griddepcontrol.wait)
+  // a programmatic dependent of the rank kernel that precedes it (which
+  // writes nothing this kernel reads before griddepcontrol.wait)
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = a.rt != nullptr ? 1 : 0;
+  lc.numAttrs = a.b != nullptr ? 1 : 0;
   LaunchScope scope(kKindGemv, s);
   e = cudaLaunchKernelEx(&lc, kern, wmap, smap, xmap, p);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -953,11 +982,11 @@ DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t 
   const int64_t ctas = std::min<int64_t>(num_sms(), units);
   const int64_t g = group > 0 ? group : 64;
   int stages = kMaxStages;
-  while (stages > 2 && dec_layout(scheme, M, g, stages).bytes > kSmemMax) --stages;
+  while (stages > 2 && dec_layout(scheme, M, r, g, stages).bytes > kSmemMax) --stages;
   DecodeConfig c;
   c.ctas = static_cast<int>(ctas);
   c.stages = stages;
-  c.smem = dec_layout(scheme, M, g, stages).bytes;
+  c.smem = dec_layout(scheme, M, r, g, stages).bytes;
   // some row block is shared between CTAs (then partials and flags are used)
   c.split_blocks = false;
   for (int64_t j = 1; j < ctas && !c.split_blocks; ++j)
@@ -988,45 +1017,9 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   }
 }
 
-int launch_rank_up(const float* st, int64_t K, const void* b, int64_t M, int64_t N, int64_t r,
-                   float* rt, cudaStream_t s) {
-  // same shared-memory carveout as the decode kernel beside it (a hint, set
-  // once per device)
-  static std::atomic<bool> carve_set[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64 || !carve_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(lora_rank_up_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
-      cudaGetLastError();  // a hint only: clear the error, launch without it
-    else if (dev < 64)
-      carve_set[dev].store(true, std::memory_order_release);
-  }
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(static_cast<unsigned>((N + kRankThreads - 1) / kRankThreads));
-  lc.blockDim = dim3(kRankThreads);
-  lc.dynamicSmemBytes = static_cast<size_t>(M * r * 4);
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  LaunchScope scope(kKindGemv, s);
-  cudaError_t e = cudaLaunchKernelEx(&lc, lora_rank_up_kernel, st, rank_small_splits(K),
-                                     static_cast<const __nv_bfloat16*>(b), static_cast<int>(M),
-                                     static_cast<int>(N), static_cast<int>(r), rt);
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_error(std::string("rank_up launch: ") + cudaGetErrorString(e));
-    return MLORA_ERR_CUDA;
-  }
-  return MLORA_OK;
-}
-
 int rank_small_splits(int64_t K) {
-  const int64_t s = (K + 511) / 512;  // ~512 k per CTA: one 8-wide chunk per thread
-  return static_cast<int>(s < 1 ? 1 : (s > 32 ? 32 : s));
+  const int64_t s = (K + 2047) / 2048;  // ~2048 k per CTA
+  return static_cast<int>(s < 1 ? 1 : (s > 16 ? 16 : s));
 }
 
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,

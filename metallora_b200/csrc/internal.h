@@ -115,7 +115,8 @@ struct GemvArgs {
   const void* x = nullptr;         // bf16 [M, K]
   const void* w = nullptr;         // codes or bf16 weights, rows of the [N, K] weight
   const void* scales_t = nullptr;  // prepared scale table [G, prepared_ld(N)] (quantised)
-  const float* rt = nullptr;     // fp32 [M, N] rank term s.(x.A^T).B^T, or nullptr
+  const void* b = nullptr;       // bf16 [N, r] or nullptr
+  const float* st = nullptr;     // fp32 [rank_small_splits(K), M, r] partials of s.x.A^T
   void* y = nullptr;             // bf16 [M, N]
   float* partials = nullptr;     // [ctas, M, 128]: one partial row block per CTA
   uint32_t* flags = nullptr;     // [ctas] zeroed (partial published)
@@ -136,11 +137,6 @@ DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t 
 int64_t gemv_row_blocks(int64_t N);
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 int rank_small_splits(int64_t K);
-// The decode path's rank term rt [M, N] from the sT partials of
-// launch_rank_small (a programmatic dependent of it; the decode kernel is one
-// of this).
-int launch_rank_up(const float* st, int64_t K, const void* b, int64_t M, int64_t N, int64_t r,
-                   float* rt, cudaStream_t s);
 // sT partials for the decode path; also zeroes the decode kernel's n_counters
 // partial flags.
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
