@@ -341,15 +341,26 @@ def run_ours(args, rank, world, local_rank):
     from metallora_b200.distributed import PeerAllReduce
     n_a, n_b = layer.A.numel(), layer.B.numel()
     peer = PeerAllReduce.create(n_a + n_b, device=dev) if world > 1 else None
+    side = torch.cuda.Stream(device=dev) if peer is not None else None
+    grads_ready = torch.cuda.Event() if peer is not None else None
+    exchanged = torch.cuda.Event() if peer is not None else None
+
+    def start_exchange():
+        # dA/dB are enqueued and the dx GEMM is not yet: the exchange kernel
+        # runs on a side stream beside that GEMM (its CTAs hold no shared
+        # memory; block 0 alone polls the peers' flags, the rest back off)
+        grads_ready.record(torch.cuda.current_stream())
+        side.wait_event(grads_ready)
+        with torch.cuda.stream(side):
+            peer.allreduce(flat_grads)
+        exchanged.record(side)
+
     if peer is not None:
         flat_grads = torch.empty(n_a + n_b, dtype=torch.float32, device=dev)
-        # written over (not added to) every step: no zeroing between steps.  The
-        # exchange runs after the backward on the same stream: overlapping it
-        # with the dx GEMM (the sink's on_grads hook on a side stream) measured
-        # slower at 2 GPUs (0.4606 vs 0.456 ms per step; the GEMM lost ~11 us
-        # with the exchange's flag-polling CTAs beside it).
-        layer._grad_sink = (peer.buffer[:n_a].view(layer.A.shape),
-                            peer.buffer[n_a:].view(layer.B.shape), False)
+        # written over (not added to) every step: no zeroing between steps
+        sink = (peer.buffer[:n_a].view(layer.A.shape), peer.buffer[n_a:].view(layer.B.shape),
+                False)
+        layer._grad_sink = sink + ((start_exchange,) if args.exchange_overlap else ())
     exchange_kind = "peer" if peer is not None else ("nccl" if world > 1 else "none")
 
     def step(xin, dyin):
@@ -359,7 +370,10 @@ def run_ours(args, rank, world, local_rank):
         xin.grad = None
         y = layer(xin)
         y.backward(dyin)
-        if peer is not None:
+        if peer is not None and args.exchange_overlap:
+            # the next step's weight gradients overwrite the exchanged buffer
+            torch.cuda.current_stream().wait_event(exchanged)
+        elif peer is not None:
             peer.allreduce(flat_grads)
         elif world > 1:
             flat = torch.cat([layer.A.grad.reshape(-1), layer.B.grad.reshape(-1)]).float()
@@ -439,7 +453,8 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded N(0,1) activations/grads, N(0,1/4096) base, U(+-1/64) A, "
                 "N(0,0.02) B)",
         "config": headline_config(world),
-        "grad_exchange": exchange_kind,
+        "grad_exchange": exchange_kind + (" (beside the dx GEMM, side stream)"
+                                          if peer is not None and args.exchange_overlap else ""),
         "host_cores_per_rank": host_cores,
         "tflops": round(total_tflops, 1),
         "step_frac_of_peak": round(total_tflops / world / peak, 4),
@@ -1043,6 +1058,9 @@ def main():
                          "(fp32, NF4, INT4/INT8 at N=1; the NF4 stack at every N)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="--workload stack: one flat all-reduce after the backward")
+    ap.add_argument("--exchange-after", dest="exchange_overlap", action="store_false",
+                    help="headline at N > 1: run the peer gradient exchange after the "
+                         "backward instead of beside the dx GEMM")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

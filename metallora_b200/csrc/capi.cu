@@ -294,12 +294,12 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
     return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
   const GemvPlan p = plan_gemv(workspace, M, K, N, r, scheme, group);
   // partial flags: zeroed by the rank kernel when there is one, else by a
-  // memset; no shared row block uses none
+  // one-CTA kernel; the decode kernel is the programmatic dependent of
+  // either.  No shared row block uses none.
   int rc;
-  if (a == nullptr && p.split) {
-    cudaError_t e = cudaMemsetAsync(p.flags, 0, p.flag_bytes, s);
-    if (e != cudaSuccess) return cuda_fail(e, "memset");
-  }
+  if (a == nullptr && p.split &&
+      (rc = launch_flags_zero(p.flags, static_cast<int64_t>(p.flag_bytes / 4), s)))
+    return rc;
   if (a != nullptr &&
       (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.flags,
                               p.split ? p.ctas : 0, s)))
@@ -320,6 +320,7 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
   g.r = r;
   g.group = group;
   g.ldy = ldy;
+  g.pdl = a != nullptr || p.split;
   return launch_gemv(g, s);
 }
 

@@ -26,17 +26,20 @@
 //               prepared scale table [groups, rows] (quantised bases) and the
 //               tokens' [x_rows x 64] boxes of x for the stage's k range
 //               (128-byte swizzle; rows past M are zero-filled);
-//   warps 1, 10, 11  (rank warps) wait for the rank kernel (programmatic
+//   warps 1, 18, 19  (rank warps) wait for the rank kernel (programmatic
 //               dependent launch), fold its sT partials into shared memory,
 //               compute the rank term sum_j B[n, j] sT[m, j] of every row block
 //               this CTA writes (mma.m16n8k16, tiles split three ways) while
 //               the consumers stream, and pre-sum the partials a finish
 //               segment needs;
-//   warps 2..9  tensor cores: 2 row groups (64 rows, four 16-row tiles each)
+//   warps 2..17 tensor cores: 4 row groups (32 rows, two 16-row tiles each)
 //               x 4 k-groups (the stage's 64-wide k quads dealt round-robin);
 //               mma.m16n8k16 with the WEIGHTS as the A operand and the tokens
-//               as B, so one token fragment feeds four tiles; the k-groups'
+//               as B, so one token fragment feeds two tiles; the k-groups'
 //               sums meet in shared memory in fixed order at segment end.
+//               Sixteen consumer warps (four per scheduler) keep the
+//               shared-memory pipe busy: the NF4 pair table alone takes one
+//               wavefront per 64 weights.
 // Dequantisation never multiplies per weight:
 //   NF4   a 256-entry table (one copy per lane, so lookups never conflict) maps
 //         a code byte to the bf16 pair (L[lo], L[hi]) of the reference's
@@ -70,12 +73,14 @@ constexpr int kDecRows = 128;     // output rows per row block
 constexpr int kBoxBytes = 128;    // inner extent of one weight box (128-byte swizzle)
 constexpr int kStageBytes = kDecRows * kBoxBytes;  // 16 KB of weights per stage
 constexpr int kMaxTok = 16;
-constexpr int kRowGroups = 2;     // consumer warps per k-group, 64 rows each
+constexpr int kRowGroups = 4;     // consumer warps per k-group, 32 rows each
 constexpr int kKG = 4;            // k-groups
-constexpr int kTiles = 4;         // 16-row MMA tiles per consumer warp
+constexpr int kTiles = 2;         // 16-row MMA tiles per consumer warp
+constexpr int kGroupRows = kTiles * 16;
+static_assert(kRowGroups * kGroupRows == 128, "a row block is 128 rows");
 constexpr int kConsumers = kRowGroups * kKG;
 constexpr int kRankWarps = 3;     // warp 1 and the two last warps
-constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 384
+constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 640
 constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic; the static barriers take the rest
 constexpr int kRankThreads = 256;            // rank kernel
 constexpr int kMaxStages = 8;
@@ -104,7 +109,7 @@ struct DecParams {
   uint32_t* flags;         // [ctas], zeroed before the launch
   int M, N, K, r, group, gps;
   int S;                   // stages per row block
-  long long units;         // row blocks * S
+  unsigned units;          // row blocks * S (units * ctas < 2^32, checked at launch)
   int stages;              // ring depth
   int x_rows;              // token rows of one x box (8 or 16)
   int x_slot, scale_slot;  // bytes per stage
@@ -233,8 +238,10 @@ __device__ __forceinline__ void rank_rows(const __nv_bfloat16* b, const float* s
 
 // ------------------------------------------------------------- work split --
 
-__device__ __forceinline__ long long unit_begin(long long units, int cta, int ctas) {
-  return units * cta / ctas;
+// 32-bit arithmetic throughout (the launch checks units * ctas < 2^32): the
+// plan sits between kernel start and the first weight copy.
+__device__ __forceinline__ unsigned unit_begin(unsigned units, int cta, int ctas) {
+  return units * static_cast<unsigned>(cta) / static_cast<unsigned>(ctas);
 }
 
 // One CTA's segments in processing order: [publish], whole blocks, [finish].
@@ -248,10 +255,11 @@ struct DecPlan {
 
 __device__ __forceinline__ DecPlan make_plan(const DecParams& p, int cta, int ctas) {
   DecPlan pl;
-  const long long u0 = unit_begin(p.units, cta, ctas), u1 = unit_begin(p.units, cta + 1, ctas);
-  const int ra = static_cast<int>(u0 / p.S), rb_last = static_cast<int>((u1 - 1) / p.S);
-  const int sa = static_cast<int>(u0 - static_cast<long long>(ra) * p.S);
-  const int eb = static_cast<int>(u1 - static_cast<long long>(rb_last) * p.S);  // end stage in last block
+  const unsigned S = static_cast<unsigned>(p.S);
+  const unsigned u0 = unit_begin(p.units, cta, ctas), u1 = unit_begin(p.units, cta + 1, ctas);
+  const int ra = static_cast<int>(u0 / S), rb_last = static_cast<int>((u1 - 1) / S);
+  const int sa = static_cast<int>(u0 - static_cast<unsigned>(ra) * S);
+  const int eb = static_cast<int>(u1 - static_cast<unsigned>(rb_last) * S);  // end stage in last block
   pl.has_pub = pl.has_fin = false;
   pl.pub_rb = pl.pub_s0 = pl.pub_s1 = pl.fin_rb = pl.fin_s0 = 0;
   if (ra == rb_last) {
@@ -319,8 +327,8 @@ __device__ __forceinline__ void plan_segment(const DecPlan& pl, int S, int t, in
 }
 
 // First CTA whose range holds unit u.
-__device__ __forceinline__ int unit_owner(long long units, int ctas, long long u) {
-  int j = static_cast<int>(u * ctas / units);
+__device__ __forceinline__ int unit_owner(unsigned units, int ctas, unsigned u) {
+  int j = static_cast<int>(u * static_cast<unsigned>(ctas) / units);
   if (j >= ctas) j = ctas - 1;
   while (j + 1 < ctas && unit_begin(units, j + 1, ctas) <= u) ++j;
   while (j > 0 && unit_begin(units, j, ctas) > u) --j;
@@ -362,6 +370,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const DecPlan& pl = pl_s;
 
   if (threadIdx.x == 0) {
+    // the descriptor fetches overlap the plan and the barrier set-up
+    prefetch_tmap(&wmap);
+    prefetch_tmap(&xmap);
+    if constexpr (D::kScaled) prefetch_tmap(&smap);
     pl_s = make_plan(p, cta, ctas);
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -375,6 +387,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   // set-up barrier 2: the producer arrives as soon as the mbarriers are
   // initialised and starts streaming; the other warps first build the table
   if (warp == 0) {
+    // bar.arrive is warp-aligned: lanes 1..31 must not arrive for the warp
+    // before lane 0 has initialised the barriers
+    __syncwarp();
     named_bar_arrive(2, kDecThreads);
   } else {
     if constexpr (kScheme == kNF4) {
@@ -390,9 +405,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      prefetch_tmap(&wmap);
-      prefetch_tmap(&xmap);
-      if constexpr (D::kScaled) prefetch_tmap(&smap);
       const uint32_t stage_tx = kStageBytes + (D::kScaled ? p.gps * kDecRows * 4 : 0) +
                                 D::kQuads * p.x_rows * 128;
       bool ok = true;
@@ -486,19 +498,26 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       // finish block (their publish segments come first), summed in CTA
       // (= k) order, ready long before this CTA streams the block's end; the
       // three rank warps take every third group of 32 float4s
-      const int jlo = unit_owner(p.units, ctas, static_cast<long long>(pl.fin_rb) * p.S);
+      const int jlo = unit_owner(p.units, ctas, static_cast<unsigned>(pl.fin_rb) * static_cast<unsigned>(p.S));
+      // every lane polls its own publishers' flags, so one round trip covers
+      // all of them; the timeout verdict is taken warp-wide
       bool ok = true;
       const uint64_t t0 = globaltimer_ns();
-      for (int j = jlo; j < cta && ok; ++j) {
-        uint32_t spins = 0;
-        while (ld_acquire_gpu(p.flags + j) == 0u) {
-          if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > MLORA_WAIT_BUDGET_NS) {
-            record_status(p.status, kDevTimeoutReduce);
-            ok = false;
-            break;
-          }
+      for (uint32_t spins = 1;; ++spins) {
+        bool up = true;
+        for (int j = jlo + lane; j < cta; j += 32) up = up & (ld_acquire_gpu(p.flags + j) != 0u);
+        if (__all_sync(0xffffffffu, up)) break;
+        if ((spins & 15u) == 0 &&
+            __any_sync(0xffffffffu, globaltimer_ns() - t0 > MLORA_WAIT_BUDGET_NS)) {
+          if (lane == 0) record_status(p.status, kDevTimeoutReduce);
+          ok = false;
+          break;
         }
       }
+      __syncwarp();
+      __threadfence();  // flags acquired by other lanes order this lane's loads as well
+      // partials summed in publisher (= k) order; four elements x four
+      // publishers of loads in flight per round
       const int n4 = p.M * kDecRows / 4;
       const float4* parts = reinterpret_cast<const float4*>(p.partials);
       float4* ps4 = reinterpret_cast<float4*>(psum);
@@ -506,10 +525,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         float4 acc[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j0 = jlo; j0 < cta && ok; j0 += 2) {
-          float4 v[2][4];  // two publishers x four float4s in flight
+        for (int j0 = jlo; j0 < cta && ok; j0 += 4) {
+          float4 v[4][4];
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj)
+          for (int jj = 0; jj < 4; ++jj)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int i = i0 + u * kRankAll;
@@ -518,7 +537,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {  // in publisher order
+          for (int jj = 0; jj < 4; ++jj) {  // in publisher order
             if (j0 + jj < cta) {
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
@@ -552,7 +571,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   // wait (then it skips the math), so none can be stranded.
   constexpr int kAll = 32 * kConsumers;  // named barrier 1
   const int cw = warp - 2;
-  const int rg = cw % kRowGroups;        // 64-row group
+  const int rg = cw % kRowGroups;        // 32-row group
   const int kg = cw / kRowGroups;        // k-group
   const int g = lane >> 2, q = lane & 3;
   const int fq = D::kFlip ? (q >> 1) : 0;
@@ -592,7 +611,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           for (int i = 0; i < kTiles; ++i) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int row = rg * 64 + i * 16 + h * 8 + g;
+              const int row = rg * kGroupRows + i * 16 + h * 8 + g;
               const uint8_t* rp = stage + row * kBoxBytes;
               if constexpr (kWords == 2) {
                 const int off = j * D::kQuadBytes + 8 * q;
@@ -730,7 +749,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       for (int i = 0; i < kTiles; ++i)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int row = rg * 64 + i * 16 + h * 8 + g;
+          const int row = rg * kGroupRows + i * 16 + h * 8 + g;
 #pragma unroll
           for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
@@ -759,7 +778,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int i = 0; i < kTiles; ++i)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int row = rg * 64 + i * 16 + h * 8 + g;
+        const int row = rg * kGroupRows + i * 16 + h * 8 + g;
         const int n = rb * kDecRows + row;
         if (n >= p.N) continue;
 #pragma unroll
@@ -842,6 +861,13 @@ __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
   }
 }
 
+// Zeroes the decode kernel's partial flags when no rank kernel precedes it
+// (plain weights, no LoRA term), and lets the decode kernel start at once as
+// its programmatic dependent.
+__global__ void __launch_bounds__(256) lora_flags_zero_kernel(uint32_t* __restrict__ flags, int n) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int i = threadIdx.x; i < n; i += blockDim.x) flags[i] = 0u;
+}
 
 int bits_of(int scheme) { return scheme == 0 ? 16 : (scheme == kINT8 ? 8 : 4); }
 int stage_k_of(int scheme) { return kBoxBytes * 8 / bits_of(scheme); }
@@ -922,7 +948,12 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   p.group = static_cast<int>(group);
   p.gps = gps;
   p.S = static_cast<int>((a.K + D::kStageK - 1) / D::kStageK);
-  p.units = static_cast<long long>(gemv_row_blocks(a.N)) * p.S;
+  const int64_t units = gemv_row_blocks(a.N) * p.S;
+  if (units * cfg.ctas >= (int64_t(1) << 32)) {
+    set_error("decode: weight too large for the 32-bit work split");
+    return MLORA_ERR_UNSUPPORTED;
+  }
+  p.units = static_cast<unsigned>(units);
   p.stages = cfg.stages;
   p.x_rows = xr;
   p.x_slot = L.x_slot;
@@ -948,13 +979,15 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   lc.blockDim = dim3(kDecThreads);
   lc.dynamicSmemBytes = static_cast<size_t>(cfg.smem);
   lc.stream = s;
-  // a programmatic dependent of the rank kernel that precedes it (which
-  // writes nothing this kernel reads before griddepcontrol.wait)
+  // a programmatic dependent of the rank (or flag-zeroing) kernel that
+  // precedes it, which writes nothing this kernel reads before
+  // griddepcontrol.wait; x and the weights were complete before that kernel
+  // started
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = a.b != nullptr ? 1 : 0;
+  lc.numAttrs = a.pdl ? 1 : 0;
   LaunchScope scope(kKindGemv, s);
   e = cudaLaunchKernelEx(&lc, kern, wmap, smap, xmap, p);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -1015,6 +1048,17 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
     case kINT8: return launch_decode_scheme<kINT8>(a, cfg, s);
     default: set_error("decode: unknown scheme"); return MLORA_ERR_INVALID_ARG;
   }
+}
+
+int launch_flags_zero(uint32_t* flags, int64_t n, cudaStream_t s) {
+  LaunchScope scope(kKindGemv, s);
+  lora_flags_zero_kernel<<<1, 256, 0, s>>>(flags, static_cast<int>(n));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("flags_zero launch: ") + cudaGetErrorString(e));
+    return MLORA_ERR_CUDA;
+  }
+  return MLORA_OK;
 }
 
 int rank_small_splits(int64_t K) {

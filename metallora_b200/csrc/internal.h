@@ -122,6 +122,7 @@ struct GemvArgs {
   uint32_t* flags = nullptr;     // [ctas] zeroed (partial published)
   int64_t M = 0, N = 0, K = 0, r = 0, group = 64;
   int64_t ldy = 0;  // row stride of y (0: N)
+  bool pdl = false;  // launched as the programmatic dependent of the kernel before it
 };
 constexpr int64_t kGemvMaxTokens = 16;
 // Decode launch shape: persistent CTAs (one per SM at most) over the stream-K
@@ -141,6 +142,8 @@ int rank_small_splits(int64_t K);
 // partial flags.
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
                       float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s);
+// Zeroes n partial flags (decode without a rank kernel before it).
+int launch_flags_zero(uint32_t* flags, int64_t n, cudaStream_t s);
 
 // ------------------------------------------------------- rank projection -----
 // out[m, j] = scale * sum_k X[m, k] * L[j, k] for j < R (L rows >= r are zero).
