@@ -255,10 +255,9 @@ int check_ptrs16(std::initializer_list<const void*> ptrs) {
 struct GemvPlan {
   bool split;
   int ctas;
-  uint32_t* flags;
-  size_t flag_bytes;
   float* st;
   float* partials;
+  int64_t partial_floats;
   size_t bytes;
 };
 
@@ -273,11 +272,10 @@ GemvPlan plan_gemv(void* ws, int64_t M, int64_t K, int64_t N, int64_t r, int sch
   p.split = cfg.split_blocks;
   p.ctas = cfg.ctas;
   Carve c(ws);
-  p.flag_bytes = p.split ? static_cast<size_t>(p.ctas) * 4 : 0;
-  p.flags = p.split ? static_cast<uint32_t*>(c.take(p.flag_bytes)) : nullptr;
   p.st = static_cast<float*>(
       c.take(static_cast<size_t>(rank_small_splits(K)) * M * (r > 0 ? r : 1) * 4));
-  p.partials = p.split ? static_cast<float*>(c.take(static_cast<size_t>(p.ctas) * M * 128 * 4))
+  p.partial_floats = p.split ? static_cast<int64_t>(p.ctas) * M * 128 : 0;
+  p.partials = p.split ? static_cast<float*>(c.take(static_cast<size_t>(p.partial_floats) * 4))
                        : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
@@ -293,16 +291,15 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
   if (workspace == nullptr || workspace_bytes < need.bytes)
     return fail(MLORA_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need.bytes) + " bytes");
   const GemvPlan p = plan_gemv(workspace, M, K, N, r, scheme, group);
-  // partial flags: zeroed by the rank kernel when there is one, else by a
-  // one-CTA kernel; the decode kernel is the programmatic dependent of
-  // either.  No shared row block uses none.
+  // partial slots: set to their empty pattern by the rank kernel when there
+  // is one, else by a small fill kernel; the decode kernel is the
+  // programmatic dependent of either.  No shared row block uses none.
   int rc;
-  if (a == nullptr && p.split &&
-      (rc = launch_flags_zero(p.flags, static_cast<int64_t>(p.flag_bytes / 4), s)))
+  if (a == nullptr && p.split && (rc = launch_partials_fill(p.partials, p.partial_floats, s)))
     return rc;
   if (a != nullptr &&
-      (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.flags,
-                              p.split ? p.ctas : 0, s)))
+      (rc = launch_rank_small(x, a, M, K, r, alpha / static_cast<float>(r), p.st, p.partials,
+                              p.partial_floats, s)))
     return rc;
   GemvArgs g;
   g.scheme = scheme;
@@ -313,7 +310,6 @@ int run_gemv(int scheme, const void* x, const void* w, const void* scales_t,
   g.st = p.st;
   g.y = y;
   g.partials = p.partials;
-  g.flags = p.flags;
   g.M = M;
   g.N = N;
   g.K = K;

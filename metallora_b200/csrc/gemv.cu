@@ -12,10 +12,15 @@
 //   whole    a complete row block: summed here and written to y;
 //   publish  the part of a row block before its end (the range's last
 //            segment): summed here and stored as this CTA's one fp32 partial
-//            [M, 128], then the consumers raise this CTA's flag;
+//            [M, 128];
 //   finish   the end of a row block that began in earlier CTAs (the range's
-//            first segment): once their flags are up, their partials are
-//            added in CTA order, then this CTA's own sum, and y is written.
+//            first segment): their partials are added in CTA order, then
+//            this CTA's own sum, and y is written.
+// The kernel before this one (the rank kernel, or a fill kernel) sets every
+// partial slot to kPartialEmpty, a signalling-NaN pattern that arithmetic
+// never produces; a publisher stores its values over it once that kernel
+// has completed, and a finisher polls the values themselves until none is
+// kPartialEmpty -- the data is the handoff, with no flag round trip.
 // Each CTA streams its publish segment first and its finish segment last, so
 // a finisher only ever waits for lower CTAs' first segments: no cycles, and
 // the summation order is fixed by the shape (bitwise repeatable).
@@ -84,6 +89,9 @@ constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 640
 constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic; the static barriers take the rest
 constexpr int kRankThreads = 256;            // rank kernel
 constexpr int kMaxStages = 8;
+// Fill pattern of an unpublished partial slot: a signalling NaN with a
+// payload; arithmetic results are never signalling NaNs.
+constexpr uint32_t kPartialEmpty = 0xFFBFFFFFu;
 
 // scheme 0 = dense bf16 weights, else QuantScheme.
 template <int kScheme>
@@ -105,8 +113,7 @@ struct DecParams {
   int st_splits;
   __nv_bfloat16* y;        // [M, ldy]
   long long ldy;
-  float* partials;         // [ctas, M, 128]: one per CTA
-  uint32_t* flags;         // [ctas], zeroed before the launch
+  float* partials;         // [ctas, M, 128]: one per CTA, set to kPartialEmpty before the launch
   int M, N, K, r, group, gps;
   int S;                   // stages per row block
   unsigned units;          // row blocks * S (units * ctas < 2^32, checked at launch)
@@ -132,14 +139,22 @@ __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_gpu(float* p, float v) {
+  asm volatile("st.relaxed.gpu.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ float4 ld_relaxed_gpu(const float4* p) {
+  float4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
+}
+
+__device__ __forceinline__ bool partial_empty(const float4& v) {
+  return __float_as_uint(v.x) == kPartialEmpty || __float_as_uint(v.y) == kPartialEmpty ||
+         __float_as_uint(v.z) == kPartialEmpty || __float_as_uint(v.w) == kPartialEmpty;
 }
 
 // The four A-fragment words of one 16-row tile for MMA step b of a quad:
@@ -464,7 +479,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (pl.has_fin) prefetch_rows(pl.fin_rb);
     if (pl.n_whole > 0) prefetch_rows(pl.w_lo);
     // sT comes from the preceding rank kernel (this grid's programmatic
-    // primary), which also zeroed the partial flags
+    // primary), which also set the partial slots to kPartialEmpty
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (p.b != nullptr) {
       for (int i = rw * 32 + lane; i < p.M * p.r; i += kRankAll) {
@@ -499,48 +514,44 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       // (= k) order, ready long before this CTA streams the block's end; the
       // three rank warps take every third group of 32 float4s
       const int jlo = unit_owner(p.units, ctas, static_cast<unsigned>(pl.fin_rb) * static_cast<unsigned>(p.S));
-      // every lane polls its own publishers' flags, so one round trip covers
-      // all of them; the timeout verdict is taken warp-wide
+      // partials summed in publisher (= k) order, two elements x four
+      // publishers of loads in flight per round; a round is reloaded until
+      // none of its values is kPartialEmpty (bounded)
       bool ok = true;
       const uint64_t t0 = globaltimer_ns();
-      for (uint32_t spins = 1;; ++spins) {
-        bool up = true;
-        for (int j = jlo + lane; j < cta; j += 32) up = up & (ld_acquire_gpu(p.flags + j) != 0u);
-        if (__all_sync(0xffffffffu, up)) break;
-        if ((spins & 15u) == 0 &&
-            __any_sync(0xffffffffu, globaltimer_ns() - t0 > MLORA_WAIT_BUDGET_NS)) {
-          if (lane == 0) record_status(p.status, kDevTimeoutReduce);
-          ok = false;
-          break;
-        }
-      }
-      __syncwarp();
-      __threadfence();  // flags acquired by other lanes order this lane's loads as well
-      // partials summed in publisher (= k) order; four elements x four
-      // publishers of loads in flight per round
       const int n4 = p.M * kDecRows / 4;
       const float4* parts = reinterpret_cast<const float4*>(p.partials);
       float4* ps4 = reinterpret_cast<float4*>(psum);
-      for (int i0 = rw * 32 + lane; i0 < n4; i0 += 4 * kRankAll) {
-        float4 acc[4];
+      constexpr int kE = 2, kP = 4;
+      for (int i0 = rw * 32 + lane; i0 < n4; i0 += kE * kRankAll) {
+        float4 acc[kE];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j0 = jlo; j0 < cta && ok; j0 += 4) {
-          float4 v[4][4];
+        for (int u = 0; u < kE; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = jlo; j0 < cta; j0 += kP) {
+          float4 v[kP][kE];
+          for (uint32_t spins = 1;; ++spins) {
+            bool ready = true;
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj)
+            for (int jj = 0; jj < kP; ++jj)
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int i = i0 + u * kRankAll;
-              v[jj][u] = j0 + jj < cta && i < n4
-                             ? __ldcg(parts + static_cast<long long>(j0 + jj) * n4 + i)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int u = 0; u < kE; ++u) {
+                const int i = i0 + u * kRankAll;
+                v[jj][u] = j0 + jj < cta && i < n4
+                               ? ld_relaxed_gpu(parts + static_cast<long long>(j0 + jj) * n4 + i)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                ready = ready && !partial_empty(v[jj][u]);
+              }
+            if (ready || !ok) break;
+            if ((spins & 15u) == 0 && globaltimer_ns() - t0 > MLORA_WAIT_BUDGET_NS) {
+              record_status(p.status, kDevTimeoutReduce);
+              ok = false;
             }
+          }
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {  // in publisher order
+          for (int jj = 0; jj < kP; ++jj) {  // in publisher order
             if (j0 + jj < cta) {
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
+              for (int u = 0; u < kE; ++u) {
                 acc[u].x += v[jj][u].x;
                 acc[u].y += v[jj][u].y;
                 acc[u].z += v[jj][u].z;
@@ -550,7 +561,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kE; ++u)
           if (i0 + u * kRankAll < n4) ps4[i0 + u * kRankAll] = acc[u];
       }
       __syncwarp();
@@ -744,6 +755,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // C fragment: rows (g, g+8) of each tile = output rows; columns (2q, 2q+1)
     // of each 8-token tile = tokens
     if (kind == 1) {
+      // the slots hold kPartialEmpty from the preceding kernel: overwrite
+      // them only once that kernel has completed
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       float* part = p.partials + static_cast<long long>(cta) * p.M * kDecRows;
 #pragma unroll
       for (int i = 0; i < kTiles; ++i)
@@ -755,17 +769,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
               const int m = nt * 8 + 2 * q + c;
-              if (m < p.M) __stcg(part + m * kDecRows + row, acc[i][nt][2 * h + c]);
+              if (m < p.M) st_relaxed_gpu(part + m * kDecRows + row, acc[i][nt][2 * h + c]);
             }
         }
-      // every writer fences its stores, then one thread raises this CTA's flag
-      // (after the rank kernel, which zeroed the flags, has completed)
-      __threadfence();
-      named_bar_sync(4, 32 * kRowGroups);
-      if (rg == 0 && lane == 0) {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        st_release_gpu(p.flags + cta, 1u);
-      }
       continue;
     }
     // whole: the rank term from rt (cycled with the rank warp); finish: the
@@ -807,13 +813,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 // slices in order.
 __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ a, int M, int K, int r,
-    int kslice, float scale, float* __restrict__ st, uint32_t* __restrict__ counters,
-    int n_counters) {
+    int kslice, float scale, float* __restrict__ st, float4* __restrict__ partials,
+    int n_partials4) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  // the decode kernel's split counters (it waits for this grid before its
-  // first ticket, so zeroing here needs no separate memset)
-  if (blockIdx.x == 0 && blockIdx.y == 0)
-    for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
+  // the decode kernel's partial slots to kPartialEmpty (it overwrites them
+  // only after this grid has completed)
+  {
+    const float e = __uint_as_float(kPartialEmpty);
+    const int nb = gridDim.x * gridDim.y, b = blockIdx.y * gridDim.x + blockIdx.x;
+    for (int i = b * kRankThreads + threadIdx.x; i < n_partials4; i += nb * kRankThreads)
+      partials[i] = make_float4(e, e, e, e);
+  }
   __shared__ float red[kRankThreads / 32][kMaxTok];
   const int j = blockIdx.x, split = blockIdx.y;
   const int k0 = split * kslice, k1 = min(K, k0 + kslice);
@@ -861,12 +871,15 @@ __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
   }
 }
 
-// Zeroes the decode kernel's partial flags when no rank kernel precedes it
-// (plain weights, no LoRA term), and lets the decode kernel start at once as
-// its programmatic dependent.
-__global__ void __launch_bounds__(256) lora_flags_zero_kernel(uint32_t* __restrict__ flags, int n) {
+// Sets the decode kernel's partial slots to kPartialEmpty when no rank
+// kernel precedes it (plain weights, no LoRA term), and lets the decode
+// kernel start at once as its programmatic dependent.
+__global__ void __launch_bounds__(256) lora_partials_fill_kernel(float4* __restrict__ partials,
+                                                                 int n4) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  for (int i = threadIdx.x; i < n; i += blockDim.x) flags[i] = 0u;
+  const float e = __uint_as_float(kPartialEmpty);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x)
+    partials[i] = make_float4(e, e, e, e);
 }
 
 int bits_of(int scheme) { return scheme == 0 ? 16 : (scheme == kINT8 ? 8 : 4); }
@@ -941,7 +954,6 @@ int launch_decode_typed(const GemvArgs& a, const DecodeConfig& cfg, cudaStream_t
   p.y = static_cast<__nv_bfloat16*>(a.y);
   p.ldy = a.ldy > 0 ? a.ldy : a.N;
   p.partials = a.partials;
-  p.flags = a.flags;
   p.M = static_cast<int>(a.M);
   p.N = static_cast<int>(a.N);
   p.K = static_cast<int>(a.K);
@@ -1020,7 +1032,7 @@ DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t 
   c.ctas = static_cast<int>(ctas);
   c.stages = stages;
   c.smem = dec_layout(scheme, M, r, g, stages).bytes;
-  // some row block is shared between CTAs (then partials and flags are used)
+  // some row block is shared between CTAs (then the partial slots are used)
   c.split_blocks = false;
   for (int64_t j = 1; j < ctas && !c.split_blocks; ++j)
     if ((units * j / ctas) % S != 0) c.split_blocks = true;
@@ -1037,8 +1049,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
     set_error("decode: shared memory for rank " + std::to_string(a.r) + " exceeds the limit");
     return MLORA_ERR_UNSUPPORTED;
   }
-  if (cfg.split_blocks && (a.flags == nullptr || a.partials == nullptr)) {
-    set_error("decode: workspace without partials and flags for a split row block");
+  if (cfg.split_blocks && a.partials == nullptr) {
+    set_error("decode: workspace without partials for a split row block");
     return MLORA_ERR_INVALID_ARG;
   }
   switch (a.scheme) {
@@ -1050,12 +1062,15 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   }
 }
 
-int launch_flags_zero(uint32_t* flags, int64_t n, cudaStream_t s) {
+int launch_partials_fill(float* partials, int64_t n, cudaStream_t s) {
   LaunchScope scope(kKindGemv, s);
-  lora_flags_zero_kernel<<<1, 256, 0, s>>>(flags, static_cast<int>(n));
+  const int64_t n4 = n / 4;
+  const int blocks = static_cast<int>(std::min<int64_t>(32, (n4 + 255) / 256));
+  lora_partials_fill_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(
+      reinterpret_cast<float4*>(partials), static_cast<int>(n4));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
-    set_error(std::string("flags_zero launch: ") + cudaGetErrorString(e));
+    set_error(std::string("partials_fill launch: ") + cudaGetErrorString(e));
     return MLORA_ERR_CUDA;
   }
   return MLORA_OK;
@@ -1067,7 +1082,7 @@ int rank_small_splits(int64_t K) {
 }
 
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
-                      float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s) {
+                      float* st, float* partials, int64_t n_partials, cudaStream_t s) {
   // same shared-memory carveout as the decode kernel that follows, so SMs
   // need no reconfiguration between the two (a hint, set once per device)
   static std::atomic<bool> carve_set[64];
@@ -1088,8 +1103,9 @@ int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_
                            s>>>(static_cast<const __nv_bfloat16*>(x),
                                 static_cast<const __nv_bfloat16*>(a), static_cast<int>(M),
                                 static_cast<int>(K), static_cast<int>(r),
-                                static_cast<int>(kslice), scale, st, counters,
-                                static_cast<int>(n_counters));
+                                static_cast<int>(kslice), scale, st,
+                                reinterpret_cast<float4*>(partials),
+                                static_cast<int>(n_partials / 4));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("rank_small launch: ") + cudaGetErrorString(e));

@@ -118,8 +118,8 @@ struct GemvArgs {
   const void* b = nullptr;       // bf16 [N, r] or nullptr
   const float* st = nullptr;     // fp32 [rank_small_splits(K), M, r] partials of s.x.A^T
   void* y = nullptr;             // bf16 [M, N]
-  float* partials = nullptr;     // [ctas, M, 128]: one partial row block per CTA
-  uint32_t* flags = nullptr;     // [ctas] zeroed (partial published)
+  float* partials = nullptr;     // [ctas, M, 128]: one partial row block per CTA, set to the
+                                 // empty pattern by the kernel before (rank or fill kernel)
   int64_t M = 0, N = 0, K = 0, r = 0, group = 64;
   int64_t ldy = 0;  // row stride of y (0: N)
   bool pdl = false;  // launched as the programmatic dependent of the kernel before it
@@ -138,12 +138,13 @@ DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t 
 int64_t gemv_row_blocks(int64_t N);
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 int rank_small_splits(int64_t K);
-// sT partials for the decode path; also zeroes the decode kernel's n_counters
-// partial flags.
+// sT partials for the decode path; also sets the decode kernel's n_partials
+// partial-slot floats (a multiple of 4) to their empty pattern.
 int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_t r, float scale,
-                      float* st, uint32_t* counters, int64_t n_counters, cudaStream_t s);
-// Zeroes n partial flags (decode without a rank kernel before it).
-int launch_flags_zero(uint32_t* flags, int64_t n, cudaStream_t s);
+                      float* st, float* partials, int64_t n_partials, cudaStream_t s);
+// Sets n partial-slot floats to their empty pattern (decode without a rank
+// kernel before it).
+int launch_partials_fill(float* partials, int64_t n, cudaStream_t s);
 
 // ------------------------------------------------------- rank projection -----
 // out[m, j] = scale * sum_k X[m, k] * L[j, k] for j < R (L rows >= r are zero).

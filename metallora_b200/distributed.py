@@ -119,6 +119,78 @@ def average_gradients(flat_grad: torch.Tensor, group=None) -> None:
                                f"{str(e).splitlines()[0] if str(e) else type(e).__name__}") from e
 
 
+class PeerLiveness:
+    """Step-by-step membership check through the process group's key-value
+    store, on the host.
+
+    Before a rank launches a step's collectives it records that it reached the
+    step (``beat``) and waits, bounded by ``timeout_s``, until every peer has
+    reached it too (``check``).  A peer that leaves between steps says so first
+    (``leave``).  The survivors then raise DistributedError at their next
+    check, before they enqueue anything, so no GPU kernel or NCCL collective is
+    ever left waiting for a rank that is gone.  A peer that stops without
+    saying so (a crash, a stall) surfaces as the same error once ``timeout_s``
+    has passed.
+
+    Each instance uses its own key prefix.  Instances must be created in the
+    same order on every rank, as collectives are."""
+
+    _count = 0
+
+    def __init__(self, group=None, timeout_s: float = 30.0, store=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.ranks = ([dist.get_global_rank(group, r) for r in range(self.world)]
+                      if group is not None else list(range(self.world)))
+        self.store = store if store is not None else dist.distributed_c10d._get_default_store()
+        self.timeout_s = float(timeout_s)
+        PeerLiveness._count += 1
+        self.prefix = f"mlora/live/{PeerLiveness._count}"
+
+    def _hb(self, r: int) -> str:
+        return f"{self.prefix}/hb/{self.ranks[r]}"
+
+    def _left(self, r: int) -> str:
+        return f"{self.prefix}/left/{self.ranks[r]}"
+
+    def beat(self, step: int) -> None:
+        """This rank has reached ``step`` (about to launch its collectives)."""
+        self.store.set(self._hb(self.rank), str(int(step)))
+
+    def leave(self) -> None:
+        """This rank leaves the group between steps; its peers' next check
+        raises instead of waiting for it."""
+        self.store.set(self._left(self.rank), "1")
+
+    def check(self, step: int) -> None:
+        """Returns once every peer has reached ``step``; raises
+        DistributedError if one has left, or has not arrived within
+        ``timeout_s``."""
+        import time
+        peers = [r for r in range(self.world) if r != self.rank]
+        deadline = time.monotonic() + self.timeout_s
+        pause = 1e-4
+        while peers:
+            left = [r for r in peers if self.store.check([self._left(r)])]
+            if left:
+                raise DistributedError(
+                    f"rank {self.ranks[left[0]]} left the process group before step {step} "
+                    f"(seen by rank {self.ranks[self.rank]})")
+            peers = [r for r in peers
+                     if not (self.store.check([self._hb(r)]) and
+                             int(self.store.get(self._hb(r))) >= step)]
+            if not peers:
+                return
+            if time.monotonic() > deadline:
+                raise DistributedError(
+                    f"rank {self.ranks[peers[0]]} did not reach step {step} within "
+                    f"{self.timeout_s:.1f} s (left or stalled; seen by rank "
+                    f"{self.ranks[self.rank]})")
+            time.sleep(pause)
+            pause = min(pause * 2, 0.01)
+
+
 def replicas_in_sync(t: torch.Tensor, group=None) -> bool:
     """True when every rank holds a bitwise-identical copy of ``t`` (checked
     through an all-gathered checksum)."""

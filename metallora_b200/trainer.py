@@ -18,7 +18,12 @@ array that the backward kernels accumulate into.  The clip is then one
 reduction kernel and AdamW one kernel launch for all adapters.  Under data
 parallelism the gradient array is averaged over the ranks in per-layer buckets
 (NCCL on a side stream), each started as soon as the backward has written it,
-so the exchange overlaps the backward of the layers before it.
+so the exchange overlaps the backward of the layers before it.  Data-parallel
+replicas start from the first rank's factors (broadcast at construction), and
+each step first checks on the host, through the process group's store, that
+every peer reached it (``PeerLiveness``): a rank that leaves between steps
+(``LoRATrainer.leave``) or stops turns the others' next step into a
+DistributedError before any collective of that step is launched.
 """
 from __future__ import annotations
 
@@ -33,7 +38,7 @@ import torch.distributed as dist
 from torch import nn
 
 from . import kernels as _k
-from .distributed import BucketedGradExchange, average_gradients
+from .distributed import BucketedGradExchange, PeerLiveness, average_gradients
 from .exceptions import ConfigurationError
 from .layers import LoRALinear
 from .logging import logger
@@ -270,7 +275,8 @@ class LoRATrainer:
     """LoRA trainer (reference: trainer.py:173-302)."""
 
     def __init__(self, model: nn.Module, config: TrainingConfig | None = None,
-                 process_group=None, overlap_grad_exchange: bool = True):
+                 process_group=None, overlap_grad_exchange: bool = True,
+                 liveness_timeout: float | None = 30.0):
         self.config = config or TrainingConfig()
         c = self.config
         if not any(isinstance(m, LoRALinear) for m in model.modules()):
@@ -288,9 +294,21 @@ class LoRATrainer:
         # while the backward of earlier layers runs (None: one all-reduce of
         # the flat buffer after the backward)
         self.exchange = None
-        if overlap_grad_exchange and dist.is_available() and dist.is_initialized() and \
-                dist.get_world_size(process_group) > 1:
+        data_parallel = dist.is_available() and dist.is_initialized() and \
+            dist.get_world_size(process_group) > 1
+        if data_parallel:
+            # every replica starts from the first rank's LoRA factors (as
+            # DistributedDataParallel does), so averaged gradients keep them equal
+            src = dist.get_global_rank(process_group, 0) if process_group is not None else 0
+            dist.broadcast(self.params.master, src=src, group=process_group)
+            self.params.refresh_compute()
+        if overlap_grad_exchange and data_parallel:
             self.exchange = self.params.attach_exchange(process_group)
+        # data parallel: every training step first checks on the host that all
+        # peers reached it (None: no check; a departed peer then surfaces as a
+        # collective timeout)
+        self.liveness = (PeerLiveness(process_group, liveness_timeout)
+                         if data_parallel and liveness_timeout is not None else None)
         self._clip = torch.ones(2, dtype=torch.float32, device=self.params.master.device)
         Path(c.output_dir).mkdir(parents=True, exist_ok=True)
 
@@ -341,8 +359,17 @@ class LoRATrainer:
         else:
             self.optimizer.update(None)
 
+    def leave(self) -> None:
+        """Leaves data-parallel training between steps: the other ranks' next
+        step raises DistributedError before it launches anything."""
+        if self.liveness is not None:
+            self.liveness.leave()
+
     def _training_step(self, batch: dict[str, torch.Tensor]) -> dict[str, float]:
         """trainer.py:228-249 (loss returned as a float, as the reference does)."""
+        if self.liveness is not None:
+            self.liveness.beat(self._micro)
+            self.liveness.check(self._micro)
         loss = self.backward(batch)
         self._micro += 1
         if self._micro % max(1, self.config.gradient_accumulation_steps) == 0:

@@ -218,3 +218,62 @@ def test_gloo_bucketed_exchange():
             want += [1.5 * (i + 1) + step] * n  # mean over ranks of (rank+1)(i+1)+step
         assert r0[f"flat{step}"] == want and res[1][f"flat{step}"] == want
     assert r0["disarmed_fired"] == [] and r0["double"] == "error"
+
+
+def _live_worker(rank, world, port, q, mode):
+    from metallora_b200.distributed import PeerLiveness
+    from metallora_b200.exceptions import DistributedError
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=30))
+    live = PeerLiveness(timeout_s=3.0)
+    for step in range(3):  # all present: every check returns
+        live.beat(step)
+        live.check(step)
+    if rank == 1:
+        if mode == "leave":
+            live.leave()
+        q.put((rank, "gone", 0.0))
+        q.close()
+        q.join_thread()  # the message is written before the process goes
+        if mode == "stall":
+            __import__("time").sleep(8.0)  # alive, but never reaches step 3
+        os._exit(0)
+    t0 = __import__("time").monotonic()
+    try:
+        live.beat(3)
+        live.check(3)
+        out = "no error"
+    except DistributedError as e:
+        out = "left" if "left the process group" in str(e) else "timeout"
+    q.put((rank, out, __import__("time").monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["leave", "stall"])
+def test_peer_liveness(mode):
+    """Host-side membership check: a peer that leaves between steps is seen
+    at once by the survivor's next check; one that stops without a word is
+    reported after the check's timeout.  Nothing waits on a collective."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_live_worker, args=(r, world, port, q, mode))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = {r: (s, t) for r, s, t in (q.get(timeout=120) for _ in range(world))}
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    assert res[1][0] == "gone"
+    if mode == "leave":
+        assert res[0][0] == "left" and res[0][1] < 2.0
+    else:
+        assert res[0][0] == "timeout" and 2.5 < res[0][1] < 10.0

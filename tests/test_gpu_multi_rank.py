@@ -5,9 +5,10 @@ least two GPUs (skipped otherwise):
   side stream while the backward runs leave the replicas bitwise identical,
   and the averaged gradient equals the mean of both ranks' own gradients;
 * failure detection without a GPU fault: rank 1 leaves between steps (after a
-  synchronize, with nothing of its own in flight); rank 0's next step ends
-  with DistributedError within the short process-group timeout instead of
-  hanging, and its process exits.
+  synchronize, with nothing of its own in flight) and says so through the
+  process group's store; rank 0's next step raises DistributedError from its
+  host-side liveness check, before it launches any kernel or collective of
+  that step, and its process exits.
 
 NVLS is off (NCCL_NVLS_ENABLE=0) and no symmetric memory is used, so no
 NVLink multicast object is bound when a rank leaves."""
@@ -59,8 +60,9 @@ def _worker(rank, world, port, q, mode):
         model = _model(dev)
         cfg = TrainingConfig(rank=16, alpha=32.0, learning_rate=1e-3, max_grad_norm=0.0,
                              output_dir=f"/tmp/mlora_mr_{rank}")
-        tr = LoRATrainer(model, cfg)
+        tr = LoRATrainer(model, cfg, liveness_timeout=20.0)
         assert tr.exchange is not None
+        res["init_in_sync"] = replicas_in_sync(tr.params.master)
         g = torch.Generator(device=dev).manual_seed(100 + rank)  # each rank its own shard
         batch = {"input_ids": torch.randn(2, 64, 256, device=dev, generator=g).to(torch.bfloat16),
                  "target_output": torch.randn(2, 64, 256, device=dev, generator=g).to(torch.bfloat16)}
@@ -68,6 +70,7 @@ def _worker(rank, world, port, q, mode):
         tr.backward(batch)
         tr.exchange.finish()
         avg = tr.params.grad.clone()
+        res["avg_in_sync"] = replicas_in_sync(avg)
         tr.params.grad.zero_()
         tr.exchange.armed = False  # this rank's own gradient, not exchanged
         tr._compute_loss(batch).backward()
@@ -77,14 +80,19 @@ def _worker(rank, world, port, q, mode):
         dist.all_gather(both, own)
         mean = sum(both) / world
         res["avg_rel_err"] = float((avg - mean).norm() / mean.norm())
+        res["step_in_sync"] = []
         for _ in range(2):
             tr._training_step(batch)
+            res["step_in_sync"].append(replicas_in_sync(tr.params.master))
         res["in_sync"] = replicas_in_sync(tr.params.master)
         torch.cuda.synchronize()
         if mode == "leave":
             if rank == 1:
+                tr.leave()  # tells the peers through the store, then goes
                 res["status"] = "left"
                 q.put(res)
+                q.close()
+                q.join_thread()  # the report is written before the process goes
                 os._exit(0)  # between steps: nothing of this rank is in flight
             t0 = time.monotonic()
             try:
@@ -101,6 +109,8 @@ def _worker(rank, world, port, q, mode):
         q.put(res)
     finally:
         if mode == "leave":
+            q.close()
+            q.join_thread()  # the report is written before the process goes
             os._exit(0)  # the survivor's communicator is gone with its process
         dist.destroy_process_group()
 
@@ -139,8 +149,9 @@ def test_two_rank_bucketed_exchange_keeps_replicas_in_sync(cuda):
     assert not hung
     for r in (0, 1):
         assert "status" not in res[r], res[r]
-        assert res[r]["in_sync"] is True
-        assert res[r]["avg_rel_err"] < 1e-6
+        assert res[r]["init_in_sync"] and res[r]["avg_in_sync"], res[r]
+        assert res[r]["avg_rel_err"] < 1e-6, res[r]
+        assert res[r]["in_sync"] is True, res[r]
 
 
 def test_rank_leaving_between_steps_raises_on_survivor(cuda):
