@@ -531,13 +531,17 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
     drained = [torch.cuda.Event() for _ in range(2)]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
+    chunks = max(1, args.e2e_chunks)
+    rows = [(M * c // chunks, M * (c + 1) // chunks) for c in range(chunks)]
+
     def load(i):
         b = i % 2
         with torch.cuda.stream(copy):
             if i >= 2:  # buffer b was the input of step i - 2
                 copy.wait_event(done[b])
-            xd[b].copy_(xh[b], non_blocking=True)
-            dyd[b].copy_(dyh[b], non_blocking=True)
+            for r0, r1 in rows:  # in row chunks, interleaved with the other direction
+                xd[b][r0:r1].copy_(xh[b][r0:r1], non_blocking=True)
+                dyd[b][r0:r1].copy_(dyh[b][r0:r1], non_blocking=True)
             loaded[b].record(copy)
 
     torch.cuda.synchronize()
@@ -571,8 +575,9 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
             drain.wait_event(done[b])
             for t in (y, dx, *(src for _, src in grads)):
                 t.record_stream(drain)
-            outs["y"][b].copy_(y.detach(), non_blocking=True)
-            outs["dx"][b].copy_(dx, non_blocking=True)
+            for r0, r1 in rows:
+                outs["y"][b][r0:r1].copy_(y.detach()[r0:r1], non_blocking=True)
+                outs["dx"][b][r0:r1].copy_(dx[r0:r1], non_blocking=True)
             for dst, src in grads:
                 dst.copy_(src, non_blocking=True)
             drained[b].record(drain)
@@ -590,6 +595,7 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
     return {"value": round(world * M * steps / (ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "ms_per_step": round(ms / steps, 4),
+            "copy_chunks": chunks,
             "path": "LoRALinear forward+backward, pinned host buffers, H2D and D2H on their "
                     "own streams overlapped with compute" +
                     (("; LoRA gradients averaged by the " +
@@ -1058,6 +1064,8 @@ def main():
                          "(fp32, NF4, INT4/INT8 at N=1; the NF4 stack at every N)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="--workload stack: one flat all-reduce after the backward")
+    ap.add_argument("--e2e-chunks", type=int, default=1,
+                    help="e2e leg: host<->device copies in this many row chunks per tensor")
     ap.add_argument("--exchange-after", dest="exchange_overlap", action="store_false",
                     help="headline at N > 1: run the peer gradient exchange after the "
                          "backward instead of beside the dx GEMM")

@@ -123,14 +123,15 @@ class PeerLiveness:
     """Step-by-step membership check through the process group's key-value
     store, on the host.
 
-    Before a rank launches a step's collectives it records that it reached the
-    step (``beat``) and waits, bounded by ``timeout_s``, until every peer has
-    reached it too (``check``).  A peer that leaves between steps says so first
-    (``leave``).  The survivors then raise DistributedError at their next
-    check, before they enqueue anything, so no GPU kernel or NCCL collective is
-    ever left waiting for a rank that is gone.  A peer that stops without
-    saying so (a crash, a stall) surfaces as the same error once ``timeout_s``
-    has passed.
+    Before a rank launches a step's collectives it counts itself in for the
+    step (``beat``) and waits, bounded by ``timeout_s``, until every rank of the
+    group has been counted (``check``).  A peer that leaves between steps says
+    so first (``leave``).  The survivors then raise DistributedError at their
+    next check, before they enqueue anything, so no GPU kernel or NCCL
+    collective is ever left waiting for a rank that is gone.  A peer that stops
+    without saying so (a crash, a stall) surfaces as the same error once
+    ``timeout_s`` has passed.  A step costs one atomic add and a few
+    polls of the store, whatever the group size.
 
     Each instance uses its own key prefix.  Instances must be created in the
     same order on every rank, as collectives are."""
@@ -141,52 +142,48 @@ class PeerLiveness:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.ranks = ([dist.get_global_rank(group, r) for r in range(self.world)]
-                      if group is not None else list(range(self.world)))
+        self.global_rank = (dist.get_global_rank(group, self.rank) if group is not None
+                            else self.rank)
         self.store = store if store is not None else dist.distributed_c10d._get_default_store()
         self.timeout_s = float(timeout_s)
         PeerLiveness._count += 1
         self.prefix = f"mlora/live/{PeerLiveness._count}"
 
-    def _hb(self, r: int) -> str:
-        return f"{self.prefix}/hb/{self.ranks[r]}"
-
-    def _left(self, r: int) -> str:
-        return f"{self.prefix}/left/{self.ranks[r]}"
-
     def beat(self, step: int) -> None:
         """This rank has reached ``step`` (about to launch its collectives)."""
-        self.store.set(self._hb(self.rank), str(int(step)))
+        self.store.add(f"{self.prefix}/arrived/{int(step)}", 1)
 
     def leave(self) -> None:
         """This rank leaves the group between steps; its peers' next check
         raises instead of waiting for it."""
-        self.store.set(self._left(self.rank), "1")
+        self.store.set(f"{self.prefix}/left_rank", str(self.global_rank))
+        self.store.add(f"{self.prefix}/left", 1)
 
     def check(self, step: int) -> None:
-        """Returns once every peer has reached ``step``; raises
+        """Returns once every rank has reached ``step``; raises
         DistributedError if one has left, or has not arrived within
         ``timeout_s``."""
         import time
-        peers = [r for r in range(self.world) if r != self.rank]
+        key = f"{self.prefix}/arrived/{int(step)}"
         deadline = time.monotonic() + self.timeout_s
         pause = 1e-4
-        while peers:
-            left = [r for r in peers if self.store.check([self._left(r)])]
-            if left:
+        while True:
+            if self.store.add(f"{self.prefix}/left", 0) > 0:
+                who = self.store.get(f"{self.prefix}/left_rank").decode()
                 raise DistributedError(
-                    f"rank {self.ranks[left[0]]} left the process group before step {step} "
-                    f"(seen by rank {self.ranks[self.rank]})")
-            peers = [r for r in peers
-                     if not (self.store.check([self._hb(r)]) and
-                             int(self.store.get(self._hb(r))) >= step)]
-            if not peers:
+                    f"rank {who} left the process group before step {step} "
+                    f"(seen by rank {self.global_rank})")
+            n = self.store.add(key, 0)
+            if n >= self.world:
+                if self.rank == 0 and step > 0:
+                    # every rank has finished polling the previous step's count
+                    self.store.delete_key(f"{self.prefix}/arrived/{int(step) - 1}")
                 return
             if time.monotonic() > deadline:
                 raise DistributedError(
-                    f"rank {self.ranks[peers[0]]} did not reach step {step} within "
-                    f"{self.timeout_s:.1f} s (left or stalled; seen by rank "
-                    f"{self.ranks[self.rank]})")
+                    f"only {n} of {self.world} ranks reached step {step} within "
+                    f"{self.timeout_s:.1f} s (a rank left or stalled; seen by rank "
+                    f"{self.global_rank})")
             time.sleep(pause)
             pause = min(pause * 2, 0.01)
 

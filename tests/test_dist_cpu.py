@@ -245,7 +245,7 @@ def _live_worker(rank, world, port, q, mode):
         live.check(3)
         out = "no error"
     except DistributedError as e:
-        out = "left" if "left the process group" in str(e) else "timeout"
+        out = "left" if "left the process group" in str(e) else ("timeout" if "reached step" in str(e) else str(e))
     q.put((rank, out, __import__("time").monotonic() - t0))
     q.close()
     q.join_thread()
