@@ -21,6 +21,10 @@
 //               128-byte-swizzled layout UMMA reads (2-stage ring).  For the
 //               rank block they copy B (forward) or A (backward) rows instead.
 // Every wait is bounded (see ptx.cuh).
+#include <algorithm>
+#include <cstdlib>
+#include <string>
+
 #include "internal.h"
 #include "ptx.cuh"
 #include "quant.cuh"
@@ -415,6 +419,366 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (M >= 256): a (2,1,1) cluster computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2, as the dense pair GEMM does.  Each CTA stages its
+// own 128 rows of X and dequantises only its own 128 rows (forward) or output
+// columns (backward) of the weight tile, so per SM the dequantisers convert
+// half as many weights per k-block as in the one-CTA kernel, while the pair
+// MMA reads half of B from each SM.  The dequantisers work in four groups on
+// four k-blocks at once (one W stage each).  NF4 11008 x 4096, r 64: 0.53 ms
+// at 4096 tokens and 0.103 ms at 512 (one-CTA kernel: 0.926 / 0.215 ms); the
+// staged path (one dequantisation pass, then the dense pair GEMM) remains
+// faster (0.29 / 0.078 ms): ~3.5 instructions per weight on 8 warps do not
+// keep up with the pair MMA's 540 cycles per k-block.
+//   even CTA: producer arms x_full[s] for both CTAs' X bytes; warp 1 issues the
+//             MMAs once both CTAs' dequantisers have arrived on w_full[s], and
+//             commits to both CTAs' x_empty / w_empty / acc_full.
+//   odd CTA:  X copies complete on the even CTA's x_full; its dequantisers
+//             arrive on the even CTA's w_full.
+// Raw codes and scales go to each CTA's own ring, on its own barriers.
+constexpr int kPHalf = 128;
+constexpr int kPStagesX = 6;
+constexpr int kPStagesW = 4;  // one per dequantiser group
+constexpr int kPStagesR = 4;
+constexpr uint32_t kPXBytes = kPHalf * kBK * 2;  // 16 KB
+constexpr uint32_t kPWBytes = kPHalf * kBK * 2;  // 16 KB
+
+template <int kScheme>
+struct QPairTraits {
+  static constexpr int kBits = kScheme == kINT8 ? 8 : 4;
+  // forward [128 rows x 64 k] or backward [64 rows x 128 columns] of codes
+  static constexpr uint32_t kCodeBytes = kPHalf * kBK * kBits / 8;
+  static constexpr uint32_t kScaleBytes = 1024;
+  static constexpr uint32_t kRawBytes = kCodeBytes + kScaleBytes;
+};
+
+template <int kScheme>
+constexpr size_t pair_smem_bytes() {
+  return 1024 + kPStagesX * kPXBytes + kPStagesW * kPWBytes +
+         kPStagesR * QPairTraits<kScheme>::kRawBytes + 512;
+}
+
+template <int kScheme, bool kWMN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    qlora_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
+                           const __grid_constant__ CUtensorMap tm_x2,
+                           const __grid_constant__ CUtensorMap tm_codes,
+                           const __grid_constant__ CUtensorMap tm_scales, const QGemmParams p) {
+  using Tr = QPairTraits<kScheme>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem<1024>(smem_raw);
+  uint8_t* xs = smem;
+  uint8_t* ws = xs + kPStagesX * kPXBytes;
+  uint8_t* rs = ws + kPStagesW * kPWBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs + kPStagesR * Tr::kRawBytes);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = x_full + kPStagesX;
+  uint64_t* r_full = x_empty + kPStagesX;
+  uint64_t* r_empty = r_full + kPStagesR;
+  uint64_t* w_full = r_empty + kPStagesR;
+  uint64_t* w_empty = w_full + kPStagesW;
+  uint64_t* acc_full = w_empty + kPStagesW;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  float* lut = reinterpret_cast<float*>(tmem_slot + 4);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t crank = cluster_ctarank();
+  const bool lead = crank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStagesX; ++s) mbar_init(&x_full[s], 1), mbar_init(&x_empty[s], 1);
+    for (int s = 0; s < kPStagesR; ++s) mbar_init(&r_full[s], 1), mbar_init(&r_empty[s], 1);
+    // the even CTA's w_full counts one arrival from each CTA's dequantisers
+    for (int s = 0; s < kPStagesW; ++s) mbar_init(&w_full[s], 2), mbar_init(&w_empty[s], 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&acc_full[b], 1), mbar_init(&acc_empty[b], 2 * kEpiWarps);
+    mbar_init(drain_bar, 1);
+    fence_mbarrier_init();
+  }
+  if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_codes);
+    prefetch_tmap(&tm_scales);
+    if (p.num_kb_extra > 0) prefetch_tmap(&tm_x2);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_kb = p.num_kb_main + p.num_kb_extra;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (elect_one()) {
+      const uint32_t lead_xfull = mapa_shared(smem_u32(x_full), 0);
+      uint32_t sx = 0, px = 0, sr = 0, pr = 0;
+      bool armed_x[kPStagesX], armed_r[kPStagesR];
+      uint32_t par_x[kPStagesX], par_r[kPStagesR];
+      for (int s = 0; s < kPStagesX; ++s) armed_x[s] = false, par_x[s] = 0;
+      for (int s = 0; s < kPStagesR; ++s) armed_r[s] = false, par_r[s] = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+        const int m0 = (tile / p.tiles_n) * (2 * kPHalf) + static_cast<int>(crank) * kPHalf;
+        const int c0 = (tile % p.tiles_n) * (2 * kPHalf) + static_cast<int>(crank) * kPHalf;
+        for (int kb = 0; kb < total_kb && ok; ++kb) {
+          const bool extra = kb >= p.num_kb_main;
+          if (!mbar_wait(&x_empty[sx], px ^ 1u, p.status, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (lead) {
+            mbar_arrive_expect_tx(&x_full[sx], 2 * kPXBytes);
+            armed_x[sx] = true;
+            par_x[sx] = px;
+          }
+          const int k0 = (extra ? kb - p.num_kb_main : kb) * kBK;
+          tma_load_2d_pair(xs + sx * kPXBytes, extra ? &tm_x2 : &tm_x, lead_xfull + sx * 8u, k0,
+                           m0);
+          if (++sx == kPStagesX) sx = 0, px ^= 1u;
+          if (extra) continue;
+          if (!mbar_wait(&r_empty[sr], pr ^ 1u, p.status, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* raw = rs + sr * Tr::kRawBytes;
+          mbar_arrive_expect_tx(&r_full[sr], Tr::kCodeBytes + p.scale_box_bytes);
+          armed_r[sr] = true;
+          par_r[sr] = pr;
+          if constexpr (kWMN) {
+            // rows: the reduction index in [kb*64, kb*64+64); this CTA's 128 output columns
+            tma_load_2d(raw, &tm_codes, &r_full[sr], c0 * Tr::kBits / 8, kb * kBK);
+            tma_load_2d(raw + Tr::kCodeBytes, &tm_scales, &r_full[sr], kb * kBK, c0 / p.group);
+          } else {
+            tma_load_2d(raw, &tm_codes, &r_full[sr], kb * kBK * Tr::kBits / 8, c0);
+            tma_load_2d(raw + Tr::kCodeBytes, &tm_scales, &r_full[sr], c0, (kb * kBK) / p.group);
+          }
+          if (++sr == kPStagesR) sr = 0, pr ^= 1u;
+        }
+      }
+      // never leave a copy in flight at exit (the even CTA's x_full counts
+      // both CTAs' X bytes; the raw copies land on this CTA's own barriers)
+      for (int s = 0; s < kPStagesX; ++s)
+        if (armed_x[s]) mbar_wait(&x_full[s], par_x[s], p.status, kDevTimeoutDrain);
+      for (int s = 0; s < kPStagesR; ++s)
+        if (armed_r[s]) mbar_wait(&r_full[s], par_r[s], p.status, kDevTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------- MMA (even CTA only) --
+    if (lead && elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(2 * kPHalf, 2 * kPHalf, false, kWMN, true);
+      const uint32_t peer_xempty = mapa_shared(smem_u32(x_empty), 1);
+      const uint32_t peer_wempty = mapa_shared(smem_u32(w_empty), 1);
+      const uint32_t peer_acc_full = mapa_shared(smem_u32(acc_full), 1);
+      uint32_t sx = 0, px = 0, sw = 0, pw = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs, ++local) {
+        const uint32_t buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
+        if (!mbar_wait(&acc_empty[buf], use ^ 1u, p.status, kDevTimeoutAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&x_full[sx], px, p.status, kDevTimeoutFull) ||
+              !mbar_wait(&w_full[sw], pw, p.status, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sxa = smem_u32(xs + sx * kPXBytes);
+          const uint32_t swa = smem_u32(ws + sw * kPWBytes);
+          int nk = 4;
+          if (kb >= p.num_kb_main) {
+            const int rem = p.R - (kb - p.num_kb_main) * kBK;
+            nk = rem >= kBK ? 4 : rem / 16;
+          }
+          for (int k = 0; k < nk; ++k) {
+            uint64_t bd;
+            if constexpr (kWMN)
+              bd = desc_mnmajor_sw128(swa, k, kMNBoxBytes);
+            else
+              bd = desc_kmajor_sw128(swa, k);
+            umma_f16_pair(d_tmem, desc_kmajor_sw128(sxa, k), bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(smem_u32(&x_empty[sx]));
+          umma_commit_pair(peer_xempty + sx * 8u);
+          umma_commit_pair(smem_u32(&w_empty[sw]));
+          umma_commit_pair(peer_wempty + sw * 8u);
+          if (++sx == kPStagesX) sx = 0, px ^= 1u;
+          if (++sw == kPStagesW) sw = 0, pw ^= 1u;
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&acc_full[buf]));
+        umma_commit_pair(peer_acc_full + buf * 8u);
+      }
+      // every MMA issued above has completed before TMEM is released
+      umma_commit_pair(smem_u32(drain_bar));
+      mbar_wait(drain_bar, 0, p.status, kDevTimeoutDrain);
+    }
+  } else if (warp < 2 + kEpiWarps) {
+    // ----------------------------------------------------------- epilogue --
+    const uint32_t quarter = warp & 3u;
+    const uint32_t row = quarter * 32 + lane;
+    const uint32_t lead_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
+    const int vec = (p.N % 8 == 0 && p.ldd % 8 == 0) ? 1 : 0;
+    int local = 0;
+    for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++local) {
+      const uint32_t buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
+      if (!mbar_wait(&acc_full[buf], use, p.status, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const int m = (tile / p.tiles_n) * (2 * kPHalf) + static_cast<int>(crank) * kPHalf +
+                    static_cast<int>(row);
+      const int n_base = (tile % p.tiles_n) * (2 * kPHalf);
+      __nv_bfloat16* out_row =
+          reinterpret_cast<__nv_bfloat16*>(p.d) + static_cast<long long>(m) * p.ldd + n_base;
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (m < p.M) {
+          const int n0 = n_base + c * 32;
+          if (!vec) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n0 + i < p.N) out_row[c * 32 + i] = __float2bfloat16_rn(__uint_as_float(r[i]));
+            continue;
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack2<__nv_bfloat16>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (n0 + q * 8 < p.N)
+              *reinterpret_cast<uint4*>(out_row + c * 32 + q * 8) =
+                  make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_acc_empty + buf * 8u);
+    }
+  } else {
+    // -------------------------------------------------------- dequantisers --
+    // Four groups of two warps; group g converts the k-blocks whose running
+    // index is g (mod 4), always into W stage g, so four k-blocks are in
+    // conversion at once.  Each of a group's 64 threads converts two 64-weight
+    // rows: forward rows u and u + 64 of this CTA's 128; backward row u of both
+    // 64-column boxes.
+    const uint32_t t = threadIdx.x - (64 + 32 * kEpiWarps);  // 0..255
+    const uint32_t grp = t >> 6, u = t & 63u;
+    const uint32_t lead_wfull = mapa_shared(smem_u32(w_full), 0);
+    uint32_t sr = 0, pr = 0, it = 0;
+    bool ok = true;
+    for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+      const int c0 = (tile % p.tiles_n) * (2 * kPHalf) + static_cast<int>(crank) * kPHalf;
+      for (int kb = 0; kb < total_kb; ++kb, ++it) {
+        const bool extra = kb >= p.num_kb_main;
+        const uint32_t my_sr = sr, my_pr = pr;
+        if (!extra && ++sr == kPStagesR) sr = 0, pr ^= 1u;
+        if ((it & 3u) != grp) continue;
+        const uint32_t sw = grp, pw = (it >> 2) & 1u;
+        if (!mbar_wait(&w_empty[sw], pw ^ 1u, p.status, kDevTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        uint8_t* wtile = ws + sw * kPWBytes;
+        if (!extra) {
+          if (!mbar_wait(&r_full[my_sr], my_pr, p.status, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          const uint8_t* raw = rs + my_sr * Tr::kRawBytes;
+          const uint8_t* scales = raw + Tr::kCodeBytes;
+#pragma unroll
+          for (uint32_t i = 0; i < 2; ++i) {
+            float s, z;
+            if constexpr (kWMN) {
+              const uint32_t g = (static_cast<uint32_t>(c0) + i * 64u) / static_cast<uint32_t>(p.group) -
+                                 static_cast<uint32_t>(c0) / static_cast<uint32_t>(p.group);
+              scale_zero<kScheme>(scales, g * 64u + u, s, z);
+              dequant_row<kScheme>(raw + u * (kPHalf * Tr::kBits / 8) + i * (64 * Tr::kBits / 8),
+                                   s, z, wtile + i * kMNBoxBytes + u * 128u, u, lut);
+            } else {
+              const uint32_t row = u + 64u * i;
+              scale_zero<kScheme>(scales, row, s, z);
+              dequant_row<kScheme>(raw + row * (kBK * Tr::kBits / 8), s, z, wtile + row * 128u,
+                                   row, lut);
+            }
+          }
+        } else {
+          // rank block: 64 columns of the up-projection operand (zero padded)
+          const int j0 = (kb - p.num_kb_main) * kBK;
+#pragma unroll
+          for (uint32_t i = 0; i < 2; ++i) {
+            if constexpr (kWMN) {
+              const int j = j0 + static_cast<int>(u);
+              uint8_t* out_row = wtile + i * kMNBoxBytes + u * 128u;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const long long col = c0 + i * 64 + c * 8;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (j < p.up_rows && col < p.up_cols)
+                  v = *reinterpret_cast<const uint4*>(p.up + static_cast<long long>(j) * p.up_ld + col);
+                st_chunk(out_row, u, c, v);
+              }
+            } else {
+              const uint32_t row = u + 64u * i;
+              const long long n = c0 + static_cast<long long>(row);
+              uint8_t* out_row = wtile + row * 128u;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const int j = j0 + c * 8;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (n < p.N && j < p.up_rows)
+                  v = *reinterpret_cast<const uint4*>(p.up + n * p.up_ld + j);
+                st_chunk(out_row, row, c, v);
+              }
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(2 + grp, 64);
+        if (u == 0) {
+          mbar_arrive_cluster(lead_wfull + sw * 8u);
+          if (!extra) mbar_arrive(&r_empty[my_sr]);
+        }
+      }
+    }
+  }
+
+  // After a failure the odd CTA may still have copies in flight that no
+  // barrier of its own tracks: give them time to land before the pair exits.
+  if (p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status) != 0) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 200000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no arrival, copy or MMA of the other CTA still targets this one
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 bool make_tmap_raw(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                    uint32_t box_outer);
@@ -493,6 +857,85 @@ int launch_q(const QGemmArgs& a, cudaStream_t stream) {
   return MLORA_OK;
 }
 
+template <int kScheme, bool kWMN>
+int launch_q_pair(const QGemmArgs& a, cudaStream_t stream) {
+  using Tr = QPairTraits<kScheme>;
+  CUtensorMap tx, tx2, tc, ts;
+  if (!make_tmap_2d_16b(&tx, a.x, a.K, a.M, a.ldx, kBK, kPHalf)) return MLORA_ERR_INVALID_ARG;
+  if (a.R > 0) {
+    const int64_t r64 = (a.R + 63) / 64 * 64;
+    if (!make_tmap_2d_16b(&tx2, a.x2, r64, a.M, a.ldx2, kBK, kPHalf)) return MLORA_ERR_INVALID_ARG;
+  } else {
+    tx2 = tx;
+  }
+  // W geometry: forward: W rows = N (out), cols = K (in); backward: W rows = K_red, cols = N_out.
+  const int64_t w_rows = kWMN ? a.K : a.N;
+  const int64_t w_cols = kWMN ? a.N : a.K;
+  const int64_t code_cols = w_cols * Tr::kBits / 8;  // bytes per W row
+  const int64_t ngroups = (w_cols + a.group - 1) / a.group;
+  uint32_t scale_box_bytes;
+  if (kWMN) {
+    // codes: 64 reduction rows x this CTA's 128 output columns
+    if (!make_tmap_raw(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.codes, code_cols, w_rows,
+                       code_cols, kPHalf * Tr::kBits / 8, kBK))
+      return MLORA_ERR_INVALID_ARG;
+    const uint32_t gbox = a.group >= kPHalf ? 1u : static_cast<uint32_t>(kPHalf / a.group);
+    if (!make_tmap_raw(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, a.scales_t, w_rows, ngroups,
+                       prepared_ld(w_rows) * 4, kBK, gbox))
+      return MLORA_ERR_INVALID_ARG;
+    scale_box_bytes = kBK * gbox * 4;
+  } else {
+    // codes: this CTA's 128 rows x 64 k
+    if (!make_tmap_raw(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.codes, code_cols, w_rows,
+                       code_cols, kBK * Tr::kBits / 8, kPHalf))
+      return MLORA_ERR_INVALID_ARG;
+    if (!make_tmap_raw(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, a.scales_t, w_rows, ngroups,
+                       prepared_ld(w_rows) * 4, kPHalf, 1))
+      return MLORA_ERR_INVALID_ARG;
+    scale_box_bytes = kPHalf * 4;
+  }
+  if (scale_box_bytes > Tr::kScaleBytes) {
+    set_error("qgemm pair: scale groups too small for the staged scale box");
+    return MLORA_ERR_UNSUPPORTED;
+  }
+  QGemmParams p;
+  p.M = static_cast<int>(a.M);
+  p.N = static_cast<int>(a.N);
+  p.num_kb_main = static_cast<int>((a.K + kBK - 1) / kBK);
+  p.R = static_cast<int>(a.R);
+  p.num_kb_extra = static_cast<int>((a.R + kBK - 1) / kBK);
+  const int tiles_m = static_cast<int>((a.M + 2 * kPHalf - 1) / (2 * kPHalf));
+  p.tiles_n = static_cast<int>((a.N + 2 * kPHalf - 1) / (2 * kPHalf));
+  p.num_tiles = tiles_m * p.tiles_n;
+  p.group = static_cast<int>(a.group);
+  p.scale_box_bytes = scale_box_bytes;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.up = static_cast<const __nv_bfloat16*>(a.up);
+  p.up_rows = static_cast<int>(a.up_rows);
+  p.up_ld = a.up_ld;
+  p.up_cols = a.up_cols;
+  p.status = device_status_ptr();
+
+  auto kern = qlora_gemm_pair_kernel<kScheme, kWMN>;
+  constexpr size_t smem = pair_smem_bytes<kScheme>();
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) {
+    set_error(std::string("cudaFuncSetAttribute(qgemm pair): ") + cudaGetErrorString(e));
+    return MLORA_ERR_CUDA;
+  }
+  const int pairs = std::min(p.num_tiles, num_sms() / 2);
+  LaunchScope scope(kKindGemm, stream);
+  kern<<<2 * pairs, kThreads, smem, stream>>>(tx, tx2, tc, ts, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("qgemm pair launch: ") + cudaGetErrorString(e));
+    return MLORA_ERR_CUDA;
+  }
+  return MLORA_OK;
+}
+
 bool make_tmap_raw(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                    uint32_t box_outer) {
@@ -502,7 +945,25 @@ bool make_tmap_raw(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, con
 
 }  // namespace
 
+// The CTA-pair kernel serves M >= 256 unless MLORA_GEMM_PAIR=0; both give the
+// same results (the same bf16 weights, the same per-tile reduction order).
+bool qpair_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MLORA_GEMM_PAIR");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
 int launch_qgemm(const QGemmArgs& a, cudaStream_t stream) {
+  if (a.M >= 2 * kPHalf && qpair_enabled()) {
+    switch (a.scheme) {
+      case kNF4: return a.w_mn_major ? launch_q_pair<kNF4, true>(a, stream) : launch_q_pair<kNF4, false>(a, stream);
+      case kINT4: return a.w_mn_major ? launch_q_pair<kINT4, true>(a, stream) : launch_q_pair<kINT4, false>(a, stream);
+      case kINT8: return a.w_mn_major ? launch_q_pair<kINT8, true>(a, stream) : launch_q_pair<kINT8, false>(a, stream);
+      default: break;
+    }
+  }
   switch (a.scheme) {
     case kNF4: return a.w_mn_major ? launch_q<kNF4, true>(a, stream) : launch_q<kNF4, false>(a, stream);
     case kINT4: return a.w_mn_major ? launch_q<kINT4, true>(a, stream) : launch_q<kINT4, false>(a, stream);
