@@ -617,6 +617,10 @@ int backward16(const void* dy, const void* x, const void* w0, const QGemmArgs* q
     ga.w_mn_major = true;
     ga.elt = elt;
     ga.out_dtype = dtype;
+    // in one call the weight-gradient kernel was launched just before: the
+    // GEMM starts on SMs it frees; its X2 (s.dy.B) was complete before that
+    // kernel passed its own wait, and dy, W0 before the call
+    ga.overlap_prev = phase == kPhaseAll;
     if ((rc = launch_gemm(ga, s))) return rc;
   }
 

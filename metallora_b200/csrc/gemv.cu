@@ -87,7 +87,6 @@ constexpr int kConsumers = kRowGroups * kKG;
 constexpr int kRankWarps = 3;     // warp 1 and the two last warps
 constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 640
 constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic; the static barriers take the rest
-constexpr int kRankThreads = 256;            // rank kernel
 constexpr int kMaxStages = 8;
 // Fill pattern of an unpublished partial slot: a signalling NaN with a
 // payload; arithmetic results are never signalling NaNs.
@@ -804,13 +803,19 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
 }
 
-// Partial sums of sT[m, j] = scale * sum_k x[m, k] A[j, k] for m < M <= 16:
-// CTA (j, s) covers the s-th k slice (~2048 k); thread t takes the 8-wide
-// chunks t, t + 256, ... and loads the A chunk and every token's chunk at once
-// (one round of memory latency for slices up to 2048), then the CTA reduces
-// in a fixed order.  It signals its dependent grid (the decode kernel) at
-// once so that grid streams weights meanwhile; the decode kernel adds the
-// slices in order.
+// Partial sums of sT[m, j] = scale * sum_k x[m, k] A[j, k] for m < M <= 16,
+// on the tensor cores: CTA (jt, s) computes the 16 rank columns of tile jt over
+// the s-th k slice (1024 k), each of its sixteen warps one 64-wide chunk, so
+// all of a slice's loads are in flight at once; mma.m16n8k16 (A's rows as the
+// A operand, the tokens as B, two 8-token tiles).  Within each 64-wide k chunk, lane q of MMA step b takes k
+// 16q + 4b .. + 3 (for A and B alike), so every lane loads its 16 consecutive
+// k of a row with two 16-byte loads.  The warps' sums meet in shared memory
+// in warp order.  Few CTAs (16 for r 64, K 4096) keep most SMs free for the
+// decode kernel, its programmatic dependent, which starts at once, streams
+// weights meanwhile and adds the slices in order.
+constexpr int kRankSmallWarps = 16;
+constexpr int kRankThreads = 32 * kRankSmallWarps;
+
 __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ a, int M, int K, int r,
     int kslice, float scale, float* __restrict__ st, float4* __restrict__ partials,
@@ -824,50 +829,67 @@ __global__ void __launch_bounds__(kRankThreads) lora_rank_small_kernel(
     for (int i = b * kRankThreads + threadIdx.x; i < n_partials4; i += nb * kRankThreads)
       partials[i] = make_float4(e, e, e, e);
   }
-  __shared__ float red[kRankThreads / 32][kMaxTok];
-  const int j = blockIdx.x, split = blockIdx.y;
+  __shared__ float red[kRankSmallWarps][16][16];  // [warp][j][m]
+  const int jt = blockIdx.x, split = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
   const int k0 = split * kslice, k1 = min(K, k0 + kslice);
-  float acc[kMaxTok];
+  const int wk = (kslice / kRankSmallWarps + 63) / 64 * 64;
+  const int wk0 = k0 + warp * wk, wk1 = min(k1, wk0 + wk);
+  const int j0 = jt * 16 + g, j1 = j0 + 8;
+  const __nv_bfloat16* a0 = j0 < r ? a + static_cast<long long>(j0) * K : nullptr;
+  const __nv_bfloat16* a1 = j1 < r ? a + static_cast<long long>(j1) * K : nullptr;
+  const __nv_bfloat16* x0 = g < M ? x + static_cast<long long>(g) * K : nullptr;
+  const __nv_bfloat16* x1 = g + 8 < M ? x + static_cast<long long>(g + 8) * K : nullptr;
+  float c[2][4];
 #pragma unroll
-  for (int m = 0; m < kMaxTok; ++m) acc[m] = 0.f;
-  const __nv_bfloat16* ar = a + static_cast<long long>(j) * K;
-  for (int k = k0 + threadIdx.x * 8; k < k1; k += kRankThreads * 8) {
-    const uint4 av = __ldg(reinterpret_cast<const uint4*>(ar + k));
-    uint4 xv[kMaxTok];
+  for (int t = 0; t < 2; ++t)
 #pragma unroll
-    for (int m = 0; m < kMaxTok; ++m)
-      xv[m] = m < M ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<long long>(m) * K + k))
-                    : make_uint4(0, 0, 0, 0);
-    const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&av);
+    for (int e = 0; e < 4; ++e) c[t][e] = 0.f;
+  auto ld16 = [&](const __nv_bfloat16* row, int k, uint4 (&v)[2]) {
+    // this lane's 16 k of a row (zero past the slice or for an absent row)
+    if (row != nullptr && k + 16 <= wk1) {
+      v[0] = __ldg(reinterpret_cast<const uint4*>(row + k));
+      v[1] = __ldg(reinterpret_cast<const uint4*>(row + k + 8));
+    } else {
+      v[0] = v[1] = make_uint4(0, 0, 0, 0);
+    }
+  };
+  for (int kc = wk0; kc < wk1; kc += 64) {
+    const int k = kc + 16 * q;
+    uint4 va0[2], va1[2], vx0[2], vx1[2];
+    ld16(a0, k, va0);
+    ld16(a1, k, va1);
+    ld16(x0, k, vx0);
+    ld16(x1, k, vx1);
+    const uint32_t* pa0 = reinterpret_cast<const uint32_t*>(va0);
+    const uint32_t* pa1 = reinterpret_cast<const uint32_t*>(va1);
+    const uint32_t* px0 = reinterpret_cast<const uint32_t*>(vx0);
+    const uint32_t* px1 = reinterpret_cast<const uint32_t*>(vx1);
 #pragma unroll
-    for (int m = 0; m < kMaxTok; ++m) {
-      if (m < M) {
-        const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv[m]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 af = __bfloat1622float2(ap[i]), xf = __bfloat1622float2(xp[i]);
-          acc[m] = fmaf(xf.x, af.x, acc[m]);
-          acc[m] = fmaf(xf.y, af.y, acc[m]);
-        }
-      }
+    for (int s = 0; s < 4; ++s) {  // MMA step s: k + 4s .. + 3 (words 2s, 2s + 1)
+      const uint32_t af[4] = {pa0[2 * s], pa1[2 * s], pa0[2 * s + 1], pa1[2 * s + 1]};
+      mma16816(c[0], af, px0[2 * s], px0[2 * s + 1]);
+      mma16816(c[1], af, px1[2 * s], px1[2 * s + 1]);
     }
   }
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // C fragment: rows (g, g + 8) = rank columns j, columns (2q, 2q + 1) of each
+  // 8-token tile = tokens
 #pragma unroll
-  for (int m = 0; m < kMaxTok; ++m) {
-    if (m < M) {
-      float v = acc[m];
+  for (int t = 0; t < 2; ++t)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) red[w][m] = v;
-    }
-  }
+    for (int e = 0; e < 4; ++e)
+      red[warp][g + 8 * (e >> 1)][t * 8 + 2 * q + (e & 1)] = c[t][e];
   __syncthreads();
-  if (threadIdx.x < M) {
-    float v = 0.f;
+  for (int i = threadIdx.x; i < 256; i += kRankThreads) {
+    const int jj = i >> 4, m = i & 15;
+    const int j = jt * 16 + jj;
+    if (j < r && m < M) {
+      float v = 0.f;
 #pragma unroll
-    for (int i = 0; i < kRankThreads / 32; ++i) v += red[i][threadIdx.x];
-    st[(static_cast<long long>(split) * M + threadIdx.x) * r + j] = v * scale;
+      for (int w = 0; w < kRankSmallWarps; ++w) v += red[w][jj][m];
+      st[(static_cast<long long>(split) * M + m) * r + j] = v * scale;
+    }
   }
 }
 
@@ -1077,7 +1099,7 @@ int launch_partials_fill(float* partials, int64_t n, cudaStream_t s) {
 }
 
 int rank_small_splits(int64_t K) {
-  const int64_t s = (K + 2047) / 2048;  // ~2048 k per CTA
+  const int64_t s = (K + 1023) / 1024;  // ~1024 k per CTA
   return static_cast<int>(s < 1 ? 1 : (s > 16 ? 16 : s));
 }
 
@@ -1098,8 +1120,8 @@ int launch_rank_small(const void* x, const void* a, int64_t M, int64_t K, int64_
   }
   LaunchScope scope(kKindGemv, s);
   const int splits = rank_small_splits(K);
-  const int64_t kslice = ((K + splits - 1) / splits + 7) / 8 * 8;
-  lora_rank_small_kernel<<<dim3(static_cast<unsigned>(r), static_cast<unsigned>(splits)), kRankThreads, 0,
+  const int64_t kslice = ((K + splits - 1) / splits + 63) / 64 * 64;
+  lora_rank_small_kernel<<<dim3(static_cast<unsigned>((r + 15) / 16), static_cast<unsigned>(splits)), kRankThreads, 0,
                            s>>>(static_cast<const __nv_bfloat16*>(x),
                                 static_cast<const __nv_bfloat16*>(a), static_cast<int>(M),
                                 static_cast<int>(K), static_cast<int>(r),

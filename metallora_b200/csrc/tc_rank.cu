@@ -399,6 +399,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                                  which ? &tm_big1 : &tm_big0, which ? &tm_st1 : &tm_st0,
                                  tile * 128, w.kb_begin, w.kb_end, p.status);
   }
+  // a programmatic dependent (the dx GEMM, which reads none of this kernel's
+  // outputs) may start on the SMs this grid frees during its reduction tail
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const bool epi = warp >= 2;
   const int row_local = static_cast<int>((warp & 3u) * 32 + lane_id());
   const long long prow = static_cast<long long>(tile) * 128 + row_local;
