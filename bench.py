@@ -883,7 +883,13 @@ def sweep(kind, sampler=None, quick=False):
                     "tokens_per_s": round(M / t * 1e3, 1),
                     "roofline": {**tensor_roofline(fl, t, clocks),
                                  "note": "fp32 as 3 bf16 products (hi.hi, hi.lo, lo.hi): "
-                                         "algorithmic fp32 FLOPs over the bf16 peak"},
+                                         "algorithmic fp32 FLOPs over the bf16 peak",
+                                 "executed_bf16_frac": round(
+                                     3 * fl / t / 1e9 / pick_peak(peaks, clocks)[0], 4),
+                                 "executed_note": "the 3 bf16 products the tensor cores run "
+                                                  "(3x the algorithmic FLOPs) over the same "
+                                                  "peak; the hi/lo split passes of x and W0 "
+                                                  "are inside the timed call"},
                     "clocks": clocks})
         return out
     if kind == "multi":

@@ -183,7 +183,8 @@ def test_golden_fp32_through_gpu(cuda, golden):
 def test_full_size_bf16_step_rows_and_grads(cuda):
     """The bf16 forward+backward workload at full size (8192 tokens,
     4096 -> 4096, rank 16).  Rows of y/dx are independent, so 64 sampled rows
-    are checked against the oracle; dA/dB against a torch fp32 reference."""
+    are checked against the oracle; dA/dB, which reduce over all 8192 tokens,
+    against the oracle's fp64 gradients of the whole batch."""
     from metallora_b200 import kernels as K
     M, Kd, N, r, alpha = 8192, 4096, 4096, 16, 32.0
     (x, W, A, B, dy), _ = make(M, Kd, N, r, torch.bfloat16, cuda, seed=8)
@@ -194,10 +195,10 @@ def test_full_size_bf16_step_rows_and_grads(cuda):
     xh, Wh, Ah, Bh, dyh = (t.float().cpu().numpy() for t in (x[rows], W, A, B, dy[rows]))
     assert_close(y[rows], lo.lora_forward(xh, Wh, Ah, Bh, alpha, np.float64), 2e-2)
     assert_close(dx[rows], lo.lora_grad_x(dyh, Wh, Ah, Bh, alpha, np.float64), 2e-2)
-    s = alpha / r
-    xf, Af, Bf, dyf = x.float(), A.float(), B.float(), dy.float()
-    assert_close(da, (s * (dyf @ Bf).t() @ xf).cpu().numpy(), 2e-2)
-    assert_close(db, (s * dyf.t() @ (xf @ Af.t())).cpu().numpy(), 2e-2)
+    xa, dya = (t.float().cpu().numpy() for t in (x, dy))
+    ref_da, ref_db = lo.lora_backward(dya, xa, Ah, Bh, alpha, None, np.float64)
+    assert_close(da, ref_da, 2e-2)
+    assert_close(db, ref_db, 2e-2)
     # linearity in x: f(2x) - f(x) == f(x) - f(0) for the full batch
     y2, _ = K.lora_linear_fwd(x * 2, W, A, B, alpha)
     assert float((y2.float() - 2 * y.float()).norm() / y.float().norm()) < 2e-2
