@@ -8,6 +8,7 @@
 //         (1 when 0), zero = clamp(rint(-min/scale)), q = clamp(rint(w/scale) + zero).
 // Dequantisers follow the reference shaders' fp32 arithmetic
 // (kernels/lora_quantized.metal:17-25).
+#include <algorithm>
 #include <string>
 
 #include "internal.h"
@@ -160,32 +161,47 @@ __global__ void dequantize_kernel(int scheme, const uint8_t* __restrict__ codes,
 // consecutive weights of one row (4 code bytes for 4-bit, 8 for INT8), so item
 // i reads codes at byte i*4 (i*8) and writes out[i*8 .. i*8+7] -- every warp
 // load and store is one contiguous run.  Each thread keeps kUnroll items'
-// loads in flight (HBM-bound: 2.5 B/weight for 4-bit to bf16).  Same fp32
-// arithmetic as dequantize_kernel, so the outputs are identical.
+// loads in flight.
+//
+// The arithmetic is the scalar kernel's, done on packed fp32 pairs (each half
+// rounds as the scalar op, so the outputs are identical):
+//   * 4-bit: one shared-memory lookup per code byte returns the pair
+//     (v(low nibble), v(high nibble)), v = the NF4 level or float(q); the
+//     table is replicated so each lane of a half-warp reads its own bank pair;
+//   * INT8: float(q) = (2^23 + q) - 2^23, the first built by a byte permute;
+//   * then (INT) - zero, * scale, and a packed round to bf16 / fp16.
+// When the groups tile the rows (K % group == 0) and group/8 is a power of
+// two, an item's scale index is item >> shift (no division).
+constexpr int kDqVecThreads = 512;
+
 template <typename O>
-__device__ __forceinline__ void store8(O* dst, const float (&v)[8]) {
+__device__ __forceinline__ void store8(O* dst, const uint64_t (&p)[4]) {
   if constexpr (sizeof(O) == 4) {
-    reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    reinterpret_cast<float4*>(dst)[0] = make_float4(f2_lo(p[0]), f2_hi(p[0]), f2_lo(p[1]), f2_hi(p[1]));
+    reinterpret_cast<float4*>(dst)[1] = make_float4(f2_lo(p[2]), f2_hi(p[2]), f2_lo(p[3]), f2_hi(p[3]));
   } else {
     uint4 u;  // round-to-nearest-even, as from_f32
-    u.x = pack2<O>(v[0], v[1]);
-    u.y = pack2<O>(v[2], v[3]);
-    u.z = pack2<O>(v[4], v[5]);
-    u.w = pack2<O>(v[6], v[7]);
+    u.x = pack2<O>(f2_lo(p[0]), f2_hi(p[0]));
+    u.y = pack2<O>(f2_lo(p[1]), f2_hi(p[1]));
+    u.z = pack2<O>(f2_lo(p[2]), f2_hi(p[2]));
+    u.w = pack2<O>(f2_lo(p[3]), f2_hi(p[3]));
     *reinterpret_cast<uint4*>(dst) = u;
   }
 }
 
-template <int kScheme, typename O, typename Idx>
-__global__ void __launch_bounds__(256) dequantize_vec_kernel(
+template <int kScheme, typename O, typename Idx, bool kShift>
+__global__ void __launch_bounds__(kDqVecThreads) dequantize_vec_kernel(
     const uint8_t* __restrict__ codes, const void* __restrict__ scales,
     const __half* __restrict__ zeros, Idx items, Idx items_per_row, Idx ng, Idx g8,
-    O* __restrict__ out) {
+    int g8_shift, O* __restrict__ out) {
   constexpr int kUnroll = 4;
-  __shared__ float lut[16];
-  if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
-  __syncthreads();
+  constexpr bool kTable = kScheme != kINT8;
+  __shared__ uint64_t table[kTable ? 256 * kPairCopies : 1];
+  if constexpr (kTable) {
+    fill_pair_table<kScheme>(table, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  const char* tbl_lane = reinterpret_cast<const char*>(table) + (threadIdx.x % kPairCopies) * 8;
   const Idx stride = static_cast<Idx>(gridDim.x) * blockDim.x;
   for (Idx base = static_cast<Idx>(blockIdx.x) * blockDim.x + threadIdx.x; base < items;
        base += stride * kUnroll) {
@@ -198,8 +214,13 @@ __global__ void __launch_bounds__(256) dequantize_vec_kernel(
       s[u] = 0.f;
       z[u] = 0.f;
       if (it < items) {
-        const Idx row = it / items_per_row;
-        const Idx gi = row * ng + (it - row * items_per_row) / g8;
+        Idx gi;
+        if constexpr (kShift) {
+          gi = it >> g8_shift;
+        } else {
+          const Idx row = it / items_per_row;
+          gi = row * ng + (it - row * items_per_row) / g8;
+        }
         if constexpr (kScheme == kINT8) {
           raw[u] = __ldg(reinterpret_cast<const uint2*>(codes) + it);
         } else {
@@ -217,18 +238,9 @@ __global__ void __launch_bounds__(256) dequantize_vec_kernel(
     for (int u = 0; u < kUnroll; ++u) {
       const Idx it = base + u * stride;
       if (it >= items) break;
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if constexpr (kScheme == kINT8) {
-          const uint32_t word = j < 4 ? raw[u].x : raw[u].y;
-          v[j] = dequant_int((word >> (8 * (j & 3))) & 0xFF, s[u], z[u]);
-        } else {
-          const uint32_t q = (raw[u].x >> (4 * j)) & 0xF;  // byte j/2, low nibble = even k
-          v[j] = kScheme == kNF4 ? dequant_nf4(q, s[u], lut) : dequant_int(q, s[u], z[u]);
-        }
-      }
-      store8<O>(out + it * 8, v);
+      uint64_t p[4];
+      dequant8_pairs<kScheme>(raw[u].x, raw[u].y, s[u], z[u], tbl_lane, p);
+      store8<O>(out + it * 8, p);
     }
   }
 }
@@ -325,10 +337,24 @@ template <int kScheme, typename O, typename Idx>
 void launch_dequantize_vec(const uint8_t* codes, const void* scales, const __half* zeros,
                            int64_t N, int64_t K, int64_t g, O* out, cudaStream_t s) {
   const int64_t items = N * K / 8;
-  const int grid = grid_1d((items + 3) / 4, 256);
-  dequantize_vec_kernel<kScheme, O, Idx><<<grid, 256, 0, s>>>(
+  const int64_t g8 = g / 8;
+  int shift = 0;
+  while ((int64_t(1) << shift) < g8) ++shift;
+  const bool fast = K % g == 0 && (int64_t(1) << shift) == g8;
+  auto* kernel = fast ? dequantize_vec_kernel<kScheme, O, Idx, true>
+                      : dequantize_vec_kernel<kScheme, O, Idx, false>;
+  // persistent-style: one wave of resident blocks, each filling its table once
+  static int per_sm[2] = {0, 0};
+  int& occ = per_sm[fast ? 1 : 0];
+  if (occ == 0 &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kDqVecThreads, 0) != cudaSuccess)
+    occ = 1;
+  occ = std::max(occ, 1);
+  int64_t grid = (items + int64_t(4) * kDqVecThreads - 1) / (int64_t(4) * kDqVecThreads);
+  grid = std::max<int64_t>(1, std::min<int64_t>(grid, int64_t(occ) * num_sms()));
+  kernel<<<static_cast<int>(grid), kDqVecThreads, 0, s>>>(
       codes, scales, zeros, static_cast<Idx>(items), static_cast<Idx>(K / 8),
-      static_cast<Idx>((K + g - 1) / g), static_cast<Idx>(g / 8), out);
+      static_cast<Idx>((K + g - 1) / g), static_cast<Idx>(g8), shift, out);
 }
 
 template <typename O>

@@ -59,7 +59,7 @@ struct QTraits {
 template <int kScheme>
 constexpr size_t smem_bytes() {
   return 1024 + kStagesX * kXTileBytes + kStagesW * kWTileBytes +
-         kStagesR * QTraits<kScheme>::kRawBytes + 512;
+         kStagesR * QTraits<kScheme>::kRawBytes + 512 + (kScheme == kINT8 ? 0 : kPairTableBytes);
 }
 
 struct QGemmParams {
@@ -84,25 +84,17 @@ __device__ __forceinline__ void st_chunk(uint8_t* row_base, uint32_t row, uint32
 }
 
 // Dequantises 8 consecutive weights held in `w` (4-bit: one word = 8 nibbles;
-// 8-bit: two words) into a 16-byte chunk of bf16.
+// 8-bit: two words) into a 16-byte chunk of bf16 (packed fp32 pairs, the
+// scalar rounding; `tbl_lane` is this thread's view of the 4-bit pair table).
 template <int kScheme>
 __device__ __forceinline__ uint4 dq8(uint32_t w0, uint32_t w1, float scale, float zero,
-                                     const float* lut) {
-  float v[8];
-  if constexpr (kScheme == kINT8) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = dequant_int((w0 >> (8 * i)) & 0xFFu, scale, zero);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[4 + i] = dequant_int((w1 >> (8 * i)) & 0xFFu, scale, zero);
-  } else if constexpr (kScheme == kNF4) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = dequant_nf4((w0 >> (4 * i)) & 0xFu, scale, lut);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = dequant_int((w0 >> (4 * i)) & 0xFu, scale, zero);
-  }
-  return make_uint4(pack2<__nv_bfloat16>(v[0], v[1]), pack2<__nv_bfloat16>(v[2], v[3]),
-                    pack2<__nv_bfloat16>(v[4], v[5]), pack2<__nv_bfloat16>(v[6], v[7]));
+                                     const char* tbl_lane) {
+  uint64_t p[4];
+  dequant8_pairs<kScheme>(w0, w1, scale, zero, tbl_lane, p);
+  return make_uint4(pack2<__nv_bfloat16>(f2_lo(p[0]), f2_hi(p[0])),
+                    pack2<__nv_bfloat16>(f2_lo(p[1]), f2_hi(p[1])),
+                    pack2<__nv_bfloat16>(f2_lo(p[2]), f2_hi(p[2])),
+                    pack2<__nv_bfloat16>(f2_lo(p[3]), f2_hi(p[3])));
 }
 
 template <int kScheme>
@@ -121,24 +113,25 @@ __device__ __forceinline__ void scale_zero(const uint8_t* scales, uint32_t idx, 
 // One thread converts one 64-element weight row of the raw tile.
 template <int kScheme>
 __device__ __forceinline__ void dequant_row(const uint8_t* codes, float s, float z,
-                                            uint8_t* out_row, uint32_t swz_row, const float* lut) {
+                                            uint8_t* out_row, uint32_t swz_row,
+                                            const char* tbl_lane) {
   if constexpr (kScheme == kINT8) {
     const uint4* c = reinterpret_cast<const uint4*>(codes);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 u = c[q];
-      st_chunk(out_row, swz_row, 2 * q, dq8<kScheme>(u.x, u.y, s, z, lut));
-      st_chunk(out_row, swz_row, 2 * q + 1, dq8<kScheme>(u.z, u.w, s, z, lut));
+      st_chunk(out_row, swz_row, 2 * q, dq8<kScheme>(u.x, u.y, s, z, tbl_lane));
+      st_chunk(out_row, swz_row, 2 * q + 1, dq8<kScheme>(u.z, u.w, s, z, tbl_lane));
     }
   } else {
     const uint4* c = reinterpret_cast<const uint4*>(codes);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const uint4 u = c[q];
-      st_chunk(out_row, swz_row, 4 * q + 0, dq8<kScheme>(u.x, 0, s, z, lut));
-      st_chunk(out_row, swz_row, 4 * q + 1, dq8<kScheme>(u.y, 0, s, z, lut));
-      st_chunk(out_row, swz_row, 4 * q + 2, dq8<kScheme>(u.z, 0, s, z, lut));
-      st_chunk(out_row, swz_row, 4 * q + 3, dq8<kScheme>(u.w, 0, s, z, lut));
+      st_chunk(out_row, swz_row, 4 * q + 0, dq8<kScheme>(u.x, 0, s, z, tbl_lane));
+      st_chunk(out_row, swz_row, 4 * q + 1, dq8<kScheme>(u.y, 0, s, z, tbl_lane));
+      st_chunk(out_row, swz_row, 4 * q + 2, dq8<kScheme>(u.z, 0, s, z, tbl_lane));
+      st_chunk(out_row, swz_row, 4 * q + 3, dq8<kScheme>(u.w, 0, s, z, tbl_lane));
     }
   }
 }
@@ -165,7 +158,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  float* lut = reinterpret_cast<float*>(tmem_slot + 4);
+  // 4-bit pair table after the 512-byte barrier area
+  uint64_t* table = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 512);
+  const char* tbl_lane = reinterpret_cast<const char*>(table) + (threadIdx.x % kPairCopies) * 8;
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -177,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
   }
-  if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+  if constexpr (kScheme != kINT8) fill_pair_table<kScheme>(table, threadIdx.x, blockDim.x);
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_codes);
@@ -366,10 +361,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t srow = (box * 64u) / static_cast<uint32_t>(p.group);
             scale_zero<kScheme>(scales, srow * 64u + row, s, z);
             dequant_row<kScheme>(raw + row * (kBN * Tr::kBits / 8) + box * (64 * Tr::kBits / 8),
-                                 s, z, wtile + box * kMNBoxBytes + row * 128u, row, lut);
+                                 s, z, wtile + box * kMNBoxBytes + row * 128u, row, tbl_lane);
           } else {
             scale_zero<kScheme>(scales, t, s, z);
-            dequant_row<kScheme>(raw + t * (kBK * Tr::kBits / 8), s, z, wtile + t * 128u, t, lut);
+            dequant_row<kScheme>(raw + t * (kBK * Tr::kBits / 8), s, z, wtile + t * 128u, t, tbl_lane);
           }
         } else {
           // rank block: copy 64 columns of the up-projection operand (zero padded)
@@ -456,7 +451,8 @@ struct QPairTraits {
 template <int kScheme>
 constexpr size_t pair_smem_bytes() {
   return 1024 + kPStagesX * kPXBytes + kPStagesW * kPWBytes +
-         kPStagesR * QPairTraits<kScheme>::kRawBytes + 512;
+         kPStagesR * QPairTraits<kScheme>::kRawBytes + 512 +
+         (kScheme == kINT8 ? 0 : kPairTableBytes);
 }
 
 template <int kScheme, bool kWMN>
@@ -482,7 +478,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  float* lut = reinterpret_cast<float*>(tmem_slot + 4);
+  // 4-bit pair table after the 512-byte barrier area
+  uint64_t* table = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 512);
+  const char* tbl_lane = reinterpret_cast<const char*>(table) + (threadIdx.x % kPairCopies) * 8;
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -500,7 +498,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
   }
-  if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+  if constexpr (kScheme != kINT8) fill_pair_table<kScheme>(table, threadIdx.x, blockDim.x);
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_codes);
@@ -714,12 +712,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                  static_cast<uint32_t>(c0) / static_cast<uint32_t>(p.group);
               scale_zero<kScheme>(scales, g * 64u + u, s, z);
               dequant_row<kScheme>(raw + u * (kPHalf * Tr::kBits / 8) + i * (64 * Tr::kBits / 8),
-                                   s, z, wtile + i * kMNBoxBytes + u * 128u, u, lut);
+                                   s, z, wtile + i * kMNBoxBytes + u * 128u, u, tbl_lane);
             } else {
               const uint32_t row = u + 64u * i;
               scale_zero<kScheme>(scales, row, s, z);
               dequant_row<kScheme>(raw + row * (kBK * Tr::kBits / 8), s, z, wtile + row * 128u,
-                                   row, lut);
+                                   row, tbl_lane);
             }
           }
         } else {
