@@ -833,6 +833,7 @@ def sweep(kind, sampler=None, quick=False):
     (tokens 1 and 4096 for INT, no lean-path comparison)."""
     import torch
 
+    from metallora_b200 import _lib
     from metallora_b200 import kernels as K
     from metallora_b200 import quant
     dev = torch.device("cuda", 0)
@@ -952,6 +953,26 @@ def sweep(kind, sampler=None, quick=False):
             flb = 2.0 * M * (N * Kd + 2 * N * r + 2 * r * Kd)
             d.update({"bwd_ms": round(tb, 4), "bwd_tflops": round(flb / tb / 1e9, 1),
                       "fwd_bwd_tflops": round((fl + flb) / (tf + tb) / 1e9, 1)})
+            if M > 16 and not quick:
+                # where the call's time goes: the library's per-launch events by
+                # kernel kind (eager calls, after the graph timings above)
+                for tag, fn in (("fwd", lambda: K.qlora_linear_fwd(x, qw, A, B, alpha)),
+                                ("bwd", lambda: K.qlora_linear_bwd(dy, x, qw, A, B, alpha,
+                                                                   saved))):
+                    reps = 5
+                    fn()
+                    torch.cuda.synchronize()
+                    _lib.profile_read(reset=True)
+                    _lib.profile_enable(True)
+                    for _ in range(reps):
+                        fn()
+                    torch.cuda.synchronize()
+                    _lib.profile_enable(False)
+                    prof = _lib.profile_read(reset=True)
+                    d[f"{tag}_kernels_ms"] = {k: round(v[0] / reps, 4) for k, v in prof.items()
+                                              if v[1]}
+                    d[f"{tag}_kernel_launches"] = {k: v[1] // reps for k, v in prof.items()
+                                                   if v[1]}
         else:
             Wm = K.merge(quant.dequantize(qw, torch.bfloat16), A, B, alpha)
             if M <= 16:

@@ -79,10 +79,11 @@ constexpr int kBoxBytes = 128;    // inner extent of one weight box (128-byte sw
 constexpr int kStageBytes = kDecRows * kBoxBytes;  // 16 KB of weights per stage
 constexpr int kMaxTok = 16;
 constexpr int kRowGroups = 4;     // consumer warps per k-group, 32 rows each
-constexpr int kKG = 4;            // k-groups
+constexpr int kKG = 4;            // k-groups (a power of two)
 constexpr int kTiles = 2;         // 16-row MMA tiles per consumer warp
 constexpr int kGroupRows = kTiles * 16;
 static_assert(kRowGroups * kGroupRows == 128, "a row block is 128 rows");
+static_assert((kKG & (kKG - 1)) == 0, "quads are dealt with a mask");
 constexpr int kConsumers = kRowGroups * kKG;
 constexpr int kRankWarps = 3;     // warp 1 and the two last warps
 constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 640
@@ -586,6 +587,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int g = lane >> 2, q = lane & 3;
   const int fq = D::kFlip ? (q >> 1) : 0;
   const uint32_t* lut_lane = lut + lane;
+  // a quad's scale group: group is 64, 128 or 256, so (64 j) / group = j >> gshift
+  const int gshift = p.group >= 256 ? 2 : (p.group >= 128 ? 1 : 0);
   bool ok = true;
   int slot = 0;
   uint32_t phase = 0;
@@ -612,7 +615,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const uint32_t* scl = reinterpret_cast<const uint32_t*>(sring + slot * p.scale_slot);
         // this warp's quad of the stage, if any (quads are dealt round-robin
         // over the k-groups along the row block's k); one copy of the body
-        const int j = ((kg - s * D::kQuads) % kKG + kKG) % kKG;
+        const int j = (kg - s * D::kQuads) & (kKG - 1);
         if (j < D::kQuads) {
           // the lane's words of rows g and g+8 of the four tiles (swizzled 16-byte chunks)
           uint32_t w[kTiles][2][kWords];
@@ -650,7 +653,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
               }
               if constexpr (D::kScaled) {
                 // prepared table: NF4 absmax (fp32) or (scale, zero) fp16 pair
-                const uint32_t wv = scl[((j * 64) / p.group) * kDecRows + row];
+                const uint32_t wv = scl[(j >> gshift) * kDecRows + row];
                 if constexpr (kScheme == kNF4) {
                   e[i][h] = make_uint2(wv, 0);
                 } else {
