@@ -953,7 +953,7 @@ def sweep(kind, sampler=None, quick=False):
             flb = 2.0 * M * (N * Kd + 2 * N * r + 2 * r * Kd)
             d.update({"bwd_ms": round(tb, 4), "bwd_tflops": round(flb / tb / 1e9, 1),
                       "fwd_bwd_tflops": round((fl + flb) / (tf + tb) / 1e9, 1)})
-            if M > 16 and not quick:
+            if M > 16:
                 # where the call's time goes: the library's per-launch events by
                 # kernel kind (eager calls, after the graph timings above)
                 for tag, fn in (("fwd", lambda: K.qlora_linear_fwd(x, qw, A, B, alpha)),
