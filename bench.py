@@ -250,6 +250,35 @@ def cpu_baseline(tokens: int, reps: int, seed: int = 0):
             "seconds_per_rep": med}
 
 
+def nf4_cpu_baseline(qw, x, A, B, alpha, group, reps: int = 3):
+    """Times the oracle's numpy restatement of the reference's NF4 forward
+    (kernels/lora_quantized.metal:97-164: dequantise the NF4 weight in fp32,
+    then y = x.W^T + s.(x.A^T).B^T) on the host cores, on the same weight and
+    tokens: the CPU beside the decode kernel.  Median of ``reps`` calls after
+    one warm-up; inputs are on the host before the timed region."""
+    from threadpoolctl import threadpool_limits
+
+    from oracle import lora_oracle as lo
+    from oracle import quant_oracle as qo
+    N, K = qw.shape
+    codes = qw.codes.cpu().numpy()
+    absmax = qw.scales.float().cpu().numpy()
+    xf, Af, Bf = (t.float().cpu().numpy() for t in (x, A, B))
+    cores = len(os.sched_getaffinity(0))
+    times = []
+    with threadpool_limits(limits=cores, user_api="blas"):
+        for _ in range(reps + 1):
+            t = time.perf_counter()
+            W = qo.dequant_nf4(codes, absmax, K, group)
+            lo.lora_forward(xf, W, Af, Bf, alpha, np.float32)
+            times.append(time.perf_counter() - t)
+        cores = _blas_threads()
+    med = statistics.median(times[1:])
+    return {"value": round(med * 1e3, 2), "unit": "ms per call", "cores": cores, "kind": "port",
+            "sample": (f"one full call ({x.shape[0]} token(s), NF4 {N}x{K}, r {A.shape[0]}): "
+                       f"numpy fp32 dequantisation + forward, median of {reps}, {_cpu_model()}")}
+
+
 # ------------------------------------------------------------- our arm -----
 
 def headline_config(world):
@@ -939,6 +968,8 @@ def sweep(kind, sampler=None, quick=False):
                           reps=10, inner=2)
             d["weight_copies"] = len(copies)
             del copies
+            if kind == "nf4" and M == 1:
+                d["cpu_baseline"] = nf4_cpu_baseline(qw, x, A, B, alpha, group)
         else:
             tf = graph_ms(lambda: K.qlora_linear_fwd(x, qw, A, B, alpha))
         d.update({"fwd_ms": round(tf, 4), "fwd_tflops": round(fl / tf / 1e9, 1),
