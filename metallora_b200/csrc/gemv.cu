@@ -84,6 +84,7 @@ constexpr int kTiles = 2;         // 16-row MMA tiles per consumer warp
 constexpr int kGroupRows = kTiles * 16;
 static_assert(kRowGroups * kGroupRows == 128, "a row block is 128 rows");
 static_assert((kKG & (kKG - 1)) == 0, "quads are dealt with a mask");
+constexpr int kLutCopies = 32;    // NF4 pair table: one copy per lane
 constexpr int kConsumers = kRowGroups * kKG;
 constexpr int kRankWarps = 3;     // warp 1 and the two last warps
 constexpr int kDecThreads = 32 * (2 + kConsumers + kRankWarps - 1);  // 640
@@ -103,8 +104,6 @@ struct Dec {
   static constexpr int kWords = kQuadBytes / 16;         // 32-bit words per lane per row per quad
   static constexpr bool kScaled = kScheme != 0;
   static constexpr bool kFlip = kScheme == kNF4 || kScheme == kINT4;
-  static constexpr int kLutCopies = 32;
-  static constexpr int kLutBytes = kScheme == kNF4 ? 256 * kLutCopies * 4 : 0;
 };
 
 struct DecParams {
@@ -175,7 +174,7 @@ __device__ __forceinline__ void a_frags(const uint32_t (&w0)[kWords], const uint
     // word b/2 holds k 8(b/2)..+7; its bytes 2(bb%2), 2(bb%2)+1 are k+0,1 and k+2,3
     const uint32_t s0 = odd ? 0x4442u : 0x4440u, s1 = odd ? 0x4443u : 0x4441u;
     const uint32_t u0 = w0[b >> 1], u1 = w1[b >> 1];
-    constexpr int kC = Dec<kScheme>::kLutCopies;
+    constexpr int kC = kLutCopies;
     a[0] = lut_lane[__byte_perm(u0, 0, s0) * kC];
     a[2] = lut_lane[__byte_perm(u0, 0, s1) * kC];
     a[1] = lut_lane[__byte_perm(u1, 0, s0) * kC];
@@ -409,8 +408,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   } else {
     if constexpr (kScheme == kNF4) {
       // lut[e * 32 + c] = (bf16 L[e & 15], bf16 L[e >> 4]) for every lane c
-      for (int i = threadIdx.x - 32; i < 256 * D::kLutCopies; i += blockDim.x - 32) {
-        const int e = i / D::kLutCopies;
+      for (int i = threadIdx.x - 32; i < 256 * kLutCopies; i += blockDim.x - 32) {
+        const int e = i / kLutCopies;
         lut[i] = pack2<__nv_bfloat16>(kNF4Levels[e & 15], kNF4Levels[e >> 4]);
       }
     }
@@ -930,7 +929,7 @@ DecLayout dec_layout(int scheme, int64_t M, int64_t r, int64_t group, int stages
   L.off_x = stages * kStageBytes;
   L.off_scale = L.off_x + stages * L.x_slot;
   L.off_lut = L.off_scale + stages * L.scale_slot;
-  const int lut = scheme == kNF4 ? 256 * 32 * 4 : 0;
+  const int lut = scheme == kNF4 ? 256 * kLutCopies * 4 : 0;
   L.off_red = L.off_lut + lut;
   const int red = (kKG - 1) * kRowGroups * kTiles * kNT * 128 * 4;
   L.off_rt = L.off_red + red;
