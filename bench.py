@@ -473,6 +473,7 @@ def run_ours(args, rank, world, local_rank):
 
     # end-to-end through the public API with host buffers (pinned), overlapped
     e2e = run_e2e(args, layer, M, K, N, dev, world, peer)
+    e2e_all = run_e2e(args, layer, M, K, N, dev, world, peer, outputs="all")
 
     total_tflops = world * flops_per_token(K, N, r) * M * args.steps / (ms / 1e3) / 1e12
     line = {
@@ -506,6 +507,9 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches,
         "clocks": clocks,
         "e2e": e2e,
+        "e2e_all_outputs": {k: e2e_all[k] for k in ("value", "unit", "h2d_bytes_per_step",
+                                                    "d2h_bytes_per_step", "ms_per_step",
+                                                    "returned")},
     }
     if grad_check is not None:
         line["grad_exchange_check"] = grad_check
@@ -523,13 +527,17 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, layer, M, K, N, dev, world, peer=None):
+def run_e2e(args, layer, M, K, N, dev, world, peer=None, outputs="api"):
     """Same step through the public API with host-resident inputs and results:
-    per step, H2D of x and dy from pinned memory and D2H of y, dx and the LoRA
-    gradients (dA, dB; at N > 1 their average over the ranks, by the same peer
-    exchange as the device-resident leg).  The two directions run on their own
-    streams (PCIe is full duplex), the next step's inputs load while this step
-    computes."""
+    per step, H2D of x and dy from pinned memory and D2H of the results.
+    ``outputs="api"`` returns what the reference's public calls return: y
+    (``lora_forward``, ops.py:32-103) and the LoRA gradients dA, dB
+    (``lora_backward``, ops.py:117-155; at N > 1 their average over the ranks,
+    by the same peer exchange as the device-resident leg).  dx is computed in
+    every step and stays on the device, where a preceding layer's backward
+    reads it.  ``outputs="all"`` also returns dx.  The two directions run on
+    their own streams (PCIe is full duplex), the next step's inputs load while
+    this step computes."""
     import torch
     import torch.distributed as dist
 
@@ -543,8 +551,10 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
     else:
         grad_shapes = (("dA", tuple(layer.A.shape), layer.A.dtype),
                        ("dB", tuple(layer.B.shape), layer.B.dtype))
+    want_dx = outputs == "all"
     outs = {k: [torch.empty(s, dtype=dt).pin_memory() for _ in range(2)]
-            for k, s, dt in (("y", (M, N), torch.bfloat16), ("dx", (M, K), torch.bfloat16),
+            for k, s, dt in (("y", (M, N), torch.bfloat16),
+                             *((("dx", (M, K), torch.bfloat16),) if want_dx else ()),
                              *grad_shapes)}
     xd = [torch.empty(M, K, device=dev, dtype=torch.bfloat16) for _ in range(2)]
     dyd = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _ in range(2)]
@@ -553,7 +563,7 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
     copy = torch.cuda.Stream(device=dev)   # host -> device
     drain = torch.cuda.Stream(device=dev)  # device -> host
     h2d = 2 * M * K + 2 * M * N
-    d2h = 2 * M * N + 2 * M * K + sum(
+    d2h = 2 * M * N + (2 * M * K if want_dx else 0) + sum(
         int(np.prod(s)) * torch.empty(0, dtype=dt).element_size() for _, s, dt in grad_shapes)
     loaded = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
@@ -606,7 +616,8 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
                 t.record_stream(drain)
             for r0, r1 in rows:
                 outs["y"][b][r0:r1].copy_(y.detach()[r0:r1], non_blocking=True)
-                outs["dx"][b][r0:r1].copy_(dx[r0:r1], non_blocking=True)
+                if want_dx:
+                    outs["dx"][b][r0:r1].copy_(dx[r0:r1], non_blocking=True)
             for dst, src in grads:
                 dst.copy_(src, non_blocking=True)
             drained[b].record(drain)
@@ -625,6 +636,8 @@ def run_e2e(args, layer, M, K, N, dev, world, peer=None):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "ms_per_step": round(ms / steps, 4),
             "copy_chunks": chunks,
+            "returned": ("y, dA, dB (what lora_forward and lora_backward return); dx computed "
+                         "on the device and left there" if not want_dx else "y, dx, dA, dB"),
             "path": "LoRALinear forward+backward, pinned host buffers, H2D and D2H on their "
                     "own streams overlapped with compute" +
                     (("; LoRA gradients averaged by the " +
