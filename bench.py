@@ -865,7 +865,7 @@ def events_ms(fn, reps=20, warm=3):
     return e0.elapsed_time(e1) / reps
 
 
-def sweep(kind, sampler=None, quick=False):
+def sweep(kind, sampler=None, quick=False, tokens=None):
     """Measurements of one of the other configurations on cuda:0, one dict per
     case.  kind: "fp32" (fp32 forward 4096->4096 r16, 2048 tokens, and the
     merged weight), "nf4" (NF4 11008x4096 block 64, r64, forward and backward
@@ -956,11 +956,12 @@ def sweep(kind, sampler=None, quick=False):
                     "ms": round(t1, 4)})
         return out
     if kind == "nf4":
-        cases = [("nf4", 64, 4096, 11008, 64, 128.0, M) for M in (1, 16, 512, 4096)]
+        cases = [("nf4", 64, 4096, 11008, 64, 128.0, M) for M in (1, 16, 512, 4096)
+                 if tokens is None or M in tokens]
     else:
         toks = (1, 4096) if quick else (1, 16, 128, 512, 4096)
         cases = [(s, 128, 4096, N, 16, 32.0, M) for s in ("int4", "int8") for N in (4096, 14336)
-                 for M in toks]
+                 for M in toks if tokens is None or M in tokens]
     for scheme, group, Kd, N, r, alpha, M in cases:
         t0 = time.time()
         W = (torch.randn(N, Kd, device=dev, generator=gen) / Kd ** 0.5).to(torch.bfloat16)
@@ -1063,7 +1064,7 @@ def run_workloads(args, rank, world, local_rank, sampler):
 
 
 def run_sweep(args):
-    for d in sweep(args.workload):
+    for d in sweep(args.workload, tokens=args.tokens):
         print(json.dumps(d), flush=True)
 
 
@@ -1127,6 +1128,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["lora", "stack", "nf4", "int", "fp32", "multi"],
                     default="lora")
+    ap.add_argument("--tokens", type=int, nargs="+", default=None,
+                    help="--workload nf4 / int: only these token counts")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--ref-tokens", type=int, default=WORKLOAD["tokens_per_gpu"])
