@@ -436,6 +436,12 @@ constexpr int kPHalf = 128;
 constexpr int kPStagesX = 6;
 constexpr int kPStagesW = 4;  // one per dequantiser group
 constexpr int kPStagesR = 4;
+// dequantiser warps of the pair kernel: four groups; each thread of a group
+// converts 128 / (group threads) 64-weight rows per k-block
+constexpr int kPDqWarps = 16;
+constexpr int kPGroupThreads = 32 * kPDqWarps / 4;
+constexpr int kPRowsPerThread = 128 / kPGroupThreads;
+constexpr int kPThreads = 64 + 32 * kEpiWarps + 32 * kPDqWarps;
 constexpr uint32_t kPXBytes = kPHalf * kBK * 2;  // 16 KB
 constexpr uint32_t kPWBytes = kPHalf * kBK * 2;  // 16 KB
 
@@ -456,7 +462,7 @@ constexpr size_t pair_smem_bytes() {
 }
 
 template <int kScheme, bool kWMN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     qlora_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
                            const __grid_constant__ CUtensorMap tm_x2,
                            const __grid_constant__ CUtensorMap tm_codes,
@@ -674,13 +680,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------- dequantisers --
-    // Four groups of two warps; group g converts the k-blocks whose running
-    // index is g (mod 4), always into W stage g, so four k-blocks are in
-    // conversion at once.  Each of a group's 64 threads converts two 64-weight
-    // rows: forward rows u and u + 64 of this CTA's 128; backward row u of both
-    // 64-column boxes.
-    const uint32_t t = threadIdx.x - (64 + 32 * kEpiWarps);  // 0..255
-    const uint32_t grp = t >> 6, u = t & 63u;
+    // Four groups; group g converts the k-blocks whose running index is g
+    // (mod 4), always into W stage g, so four k-blocks are in conversion at
+    // once.  Work item w = u + kPGroupThreads * i0 of a group's 128: forward
+    // row w of this CTA's 128; backward row w % 64 of 64-column box w / 64.
+    const uint32_t t = threadIdx.x - (64 + 32 * kEpiWarps);
+    const uint32_t grp = t / kPGroupThreads, u = t % kPGroupThreads;
     const uint32_t lead_wfull = mapa_shared(smem_u32(w_full), 0);
     uint32_t sr = 0, pr = 0, it = 0;
     bool ok = true;
@@ -705,16 +710,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint8_t* raw = rs + my_sr * Tr::kRawBytes;
           const uint8_t* scales = raw + Tr::kCodeBytes;
 #pragma unroll
-          for (uint32_t i = 0; i < 2; ++i) {
+          for (uint32_t i0 = 0; i0 < kPRowsPerThread; ++i0) {
+            const uint32_t w = u + kPGroupThreads * i0;
             float s, z;
             if constexpr (kWMN) {
+              const uint32_t i = w >> 6, uu = w & 63u;
               const uint32_t g = (static_cast<uint32_t>(c0) + i * 64u) / static_cast<uint32_t>(p.group) -
                                  static_cast<uint32_t>(c0) / static_cast<uint32_t>(p.group);
-              scale_zero<kScheme>(scales, g * 64u + u, s, z);
-              dequant_row<kScheme>(raw + u * (kPHalf * Tr::kBits / 8) + i * (64 * Tr::kBits / 8),
-                                   s, z, wtile + i * kMNBoxBytes + u * 128u, u, tbl_lane);
+              scale_zero<kScheme>(scales, g * 64u + uu, s, z);
+              dequant_row<kScheme>(raw + uu * (kPHalf * Tr::kBits / 8) + i * (64 * Tr::kBits / 8),
+                                   s, z, wtile + i * kMNBoxBytes + uu * 128u, uu, tbl_lane);
             } else {
-              const uint32_t row = u + 64u * i;
+              const uint32_t row = w;
               scale_zero<kScheme>(scales, row, s, z);
               dequant_row<kScheme>(raw + row * (kBK * Tr::kBits / 8), s, z, wtile + row * 128u,
                                    row, tbl_lane);
@@ -724,20 +731,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           // rank block: 64 columns of the up-projection operand (zero padded)
           const int j0 = (kb - p.num_kb_main) * kBK;
 #pragma unroll
-          for (uint32_t i = 0; i < 2; ++i) {
+          for (uint32_t i0 = 0; i0 < kPRowsPerThread; ++i0) {
+            const uint32_t w = u + kPGroupThreads * i0;
             if constexpr (kWMN) {
-              const int j = j0 + static_cast<int>(u);
-              uint8_t* out_row = wtile + i * kMNBoxBytes + u * 128u;
+              const uint32_t i = w >> 6, uu = w & 63u;
+              const int j = j0 + static_cast<int>(uu);
+              uint8_t* out_row = wtile + i * kMNBoxBytes + uu * 128u;
 #pragma unroll
               for (int c = 0; c < 8; ++c) {
                 const long long col = c0 + i * 64 + c * 8;
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if (j < p.up_rows && col < p.up_cols)
                   v = *reinterpret_cast<const uint4*>(p.up + static_cast<long long>(j) * p.up_ld + col);
-                st_chunk(out_row, u, c, v);
+                st_chunk(out_row, uu, c, v);
               }
             } else {
-              const uint32_t row = u + 64u * i;
+              const uint32_t row = w;
               const long long n = c0 + static_cast<long long>(row);
               uint8_t* out_row = wtile + row * 128u;
 #pragma unroll
@@ -752,7 +761,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         fence_proxy_async_smem();
-        named_bar_sync(2 + grp, 64);
+        named_bar_sync(2 + grp, kPGroupThreads);
         if (u == 0) {
           mbar_arrive_cluster(lead_wfull + sw * 8u);
           if (!extra) mbar_arrive(&r_empty[my_sr]);
@@ -925,7 +934,7 @@ int launch_q_pair(const QGemmArgs& a, cudaStream_t stream) {
   }
   const int pairs = std::min(p.num_tiles, num_sms() / 2);
   LaunchScope scope(kKindGemm, stream);
-  kern<<<2 * pairs, kThreads, smem, stream>>>(tx, tx2, tc, ts, p);
+  kern<<<2 * pairs, kPThreads, smem, stream>>>(tx, tx2, tc, ts, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("qgemm pair launch: ") + cudaGetErrorString(e));
