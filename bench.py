@@ -471,7 +471,12 @@ def run_ours(args, rank, world, local_rank):
 
     grad_check = exchange_check(peer, layer, flat_grads, dev, world) if world > 1 else None
 
-    # end-to-end through the public API with host buffers (pinned), overlapped
+    # end-to-end through the public API with host buffers (pinned), overlapped.
+    # run_e2e averages the gradients itself, once per step on the compute
+    # stream: the side-stream exchange hook comes off first, so that only one
+    # exchange kernel (they wait on one another's flags) is ever in flight
+    if peer is not None:
+        layer._grad_sink = sink
     e2e = run_e2e(args, layer, M, K, N, dev, world, peer)
     e2e_all = run_e2e(args, layer, M, K, N, dev, world, peer, outputs="all")
 
