@@ -59,7 +59,7 @@ struct QTraits {
 template <int kScheme>
 constexpr size_t smem_bytes() {
   return 1024 + kStagesX * kXTileBytes + kStagesW * kWTileBytes +
-         kStagesR * QTraits<kScheme>::kRawBytes + 512 + (kScheme == kINT8 ? 0 : kPairTableBytes);
+         kStagesR * QTraits<kScheme>::kRawBytes + 512;
 }
 
 struct QGemmParams {
@@ -83,18 +83,62 @@ __device__ __forceinline__ void st_chunk(uint8_t* row_base, uint32_t row, uint32
   *reinterpret_cast<uint4*>(row_base + ((chunk ^ (row & 7u)) << 4)) = v;
 }
 
-// Dequantises 8 consecutive weights held in `w` (4-bit: one word = 8 nibbles;
-// 8-bit: two words) into a 16-byte chunk of bf16 (packed fp32 pairs, the
-// scalar rounding; `tbl_lane` is this thread's view of the 4-bit pair table).
-template <int kScheme>
-__device__ __forceinline__ uint4 dq8(uint32_t w0, uint32_t w1, float scale, float zero,
-                                     const char* tbl_lane) {
+// Dequantises 8 consecutive INT8 weights held in w0/w1 into a 16-byte chunk
+// of bf16 (packed fp32 pairs, the scalar rounding).
+__device__ __forceinline__ uint4 dq8_int8(uint32_t w0, uint32_t w1, float scale, float zero) {
   uint64_t p[4];
-  dequant8_pairs<kScheme>(w0, w1, scale, zero, tbl_lane, p);
+  dequant8_pairs<kINT8>(w0, w1, scale, zero, nullptr, p);
   return make_uint4(pack2<__nv_bfloat16>(f2_lo(p[0]), f2_hi(p[0])),
                     pack2<__nv_bfloat16>(f2_lo(p[1]), f2_hi(p[1])),
                     pack2<__nv_bfloat16>(f2_lo(p[2]), f2_hi(p[2])),
                     pack2<__nv_bfloat16>(f2_lo(p[3]), f2_hi(p[3])));
+}
+
+// A 4-bit row of 64 weights shares one scale (and zero): its codes take at
+// most 16 values v(c) = bf16((L[c] or float(c) - zero) * scale), computed here
+// once in the scalar rounding and kept as byte planes: lo[t] holds the low
+// bytes of v(4t .. 4t+3), hi[t] their high bytes.
+template <int kScheme>
+__device__ __forceinline__ void row_codebook(float s, float z, uint32_t (&lo)[4],
+                                             uint32_t (&hi)[4]) {
+  const uint64_t ss = f2_pack(s, s), zz = f2_pack(z, z);
+  uint32_t v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint64_t p;
+    if constexpr (kScheme == kNF4)
+      p = f2_pack(kNF4Levels[2 * j], kNF4Levels[2 * j + 1]);
+    else
+      p = f2_sub(f2_pack(static_cast<float>(2 * j), static_cast<float>(2 * j + 1)), zz);
+    p = f2_mul(p, ss);
+    v[j] = pack2<__nv_bfloat16>(f2_lo(p), f2_hi(p));
+  }
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    lo[t] = __byte_perm(v[2 * t], v[2 * t + 1], 0x6420);
+    hi[t] = __byte_perm(v[2 * t], v[2 * t + 1], 0x7531);
+  }
+}
+
+// Eight bf16 weights (one word of 4-bit codes, nibble i = weight i) from the
+// row's codebook, by byte permutes only: for four codes at a time, one permute
+// per plane picks the byte of v(c & 7) from each 8-entry half, a second keeps
+// the half that bit 3 of the code names, a third interleaves low and high
+// bytes into bf16 pairs.
+__device__ __forceinline__ uint4 codebook8(uint32_t w, const uint32_t (&lo)[4],
+                                           const uint32_t (&hi)[4]) {
+  uint32_t out[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t c = h ? (w >> 16) : w;        // a permute reads selector bits 0-15
+    const uint32_t sel = c & 0x7777u;             // c & 7 per nibble
+    const uint32_t msel = ((c >> 1) & 0x4444u) | 0x3210u;  // byte i, or byte i of the upper half
+    const uint32_t l = __byte_perm(__byte_perm(lo[0], lo[1], sel), __byte_perm(lo[2], lo[3], sel), msel);
+    const uint32_t u = __byte_perm(__byte_perm(hi[0], hi[1], sel), __byte_perm(hi[2], hi[3], sel), msel);
+    out[2 * h] = __byte_perm(l, u, 0x5140);       // weights 4h, 4h + 1
+    out[2 * h + 1] = __byte_perm(l, u, 0x7362);   // weights 4h + 2, 4h + 3
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 template <int kScheme>
@@ -113,25 +157,26 @@ __device__ __forceinline__ void scale_zero(const uint8_t* scales, uint32_t idx, 
 // One thread converts one 64-element weight row of the raw tile.
 template <int kScheme>
 __device__ __forceinline__ void dequant_row(const uint8_t* codes, float s, float z,
-                                            uint8_t* out_row, uint32_t swz_row,
-                                            const char* tbl_lane) {
+                                            uint8_t* out_row, uint32_t swz_row) {
   if constexpr (kScheme == kINT8) {
     const uint4* c = reinterpret_cast<const uint4*>(codes);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 u = c[q];
-      st_chunk(out_row, swz_row, 2 * q, dq8<kScheme>(u.x, u.y, s, z, tbl_lane));
-      st_chunk(out_row, swz_row, 2 * q + 1, dq8<kScheme>(u.z, u.w, s, z, tbl_lane));
+      st_chunk(out_row, swz_row, 2 * q, dq8_int8(u.x, u.y, s, z));
+      st_chunk(out_row, swz_row, 2 * q + 1, dq8_int8(u.z, u.w, s, z));
     }
   } else {
+    uint32_t lo[4], hi[4];
+    row_codebook<kScheme>(s, z, lo, hi);
     const uint4* c = reinterpret_cast<const uint4*>(codes);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const uint4 u = c[q];
-      st_chunk(out_row, swz_row, 4 * q + 0, dq8<kScheme>(u.x, 0, s, z, tbl_lane));
-      st_chunk(out_row, swz_row, 4 * q + 1, dq8<kScheme>(u.y, 0, s, z, tbl_lane));
-      st_chunk(out_row, swz_row, 4 * q + 2, dq8<kScheme>(u.z, 0, s, z, tbl_lane));
-      st_chunk(out_row, swz_row, 4 * q + 3, dq8<kScheme>(u.w, 0, s, z, tbl_lane));
+      st_chunk(out_row, swz_row, 4 * q + 0, codebook8(u.x, lo, hi));
+      st_chunk(out_row, swz_row, 4 * q + 1, codebook8(u.y, lo, hi));
+      st_chunk(out_row, swz_row, 4 * q + 2, codebook8(u.z, lo, hi));
+      st_chunk(out_row, swz_row, 4 * q + 3, codebook8(u.w, lo, hi));
     }
   }
 }
@@ -158,9 +203,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  // 4-bit pair table after the 512-byte barrier area
-  uint64_t* table = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 512);
-  const char* tbl_lane = reinterpret_cast<const char*>(table) + (threadIdx.x % kPairCopies) * 8;
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -172,7 +214,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
   }
-  if constexpr (kScheme != kINT8) fill_pair_table<kScheme>(table, threadIdx.x, blockDim.x);
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_codes);
@@ -361,10 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t srow = (box * 64u) / static_cast<uint32_t>(p.group);
             scale_zero<kScheme>(scales, srow * 64u + row, s, z);
             dequant_row<kScheme>(raw + row * (kBN * Tr::kBits / 8) + box * (64 * Tr::kBits / 8),
-                                 s, z, wtile + box * kMNBoxBytes + row * 128u, row, tbl_lane);
+                                 s, z, wtile + box * kMNBoxBytes + row * 128u, row);
           } else {
             scale_zero<kScheme>(scales, t, s, z);
-            dequant_row<kScheme>(raw + t * (kBK * Tr::kBits / 8), s, z, wtile + t * 128u, t, tbl_lane);
+            dequant_row<kScheme>(raw + t * (kBK * Tr::kBits / 8), s, z, wtile + t * 128u, t);
           }
         } else {
           // rank block: copy 64 columns of the up-projection operand (zero padded)
@@ -457,8 +498,7 @@ struct QPairTraits {
 template <int kScheme>
 constexpr size_t pair_smem_bytes() {
   return 1024 + kPStagesX * kPXBytes + kPStagesW * kPWBytes +
-         kPStagesR * QPairTraits<kScheme>::kRawBytes + 512 +
-         (kScheme == kINT8 ? 0 : kPairTableBytes);
+         kPStagesR * QPairTraits<kScheme>::kRawBytes + 512;
 }
 
 template <int kScheme, bool kWMN>
@@ -484,9 +524,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  // 4-bit pair table after the 512-byte barrier area
-  uint64_t* table = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 512);
-  const char* tbl_lane = reinterpret_cast<const char*>(table) + (threadIdx.x % kPairCopies) * 8;
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -504,7 +541,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
   }
-  if constexpr (kScheme != kINT8) fill_pair_table<kScheme>(table, threadIdx.x, blockDim.x);
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_codes);
@@ -719,12 +755,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                                  static_cast<uint32_t>(c0) / static_cast<uint32_t>(p.group);
               scale_zero<kScheme>(scales, g * 64u + uu, s, z);
               dequant_row<kScheme>(raw + uu * (kPHalf * Tr::kBits / 8) + i * (64 * Tr::kBits / 8),
-                                   s, z, wtile + i * kMNBoxBytes + uu * 128u, uu, tbl_lane);
+                                   s, z, wtile + i * kMNBoxBytes + uu * 128u, uu);
             } else {
               const uint32_t row = w;
               scale_zero<kScheme>(scales, row, s, z);
               dequant_row<kScheme>(raw + row * (kBK * Tr::kBits / 8), s, z, wtile + row * 128u,
-                                   row, tbl_lane);
+                                   row);
             }
           }
         } else {
