@@ -475,7 +475,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Raw codes and scales go to each CTA's own ring, on its own barriers.
 constexpr int kPHalf = 128;
 constexpr int kPStagesX = 6;
-constexpr int kPStagesW = 4;  // one per dequantiser group
 constexpr int kPStagesR = 4;
 // dequantiser warps of the pair kernel: four groups; each thread of a group
 // converts 128 / (group threads) 64-weight rows per k-block
@@ -493,11 +492,14 @@ struct QPairTraits {
   static constexpr uint32_t kCodeBytes = kPHalf * kBK * kBits / 8;
   static constexpr uint32_t kScaleBytes = 1024;
   static constexpr uint32_t kRawBytes = kCodeBytes + kScaleBytes;
+  // W stages, dealt round-robin (k-block i converts into stage i % kStagesW):
+  // as many as the shared memory holds beside the X and raw rings
+  static constexpr int kStagesW = kBits == 4 ? 6 : 5;
 };
 
 template <int kScheme>
 constexpr size_t pair_smem_bytes() {
-  return 1024 + kPStagesX * kPXBytes + kPStagesW * kPWBytes +
+  return 1024 + kPStagesX * kPXBytes + QPairTraits<kScheme>::kStagesW * kPWBytes +
          kPStagesR * QPairTraits<kScheme>::kRawBytes + 512;
 }
 
@@ -512,15 +514,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   uint8_t* smem = align_smem<1024>(smem_raw);
   uint8_t* xs = smem;
   uint8_t* ws = xs + kPStagesX * kPXBytes;
-  uint8_t* rs = ws + kPStagesW * kPWBytes;
+  uint8_t* rs = ws + Tr::kStagesW * kPWBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(rs + kPStagesR * Tr::kRawBytes);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + kPStagesX;
   uint64_t* r_full = x_empty + kPStagesX;
   uint64_t* r_empty = r_full + kPStagesR;
   uint64_t* w_full = r_empty + kPStagesR;
-  uint64_t* w_empty = w_full + kPStagesW;
-  uint64_t* acc_full = w_empty + kPStagesW;
+  uint64_t* w_empty = w_full + Tr::kStagesW;
+  uint64_t* acc_full = w_empty + Tr::kStagesW;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
@@ -536,7 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     for (int s = 0; s < kPStagesX; ++s) mbar_init(&x_full[s], 1), mbar_init(&x_empty[s], 1);
     for (int s = 0; s < kPStagesR; ++s) mbar_init(&r_full[s], 1), mbar_init(&r_empty[s], 1);
     // the even CTA's w_full counts one arrival from each CTA's dequantisers
-    for (int s = 0; s < kPStagesW; ++s) mbar_init(&w_full[s], 2), mbar_init(&w_empty[s], 1);
+    for (int s = 0; s < Tr::kStagesW; ++s) mbar_init(&w_full[s], 2), mbar_init(&w_empty[s], 1);
     for (int b = 0; b < 2; ++b) mbar_init(&acc_full[b], 1), mbar_init(&acc_empty[b], 2 * kEpiWarps);
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
@@ -658,7 +660,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           umma_commit_pair(smem_u32(&w_empty[sw]));
           umma_commit_pair(peer_wempty + sw * 8u);
           if (++sx == kPStagesX) sx = 0, px ^= 1u;
-          if (++sw == kPStagesW) sw = 0, pw ^= 1u;
+          if (++sw == Tr::kStagesW) sw = 0, pw ^= 1u;
         }
         if (!ok) break;
         umma_commit_pair(smem_u32(&acc_full[buf]));
@@ -717,8 +719,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   } else {
     // -------------------------------------------------------- dequantisers --
     // Four groups; group g converts the k-blocks whose running index is g
-    // (mod 4), always into W stage g, so four k-blocks are in conversion at
-    // once.  Work item w = u + kPGroupThreads * i0 of a group's 128: forward
+    // (mod 4), k-block i into W stage i % 6, so four k-blocks are in
+    // conversion at once and six are buffered.  A group waits only for stages
+    // of earlier k-blocks, so the order is deadlock-free.  Work item w = u + kPGroupThreads * i0 of a group's 128: forward
     // row w of this CTA's 128; backward row w % 64 of 64-column box w / 64.
     const uint32_t t = threadIdx.x - (64 + 32 * kEpiWarps);
     const uint32_t grp = t / kPGroupThreads, u = t % kPGroupThreads;
@@ -732,7 +735,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const uint32_t my_sr = sr, my_pr = pr;
         if (!extra && ++sr == kPStagesR) sr = 0, pr ^= 1u;
         if ((it & 3u) != grp) continue;
-        const uint32_t sw = grp, pw = (it >> 2) & 1u;
+        const uint32_t sw = it % Tr::kStagesW, pw = (it / Tr::kStagesW) & 1u;
         if (!mbar_wait(&w_empty[sw], pw ^ 1u, p.status, kDevTimeoutEmpty)) {
           ok = false;
           break;
@@ -883,6 +886,7 @@ int launch_q(const QGemmArgs& a, cudaStream_t stream) {
 
   auto kern = qlora_gemm_kernel<kScheme, kWMN>;
   constexpr size_t smem = smem_bytes<kScheme>();
+  static_assert(smem <= 232448, "rings exceed the 227 KB of shared memory per CTA");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) {
@@ -962,6 +966,7 @@ int launch_q_pair(const QGemmArgs& a, cudaStream_t stream) {
 
   auto kern = qlora_gemm_pair_kernel<kScheme, kWMN>;
   constexpr size_t smem = pair_smem_bytes<kScheme>();
+  static_assert(smem <= 232448, "pair kernel rings exceed the 227 KB of shared memory per CTA");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) {
