@@ -223,20 +223,29 @@ __device__ __forceinline__ void rank_rows(const __nv_bfloat16* b, const float* s
     for (int nt = 0; nt < kNT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) c[nt][e] = 0.f;
-    for (int j0 = 0; j0 < r; j0 += 16) {
-      const int ja = j0 + 2 * q, jb = ja + 8;  // rank pairs (ja, ja+1), (jb, jb+1)
-      uint32_t a[4];
-      a[0] = n0 < N && ja < r ? __ldg(b0p + ja / 2) : 0u;
-      a[1] = n1 < N && ja < r ? __ldg(b1p + ja / 2) : 0u;
-      a[2] = n0 < N && jb < r ? __ldg(b0p + jb / 2) : 0u;
-      a[3] = n1 < N && jb < r ? __ldg(b1p + jb / 2) : 0u;
+    for (int j0 = 0; j0 < r; j0 += 64) {
+      // four 16-wide rank steps: all their B loads in flight, then the MMAs
+      uint32_t a[4][4];
 #pragma unroll
-      for (int nt = 0; nt < kNT; ++nt) {
-        const int m = nt * 8 + g;
-        const float* sm = sts + m * r;
-        const uint32_t x0 = m < M && ja < r ? pack2<__nv_bfloat16>(sm[ja], sm[ja + 1]) : 0u;
-        const uint32_t x1 = m < M && jb < r ? pack2<__nv_bfloat16>(sm[jb], sm[jb + 1]) : 0u;
-        mma16816(c[nt], a, x0, x1);
+      for (int jj = 0; jj < 4; ++jj) {
+        const int ja = j0 + 16 * jj + 2 * q, jb = ja + 8;  // rank pairs (ja, ja+1), (jb, jb+1)
+        a[jj][0] = n0 < N && ja < r ? __ldg(b0p + ja / 2) : 0u;
+        a[jj][1] = n1 < N && ja < r ? __ldg(b1p + ja / 2) : 0u;
+        a[jj][2] = n0 < N && jb < r ? __ldg(b0p + jb / 2) : 0u;
+        a[jj][3] = n1 < N && jb < r ? __ldg(b1p + jb / 2) : 0u;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int ja = j0 + 16 * jj + 2 * q, jb = ja + 8;
+        if (j0 + 16 * jj >= r) break;
+#pragma unroll
+        for (int nt = 0; nt < kNT; ++nt) {
+          const int m = nt * 8 + g;
+          const float* sm = sts + m * r;
+          const uint32_t x0 = m < M && ja < r ? pack2<__nv_bfloat16>(sm[ja], sm[ja + 1]) : 0u;
+          const uint32_t x1 = m < M && jb < r ? pack2<__nv_bfloat16>(sm[jb], sm[jb + 1]) : 0u;
+          mma16816(c[nt], a[jj], x0, x1);
+        }
       }
     }
     // C fragment: rows (row, row + 8) x tokens (nt*8 + 2q, +1)
@@ -481,19 +490,56 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // primary), which also set the partial slots to kPartialEmpty
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (p.b != nullptr) {
-      for (int i = rw * 32 + lane; i < p.M * p.r; i += kRankAll) {
-        float v = 0.f;
-        for (int s0 = 0; s0 < p.st_splits; s0 += 8) {  // loads in flight together
-          float t8[8];
+      // sT = the sum of the rank kernel's K splits, in split order
+      const int n = p.M * p.r;
+      if ((n & 3) == 0) {
+        // four elements per load; two float4 lanes x four splits in flight
+        const int n4 = n >> 2;
+        const float4* st4 = reinterpret_cast<const float4*>(p.st);
+        float4* sts4 = reinterpret_cast<float4*>(sts);
+        for (int i0 = rw * 32 + lane; i0 < n4; i0 += 2 * kRankAll) {
+          float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+          for (int s0 = 0; s0 < p.st_splits; s0 += 4) {
+            float4 v[4][2];
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            t8[u] = s0 + u < p.st_splits
-                        ? __ldcg(p.st + static_cast<long long>(s0 + u) * p.M * p.r + i)
-                        : 0.f;
+            for (int u = 0; u < 4; ++u)
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v += t8[u];
+              for (int e = 0; e < 2; ++e) {
+                const int i = i0 + e * kRankAll;
+                v[u][e] = s0 + u < p.st_splits && i < n4
+                              ? __ldcg(st4 + static_cast<long long>(s0 + u) * n4 + i)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (s0 + u < p.st_splits)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  acc[e].x += v[u][e].x;
+                  acc[e].y += v[u][e].y;
+                  acc[e].z += v[u][e].z;
+                  acc[e].w += v[u][e].w;
+                }
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            if (i0 + e * kRankAll < n4) sts4[i0 + e * kRankAll] = acc[e];
         }
-        sts[i] = v;
+      } else {
+        for (int i = rw * 32 + lane; i < n; i += kRankAll) {
+          float v = 0.f;
+          for (int s0 = 0; s0 < p.st_splits; s0 += 8) {  // loads in flight together
+            float t8[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              t8[u] = s0 + u < p.st_splits ? __ldcg(p.st + static_cast<long long>(s0 + u) * n + i)
+                                           : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (s0 + u < p.st_splits) v += t8[u];
+          }
+          sts[i] = v;
+        }
       }
       named_bar_sync(3, kRankAll);
       // the rank terms of the finish block and of the first whole block while
