@@ -76,7 +76,6 @@ __device__ __forceinline__ uint64_t f2_from_bytes(uint32_t word, uint32_t sel0, 
 // half-warp read distinct bank pairs (an LDS.64 of a warp is two wavefronts
 // whatever the codes).
 constexpr int kPairCopies = 16;
-constexpr int kPairTableBytes = 256 * kPairCopies * 8;
 
 template <int kScheme>
 __device__ __forceinline__ void fill_pair_table(uint64_t* t, int tid, int nthreads) {
