@@ -8,6 +8,7 @@
 // replacing qlora_forward_nf4 / qlora_forward_int4 (kernels/lora_quantized.metal:29-164),
 // which re-read and re-dequantised every weight for every token.
 //
+// One-CTA kernel (M < 256; the CTA-pair variant below takes M >= 256).
 // Warp roles (14 warps, one CTA per SM):
 //   warp 0      TMA producer: bf16 X tiles [128 x 64] into a 4-stage ring, and the
 //               packed codes + per-block scales of the matching W tile into a
@@ -17,7 +18,8 @@
 //   warps 2-5   epilogue (as in the dense kernel).
 //   warps 6-13  dequantisers: each thread turns one 64-element row of the raw
 //               tile into bf16 -- value = bf16_rn(fp32 dequant), the reference's
-//               fp32 arithmetic -- and stores it 16 bytes at a time into the
+//               fp32 arithmetic (4-bit rows through a per-row register
+//               codebook) -- and stores it 16 bytes at a time into the
 //               128-byte-swizzled layout UMMA reads (2-stage ring).  For the
 //               rank block they copy B (forward) or A (backward) rows instead.
 // Every wait is bounded (see ptx.cuh).
@@ -461,12 +463,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // own 128 rows of X and dequantises only its own 128 rows (forward) or output
 // columns (backward) of the weight tile, so per SM the dequantisers convert
 // half as many weights per k-block as in the one-CTA kernel, while the pair
-// MMA reads half of B from each SM.  The dequantisers work in four groups on
-// four k-blocks at once (one W stage each).  NF4 11008 x 4096, r 64: 0.53 ms
-// at 4096 tokens and 0.103 ms at 512 (one-CTA kernel: 0.926 / 0.215 ms); the
-// staged path (one dequantisation pass, then the dense pair GEMM) remains
-// faster (0.29 / 0.078 ms): ~3.5 instructions per weight on 8 warps do not
-// keep up with the pair MMA's 540 cycles per k-block.
+// MMA reads half of B from each SM.  Sixteen dequantiser warps work in four
+// groups on four k-blocks at once, k-block i into W stage i mod kStagesW;
+// a 4-bit row goes through a register codebook (row_codebook / codebook8).
+// NF4 11008 x 4096, r 64: 0.39-0.43 ms at 4096 tokens and 0.082-0.090 ms at
+// 512; the staged path (one dequantisation pass, then the dense pair GEMM)
+// stays faster at 4096 tokens (0.29 ms), where each weight is converted
+// once per 256-token tile, 16 times.
 //   even CTA: producer arms x_full[s] for both CTAs' X bytes; warp 1 issues the
 //             MMAs once both CTAs' dequantisers have arrived on w_full[s], and
 //             commits to both CTAs' x_empty / w_empty / acc_full.
