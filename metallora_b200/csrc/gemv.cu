@@ -186,19 +186,24 @@ __device__ __forceinline__ void a_frags(const uint32_t (&w0)[kWords], const uint
     a[2] = bf16x2_sub(((t0 >> 4) & 0x000F000Fu) | 0x43004300u, z0);  // (k+1, k+3)
     a[1] = bf16x2_sub((t1 & 0x000F000Fu) | 0x43004300u, z1);
     a[3] = bf16x2_sub(((t1 >> 4) & 0x000F000Fu) | 0x43004300u, z1);
-  } else {  // INT8: word b holds k+0..3
-    const float f0 = __uint_as_float(z0), f1 = __uint_as_float(z1);
+  } else {  // INT8: word b holds k+0..3; (2^23 + q) - (2^23 + zero) on packed pairs
+    const uint64_t zz0 = (static_cast<uint64_t>(z0) << 32) | z0;
+    const uint64_t zz1 = (static_cast<uint64_t>(z1) << 32) | z1;
     const uint32_t u0 = w0[b], u1 = w1[b];
-    float f[8];
+    uint64_t f[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[i] = __fsub_rn(__uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7440u + i)), f0);
-      f[4 + i] = __fsub_rn(__uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7440u + i)), f1);
+    for (int i = 0; i < 2; ++i) {
+      f[i] = f2_sub((static_cast<uint64_t>(__byte_perm(u0, 0x4B000000u, 0x7441u + 2 * i)) << 32) |
+                        __byte_perm(u0, 0x4B000000u, 0x7440u + 2 * i),
+                    zz0);
+      f[2 + i] = f2_sub((static_cast<uint64_t>(__byte_perm(u1, 0x4B000000u, 0x7441u + 2 * i)) << 32) |
+                            __byte_perm(u1, 0x4B000000u, 0x7440u + 2 * i),
+                        zz1);
     }
-    a[0] = pack2<__nv_bfloat16>(f[0], f[1]);
-    a[2] = pack2<__nv_bfloat16>(f[2], f[3]);
-    a[1] = pack2<__nv_bfloat16>(f[4], f[5]);
-    a[3] = pack2<__nv_bfloat16>(f[6], f[7]);
+    a[0] = pack2<__nv_bfloat16>(f2_lo(f[0]), f2_hi(f[0]));
+    a[2] = pack2<__nv_bfloat16>(f2_lo(f[1]), f2_hi(f[1]));
+    a[1] = pack2<__nv_bfloat16>(f2_lo(f[2]), f2_hi(f[2]));
+    a[3] = pack2<__nv_bfloat16>(f2_lo(f[3]), f2_hi(f[3]));
   }
 }
 
