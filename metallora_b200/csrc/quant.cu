@@ -347,8 +347,10 @@ void launch_dequantize_vec(const uint8_t* codes, const void* scales, const __hal
   static int per_sm[2] = {0, 0};
   int& occ = per_sm[fast ? 1 : 0];
   if (occ == 0 &&
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kDqVecThreads, 0) != cudaSuccess)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kDqVecThreads, 0) != cudaSuccess) {
     occ = 1;
+    (void)cudaGetLastError();  // the launch check below must see the launch's own status
+  }
   occ = std::max(occ, 1);
   int64_t grid = (items + int64_t(4) * kDqVecThreads - 1) / (int64_t(4) * kDqVecThreads);
   grid = std::max<int64_t>(1, std::min<int64_t>(grid, int64_t(occ) * num_sms()));
