@@ -9,6 +9,7 @@
 // Dequantisers follow the reference shaders' fp32 arithmetic
 // (kernels/lora_quantized.metal:17-25).
 #include <algorithm>
+#include <atomic>
 #include <string>
 
 #include "internal.h"
@@ -344,14 +345,17 @@ void launch_dequantize_vec(const uint8_t* codes, const void* scales, const __hal
   auto* kernel = fast ? dequantize_vec_kernel<kScheme, O, Idx, true>
                       : dequantize_vec_kernel<kScheme, O, Idx, false>;
   // persistent-style: one wave of resident blocks, each filling its table once
-  static int per_sm[2] = {0, 0};
-  int& occ = per_sm[fast ? 1 : 0];
-  if (occ == 0 &&
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kDqVecThreads, 0) != cudaSuccess) {
-    occ = 1;
-    (void)cudaGetLastError();  // the launch check below must see the launch's own status
+  static std::atomic<int> per_sm[2] = {{0}, {0}};
+  int occ = per_sm[fast ? 1 : 0].load(std::memory_order_relaxed);
+  if (occ == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kDqVecThreads, 0) !=
+        cudaSuccess) {
+      occ = 1;
+      (void)cudaGetLastError();  // the launch check below must see the launch's own status
+    }
+    occ = std::max(occ, 1);
+    per_sm[fast ? 1 : 0].store(occ, std::memory_order_relaxed);
   }
-  occ = std::max(occ, 1);
   int64_t grid = (items + int64_t(4) * kDqVecThreads - 1) / (int64_t(4) * kDqVecThreads);
   grid = std::max<int64_t>(1, std::min<int64_t>(grid, int64_t(occ) * num_sms()));
   kernel<<<static_cast<int>(grid), kDqVecThreads, 0, s>>>(
