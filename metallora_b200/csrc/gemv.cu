@@ -397,14 +397,39 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __shared__ DecPlan pl_s;
   const DecPlan& pl = pl_s;
 
+  // one stage's copies (weight box, scale box, the tokens' boxes), completing
+  // on full_bar[slot]; issued by thread 0 only
+  const uint32_t stage_tx = kStageBytes + (D::kScaled ? p.gps * kDecRows * 4 : 0) +
+                            D::kQuads * p.x_rows * 128;
+  auto issue_stage = [&](int slot, int rb, int s) {
+    mbar_arrive_expect_tx(&full_bar[slot], stage_tx);
+    tma_load_2d(ring + slot * kStageBytes, &wmap, &full_bar[slot], s * kBoxBytes, rb * kDecRows);
+    if constexpr (D::kScaled)  // [gps groups x 128 rows] of the prepared scale table
+      tma_load_2d(const_cast<uint8_t*>(sring) + slot * p.scale_slot, &smap, &full_bar[slot],
+                  rb * kDecRows, (s * D::kStageK) / p.group);
+#pragma unroll
+    for (int j = 0; j < D::kQuads; ++j)  // the tokens' k range of this stage
+      tma_load_2d(xring + slot * p.x_slot + j * p.x_rows * 128, &xmap, &full_bar[slot],
+                  s * D::kStageK + 64 * j, 0);
+  };
+
   if (threadIdx.x == 0) {
     // the descriptor fetches overlap the plan and the barrier set-up
     prefetch_tmap(&wmap);
     prefetch_tmap(&xmap);
     if constexpr (D::kScaled) prefetch_tmap(&smap);
     pl_s = make_plan(p, cta, ctas);
+    // the first stage's copies leave before the rest of the set-up (every
+    // CTA has at least one unit: the grid is at most the unit count)
+    mbar_init(&full_bar[0], 1);
+    fence_mbarrier_init();
+    {
+      int rb, s0, s1, kind;
+      plan_segment(pl_s, p.S, 0, rb, s0, s1, kind);
+      issue_stage(0, rb, s0);
+    }
     for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&full_bar[s], 1);
+      if (s > 0) mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kConsumers);
     }
     mbar_init(&rt_full, kRankWarps);
@@ -433,8 +458,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      const uint32_t stage_tx = kStageBytes + (D::kScaled ? p.gps * kDecRows * 4 : 0) +
-                                D::kQuads * p.x_rows * 128;
       bool ok = true;
       uint32_t issued = 0;
       int slot = 0;
@@ -443,20 +466,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         int rb, s0, s1, kind;
         plan_segment(pl, p.S, t, rb, s0, s1, kind);
         for (int s = s0; s < s1; ++s) {
-          if (!mbar_wait(&empty_bar[slot], phase ^ 1, p.status, kDevTimeoutEmpty)) {
-            ok = false;
-            break;
+          if (issued > 0) {  // the first stage left during the set-up
+            if (!mbar_wait(&empty_bar[slot], phase ^ 1, p.status, kDevTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            issue_stage(slot, rb, s);
           }
-          mbar_arrive_expect_tx(&full_bar[slot], stage_tx);
-          tma_load_2d(ring + slot * kStageBytes, &wmap, &full_bar[slot], s * kBoxBytes,
-                      rb * kDecRows);
-          if constexpr (D::kScaled)  // [gps groups x 128 rows] of the prepared scale table
-            tma_load_2d(const_cast<uint8_t*>(sring) + slot * p.scale_slot, &smap,
-                        &full_bar[slot], rb * kDecRows, (s * D::kStageK) / p.group);
-#pragma unroll
-          for (int j = 0; j < D::kQuads; ++j)  // the tokens' k range of this stage
-            tma_load_2d(xring + slot * p.x_slot + j * p.x_rows * 128, &xmap, &full_bar[slot],
-                        s * D::kStageK + 64 * j, 0);
           ++issued;
           if (++slot == p.stages) {
             slot = 0;
