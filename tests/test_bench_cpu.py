@@ -46,3 +46,27 @@ def test_our_arm_and_smoke_fail_without_gpu():
     import __graft_entry__
     with pytest.raises(Exception):
         __graft_entry__.smoke()
+
+
+def test_nf4_cpu_baseline_shape():
+    """The NF4 decode row's CPU baseline times the oracle's restatement of the
+    reference's NF4 forward on the given weight and reports the fields the
+    bench line carries."""
+    import types
+
+    import numpy as np
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from oracle import quant_oracle as qo
+    rng = np.random.default_rng(0)
+    N, K, r = 96, 256, 8
+    codes, absmax = qo.quantize_nf4((rng.standard_normal((N, K)) / 16).astype(np.float32), 64)[:2]
+    qw = types.SimpleNamespace(codes=torch.from_numpy(codes), scales=torch.from_numpy(absmax),
+                               shape=(N, K))
+    x = torch.randn(1, K).to(torch.bfloat16)
+    A = (torch.rand(r, K) / 16).to(torch.bfloat16)
+    B = (torch.randn(N, r) * 0.1).to(torch.bfloat16)
+    cb = bench.nf4_cpu_baseline(qw, x, A, B, 16.0, 64, reps=2)
+    assert cb["kind"] == "port" and cb["unit"] == "ms per call"
+    assert cb["value"] > 0 and cb["cores"] >= 1
+    assert f"NF4 {N}x{K}" in cb["sample"] and f"r {r}" in cb["sample"]
