@@ -1115,7 +1115,18 @@ DecodeConfig decode_config(int scheme, int64_t M, int64_t N, int64_t K, int64_t 
   const int sk = stage_k_of(scheme);
   const int64_t S = (K + sk - 1) / sk;
   const int64_t units = gemv_row_blocks(N) * S;
-  const int64_t ctas = std::min<int64_t>(num_sms(), units);
+  // With a LoRA term the small rank kernel runs first, one CTA per SM, and a
+  // decode CTA cannot share an SM with it: decode CTAs placed there start only
+  // when it ends and finish last.  Leaving those SMs to the rank kernel makes
+  // every decode CTA start at once, at the price of fewer SMs streaming.
+  // Measured (same box): worth it for 16 tokens (NF4 18.7 -> 17.6 us, INT8
+  // 27.3 -> 23.2 us, INT4 16.9 -> 14.3 us) and for a rank kernel of at most 8
+  // CTAs at one token (INT4/INT8 r 16: -0.15 to -0.35 us); not for NF4 r 64
+  // at one token (16 SMs reserved: 13.65 -> 14.02 us).
+  const int64_t rank_ctas = r > 0 ? (r + 15) / 16 * rank_small_splits(K) : 0;
+  const int64_t reserve = rank_ctas > 0 && (M > 8 || rank_ctas <= 8)
+                              ? std::min<int64_t>(rank_ctas, num_sms() / 4) : 0;
+  const int64_t ctas = std::min<int64_t>(num_sms() - reserve, units);
   const int64_t g = group > 0 ? group : 64;
   int stages = kMaxStages;
   while (stages > 2 && dec_layout(scheme, M, r, g, stages).bytes > kSmemMax) --stages;
